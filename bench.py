@@ -1,0 +1,522 @@
+"""KV save/load benchmark on the Llama-3-8B GQA workload (32 layers, 8 KV heads
+x 128, bf16, block 16, 16384 blocks per layer; 64 requests x 2048 tokens).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+One process per GPU (torchrun for N > 1).  At N GPUs the KV heads are split
+tensor-parallel (8/N heads per rank); every rank saves and loads its own head
+shard (no data exchange) and one NCCL all-reduce(min) agrees the per-request
+hit length before loading.
+
+Printed JSON line (rank 0):
+  value      save+load payload GB/s of all ranks with the records in HBM:
+             one gather launch (paged -> records) and one scatter launch
+             (records -> a fresh block table) per step, CUDA-event timed
+  e2e        the same metric through the public C API with the pinned host
+             record pool: device block hashing of the tokens, cache_store,
+             cache_lookup_batch, all-reduce(min), one cache_load per request
+             (host clock, H2D/D2H inside); p50 per-request load latency
+  roofline   gather kernel vs the measured HBM copy peak
+  link       e2e save/load vs the host link measured in the same run
+  cpu_baseline  the oracle's C restatement of CrossCache's CPU memcpy path
+             on the host cores, on a bounded sample of the workload
+--impl reference times CrossCache's own CPU transfer path (its mem.cpp
+compiled from the reference sources, oracle/_ref) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "KV save/load GB/s per GPU and p50 per-request load latency"
+L, KV_HEADS, HEAD_DIM, ELT, BS, NUM_BLOCKS = 32, 8, 128, 2, 16, 16384
+REQS, TOKENS, CHUNK, VOCAB = 64, 2048, 256, 128256
+GB = 1e9
+
+
+def workload_config(tp: int) -> dict:
+    return {
+        "workload": "llama3-8b-gqa-kv-offload: 32 layers x 8 KV heads x 128 bf16, block 16, "
+                    "16384 blocks/layer; 64 requests x 2048 tokens; 256-token records",
+        "layers": L, "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "kv_dtype": "bf16",
+        "block_size": BS, "blocks_per_layer": NUM_BLOCKS, "requests": REQS,
+        "tokens_per_request": TOKENS, "chunk_tokens": CHUNK, "tp": tp,
+        "kv_heads_per_rank": KV_HEADS // tp,
+        "l2": "inputs larger than L2: 32 GiB/tp paged cache, 16 GiB/tp of records per step",
+    }
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def ncu_traffic() -> float | None:
+    """DRAM bytes per gather launch from the committed ncu summary, if any."""
+    f = ROOT / "profiles" / "kv_copy_gather.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_full_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        mhz, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                mhz.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(mhz)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle port / compiled reference), host memory only
+
+def cpu_sample_run(impl: str, seconds: float | None, iters: int | None, threads: int) -> dict:
+    """Save then load a bounded sample (64 of the 512 records, 1024 blocks) of
+    the workload shapes through a CPU implementation of CrossCache's path.
+    Returns GB/s of save+load payload."""
+    sys.path.insert(0, str(ROOT))
+    from oracle import kvcopy as ok
+
+    nb, chunks = 1024, 64
+    unit = KV_HEADS * HEAD_DIM * ELT
+    layer_bytes = nb * BS * unit
+    k = [np.full(layer_bytes, l, np.uint8) for l in range(L)]
+    v = [np.full(layer_bytes, 100 + l, np.uint8) for l in range(L)]
+    rec_bytes = 2 * L * CHUNK * unit
+    recs = [np.zeros(rec_bytes, np.uint8) for _ in range(chunks)]
+    rng = np.random.default_rng(2)
+    bids = rng.permutation(nb).astype(np.uint64)
+    bids2 = rng.permutation(nb).astype(np.uint64)
+    bpc = CHUNK // BS
+    payload = 2 * chunks * rec_bytes
+
+    if impl == "reference":
+        ref = ok.RefMem()
+        slots1 = [ok.slot_mapping(bids[c * bpc:(c + 1) * bpc], BS) for c in range(chunks)]
+        slots2 = [ok.slot_mapping(bids2[c * bpc:(c + 1) * bpc], BS) for c in range(chunks)]
+        pool = ThreadPoolExecutor(threads)
+
+        def one_step():
+            list(pool.map(lambda c: ref.lib.transfer_kvcache(ref.ad, C.byref(_params(ref, recs[c], k, v, slots1[c], True))),
+                          range(chunks)))
+            list(pool.map(lambda c: ref.lib.transfer_kvcache(ref.ad, C.byref(_params(ref, recs[c], k, v, slots2[c], False))),
+                          range(chunks)))
+        # the reference prints a log line per token to stdout: send it to /dev/null
+        sys.stdout.flush()
+        saved, devnull = os.dup(1), os.open(os.devnull, os.O_WRONLY)
+        os.dup2(devnull, 1)
+        try:
+            times = _time_steps(one_step, seconds, iters)
+            ref.libc.fflush(None)
+        finally:
+            os.dup2(saved, 1)
+            os.close(saved)
+            os.close(devnull)
+        kind, sample = "reference", "CrossCache src/device/mem/mem.cpp TransferKVCache (compiled, oracle/_ref)"
+    else:
+        def one_step():
+            ok.cache_op(recs, k, v, bids, CHUNK, BS, unit, 1, True, threads)
+            ok.cache_op(recs, k, v, bids2, CHUNK, BS, unit, 1, False, threads)
+        times = _time_steps(one_step, seconds, iters)
+        kind, sample = "port", "oracle/kvcopy_oracle.c restatement of mem.cpp:114-173 + cache.c:513-593"
+    gbs = [payload / t / GB for t in times]
+    return {"value": statistics.median(gbs), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{sample}; 64 of 512 records (1024 blocks, {rec_bytes >> 20} MiB records), "
+                      f"save then load into a second block table, paged cache in host memory; "
+                      f"median of {len(times)} passes",
+            "times_s": [round(t, 4) for t in times]}
+
+
+def _params(ref, rec, k, v, slots, direction):
+    from oracle.kvcopy import _RefParams
+    kp = np.array([a.ctypes.data for a in k], np.uint64)
+    vp = np.array([a.ctypes.data for a in v], np.uint64)
+    p = _RefParams(caches=rec.ctypes.data, caches_h=rec.ctypes.data, keys_ptrs=kp.ctypes.data,
+                   value_ptrs=vp.ctypes.data, page_buffer_size=0, slot_mapping=slots.ctypes.data,
+                   devid=0, caches_element_size=1, num_layers=len(kp), num_tokens=CHUNK,
+                   hidden_dim_size=KV_HEADS * HEAD_DIM * ELT, direction=direction)
+    p._keep = (kp, vp)
+    return p
+
+
+def _time_steps(fn, seconds, iters):
+    times = []
+    start = time.perf_counter()
+    while True:
+        t = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t)
+        if iters is not None and len(times) >= iters:
+            break
+        if seconds is not None and time.perf_counter() - start >= seconds:
+            break
+    return times
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    have_ref = (ROOT / "oracle" / "_ref" / "libref_mem.so").exists()
+    impl = "reference" if have_ref else "port"
+    cpu_sample_run(impl, None, args.warmup, threads)      # warm-up passes
+    res = cpu_sample_run(impl, None, args.steps, threads)
+    v = res["value"]
+    line = {"metric": METRIC, "value": round(v, 3), "unit": "GB/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(statistics.median(res["times_s"]) * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": workload_config(args.gpus),
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from demo_b200 import cache as cc
+    from demo_b200._lib import KvCopyDesc, lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    if KV_HEADS % world:
+        raise SystemExit("world size must divide 8 KV heads")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    heads = KV_HEADS // world
+    hidden = heads * HEAD_DIM
+    unit = hidden * ELT
+    bpc = CHUNK // BS
+    nblk = REQS * TOKENS // BS                 # 8192 blocks
+    nrec = nblk // bpc                         # 512 records
+    rec_bytes = 2 * L * CHUNK * unit
+    payload = nrec * rec_bytes                 # one direction, this rank
+
+    # paged cache: this rank's head shard of N(0,1) bf16 values (seed 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    layers = []
+    for _ in range(L):
+        full = torch.randn(2, NUM_BLOCKS, BS, KV_HEADS, HEAD_DIM, generator=g, device=dev,
+                           dtype=torch.float32).to(torch.bfloat16)
+        layers.append(full[:, :, :, rank * heads:(rank + 1) * heads].contiguous())
+        del full
+    torch.cuda.empty_cache()
+    layout, kp, vp = cc.layout_from_kv_tensors(layers)
+    # block tables: seeded permutations of free block ids (save: seed 2, reload: seed 3)
+    bt_save = torch.randperm(NUM_BLOCKS, generator=torch.Generator().manual_seed(2))[:nblk].numpy().astype(np.uint64)
+    bt_load = torch.randperm(NUM_BLOCKS, generator=torch.Generator().manual_seed(3))[:nblk].numpy().astype(np.uint64)
+    tokens = torch.randint(0, VOCAB, (REQS, TOKENS), generator=torch.Generator().manual_seed(1),
+                           dtype=torch.int64).to(torch.int32).numpy()
+
+    # ---------------- value: device-resident records, kernel path ----------
+    kp_d = torch.tensor(kp, dtype=torch.int64, device=dev)
+    vp_d = torch.tensor(vp, dtype=torch.int64, device=dev)
+    records = torch.empty(nrec * rec_bytes, dtype=torch.uint8, device=dev)
+    rec_ptrs = torch.arange(nrec, dtype=torch.int64, device=dev) * rec_bytes + records.data_ptr()
+    b_save = torch.from_numpy(bt_save.astype(np.int64)).to(dev)
+    b_load = torch.from_numpy(bt_load.astype(np.int64)).to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def desc(bids, direction):
+        return KvCopyDesc(layer_k=kp_d.data_ptr(), layer_v=vp_d.data_ptr(), records=rec_ptrs.data_ptr(),
+                          slots=None, block_ids=bids.data_ptr(), error=err.data_ptr(),
+                          page_buffer_size=NUM_BLOCKS * BS, unit_bytes=unit, num_tokens=CHUNK,
+                          block_size=BS, num_layers=L, num_records=nrec, direction=direction)
+
+    d_gather, d_scatter = desc(b_save, 1), desc(b_load, 0)
+    assert lib.kv_copy_payload_bytes(C.byref(d_gather)) == payload
+    stream = torch.cuda.Stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+
+    def kernel_step(ev=None):
+        if ev:
+            ev[0].record(stream)
+        assert lib.kv_copy_launch(C.byref(d_gather), sptr) == 0
+        if ev:
+            ev[1].record(stream)
+        assert lib.kv_copy_launch(C.byref(d_scatter), sptr) == 0
+        if ev:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        kernel_step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    l0 = lib.crosscache_kernel_launches()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            kernel_step(evs[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    launches = lib.crosscache_kernel_launches() - l0
+    dt = max_over_ranks(t0.elapsed_time(t1) / 1e3)
+    gather_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    scatter_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    assert int(err.item()) == 0, "kv copy reported an error"
+    # verify: block bt_load[i] of the destination == block bt_save[i] of the source
+    ok_value = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers)
+    total_payload = sum_over_ranks(2 * payload)
+    value = total_payload * args.steps / dt / GB
+    hbm_peak, peak_kind = peaks()
+    achieved = 2 * payload / (gather_ms / 1e3) / GB       # read + write bytes per gather launch
+    del records
+    torch.cuda.empty_cache()
+
+    # ---------------- e2e: public C API, pinned host pool -------------------
+    e2e = None
+    link = None
+    p50 = None
+    if not args.skip_e2e:
+        # host-link peaks measured in this run (pinned 256 MiB copies)
+        hbuf = torch.empty(256 << 20, dtype=torch.uint8, pin_memory=True)
+        dbuf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        link_peak = {}
+        for name, fn in (("h2d", lambda: dbuf.copy_(hbuf, non_blocking=True)),
+                         ("d2h", lambda: hbuf.copy_(dbuf, non_blocking=True))):
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(8):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            link_peak[name] = 8 * (256 << 20) / (a.elapsed_time(b) / 1e3) / GB
+        del hbuf, dbuf
+
+        cc.init(CHUNK, (nrec + 1) * rec_bytes, None)
+        w = cc.Worker("llama-3-8b", layout, kp, vp, node_id=local, world_size=world, rank=rank)
+        w.register()
+        from demo_b200._lib import lib as L_
+        flat_tok = np.ascontiguousarray(tokens.reshape(-1))
+        tok_lens = np.full(REQS, TOKENS, dtype=np.int64)
+        none_hash = __import__("hashlib").sha256(__import__("pickle").dumps("0", protocol=5)).digest()
+        hashes = np.zeros((nblk, 32), dtype=np.uint8)
+        key_nums = np.full(REQS, TOKENS // CHUNK, dtype=np.uint32)
+        hits = np.zeros(REQS, dtype=np.uint32)
+        bt_save_c = np.ascontiguousarray(bt_save)
+        per_req_blocks = TOKENS // BS
+        load_bids = [np.ascontiguousarray(bt_load[r * per_req_blocks:(r + 1) * per_req_blocks]) for r in range(REQS)]
+
+        def e2e_step(lat: list | None):
+            t_a = time.perf_counter()
+            w.clear()
+            n = L_.kv_block_hash_host(local, flat_tok.ctypes.data, tok_lens.ctypes.data, REQS, BS, none_hash,
+                                      hashes.ctypes.data)
+            assert n == nblk
+            keys = np.ascontiguousarray(hashes[bpc - 1::bpc])              # 512 chunk keys
+            kb = keys.tobytes()
+            t_b = time.perf_counter()
+            ret = L_.cache_store(C.byref(w.ctx), kb, 32, bt_save_c.ctypes.data, nblk)
+            assert ret == 0, ret
+            t_c = time.perf_counter()
+            ret = L_.cache_lookup_batch(C.byref(w.ctx), kb, key_nums.ctypes.data, REQS, 32, hits.ctypes.data)
+            assert ret == 0
+            hit = hits
+            if world > 1:
+                ht = torch.from_numpy(hits.astype(np.int32)).to(dev)
+                dist.all_reduce(ht, op=dist.ReduceOp.MIN)
+                hit = ht.cpu().numpy()
+            per_req_keys = TOKENS // CHUNK
+            for r in range(REQS):
+                h = int(hit[r])
+                ts = time.perf_counter()
+                kr = kb[r * per_req_keys * 32:(r * per_req_keys + h) * 32]
+                ret = L_.cache_load(C.byref(w.ctx), kr, 32, load_bids[r].ctypes.data, h * bpc)
+                assert ret == 0, ret
+                if lat is not None:
+                    lat.append(time.perf_counter() - ts)
+            t_d = time.perf_counter()
+            return t_b - t_a, t_c - t_b, t_d - t_c, int(hit.sum())
+
+        for t in layers:   # verification needs the destination blocks to start empty
+            t[:, b_load] = 0
+        for _ in range(args.warmup):
+            e2e_step(None)
+        ok_e2e = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers)
+        lat: list[float] = []
+        parts = []
+        l1 = lib.crosscache_kernel_launches()
+        barrier()
+        torch.cuda.synchronize()
+        ts0 = time.perf_counter()
+        for _ in range(args.steps):
+            parts.append(e2e_step(lat))
+        torch.cuda.synchronize()
+        te = max_over_ranks(time.perf_counter() - ts0)
+        barrier()
+        e2e_launches = lib.crosscache_kernel_launches() - l1
+        st = w.stats()
+        w.unregister()
+        cc.exit()
+        hit_blocks = parts[-1][3] * bpc
+        save_s = max_over_ranks(statistics.median(p[1] for p in parts))
+        load_s = max_over_ranks(statistics.median(p[2] for p in parts))
+        hash_s = max_over_ranks(statistics.median(p[0] for p in parts))
+        p50 = max_over_ranks(statistics.median(lat)) * 1e3
+        e2e_value = total_payload * args.steps / te / GB
+        h2d = payload + flat_tok.nbytes + tok_lens.nbytes + nblk * 8
+        d2h = payload + hashes.nbytes
+        e2e = {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "ms_per_step": round(te / args.steps * 1e3, 3),
+               "save_gbs_per_gpu": round(payload / save_s / GB, 3),
+               "load_gbs_per_gpu": round(payload / load_s / GB, 3),
+               "hash_ms": round(hash_s * 1e3, 3), "p50_load_latency_ms": round(p50, 3),
+               "p90_load_latency_ms": round(float(np.percentile(lat, 90)) * 1e3, 3),
+               "hit_blocks_per_request": hit_blocks // REQS, "gpu_launches": int(e2e_launches),
+               "verified_bytes": bool(ok_e2e), "evictions": st["evictions"]}
+        link = {"d2h_peak_gbs": round(link_peak["d2h"], 2), "h2d_peak_gbs": round(link_peak["h2d"], 2),
+                "save_frac": round(payload / save_s / GB / link_peak["d2h"], 4),
+                "load_frac": round(payload / load_s / GB / link_peak["h2d"], 4),
+                "note": "per GPU; pinned 256 MiB cudaMemcpyAsync measured in this run"}
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        cpu = cpu_sample_run("port", args.cpu_seconds, None, os.cpu_count() or 1)
+        cpu.pop("times_s", None)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (seeded N(0,1) bf16 KV, uniform token ids, random block tables)",
+            "config": workload_config(world),
+            "roofline": {"bound": "hbm", "kernel": "kv_copy gather (save)", "achieved": round(achieved, 1),
+                         "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                         "peak_kind": peak_kind, "traffic": ncu_traffic(),
+                         "algorithmic_bytes_per_launch": 2 * payload,
+                         "gather_ms": round(gather_ms, 4), "scatter_ms": round(scatter_ms, 4),
+                         "scatter_frac": round(2 * payload / (scatter_ms / 1e3) / GB / hbm_peak, 4)},
+            "e2e": e2e, "link": link, "p50_load_latency_ms": round(p50, 3) if p50 is not None else None,
+            "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": clocks.summary(),
+            "verified_bytes": bool(ok_value),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

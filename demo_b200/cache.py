@@ -1,0 +1,186 @@
+"""In-process Python front end of the cache-manager C API (include/cache.h).
+
+CrossCache's vLLM worker hands its KV tensors to a separate C server over
+ZeroMQ + Ascend IPC keys (python/adaptor.py:149-228, src/main.c:244-348).
+This module drives the same C API in the worker's own process: the paged KV
+tensors are registered by raw device pointer (per_len 8), and keys / block
+ids go straight to cache_store / cache_load / cache_lookup.  PyTorch is used
+only to read tensor pointers and shapes.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import errno
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+
+from ._lib import (CACHE_BACKEND_CUDA, CACHE_BACKEND_MEM, CacheStats, ModelInfo, WorkerContext,
+                   lib)
+
+KEY_LEN = 32
+
+
+class CacheError(RuntimeError):
+    def __init__(self, what: str, ret: int):
+        name = errno.errorcode.get(-ret, str(ret)) if ret < 0 else str(ret)
+        super().__init__(f"{what} failed: {ret} ({name})")
+        self.ret = ret
+
+
+def init(chunk_size: int = 256, pool_size: int = 4 << 30, root_dir: str | None = None,
+         backend: int = CACHE_BACKEND_CUDA) -> None:
+    """cache_init (CrossCache cache.c:759-787) with an explicit backend."""
+    ret = lib.cache_init_backend(chunk_size, pool_size, root_dir.encode() if root_dir else None, backend)
+    if ret:
+        raise CacheError("cache_init", ret)
+
+
+def exit() -> None:  # noqa: A001 - mirrors cache_exit
+    lib.cache_exit()
+
+
+def _keys_buffer(keys: Sequence[bytes]) -> bytes:
+    for k in keys:
+        if len(k) != KEY_LEN:
+            raise ValueError(f"keys must be {KEY_LEN} bytes (got {len(k)})")
+    return b"".join(keys)
+
+
+@dataclass
+class KVLayout:
+    num_layers: int
+    num_blocks: int
+    block_size: int
+    hidden_dim_size: int     # heads * head_dim of this rank
+    element_size: int
+    kv: int                  # 2 = K and V, 1 = K only (MLA)
+
+    @property
+    def unit(self) -> int:
+        return self.hidden_dim_size * self.element_size
+
+    @property
+    def per_token_size(self) -> int:
+        return self.kv * self.num_layers * self.unit
+
+
+class Worker:
+    """One registered worker: a (model, world_size, rank) entry of the cache.
+
+    `k_ptrs` / `v_ptrs` are per-layer base addresses of the K and V planes
+    (device pointers for the CUDA backend, host pointers for the MEM backend).
+    """
+
+    def __init__(self, model_name: str, layout: KVLayout, k_ptrs: Sequence[int],
+                 v_ptrs: Sequence[int] | None, node_id: int = 0, world_size: int = 1,
+                 rank: int = 0):
+        if len(k_ptrs) != layout.num_layers or (v_ptrs is not None and len(v_ptrs) != layout.num_layers):
+            raise ValueError("one pointer per layer")
+        if (v_ptrs is None) != (layout.kv == 1):
+            raise ValueError("layout.kv must be 1 exactly when v_ptrs is None")
+        self.layout = layout
+        self._name = model_name.encode()
+        self._k = np.asarray(k_ptrs, dtype=np.uint64)
+        self._v = np.asarray(v_ptrs, dtype=np.uint64) if v_ptrs is not None else None
+        self.ctx = WorkerContext()
+        self.ctx.model = ModelInfo(self._name, layout.element_size, layout.num_layers, layout.hidden_dim_size)
+        self.ctx.node_id = node_id
+        self.ctx.world_size = world_size
+        self.ctx.rank_id = rank
+        self.ctx.per_token_size = layout.per_token_size
+        self.ctx.num_blocks = layout.num_blocks
+        self.ctx.block_size = layout.block_size
+        self.ctx.per_len = 8
+        self.ctx.k_raw_ptrs = self._k.ctypes.data
+        self.ctx.v_raw_ptrs = self._v.ctypes.data if self._v is not None else None
+        self.registered = False
+
+    # -- reference API ------------------------------------------------------
+    def register(self) -> None:
+        ret = lib.cache_register(C.byref(self.ctx))
+        if ret:
+            raise CacheError("cache_register", ret)
+        self.registered = True
+
+    def unregister(self) -> None:
+        if self.registered:
+            lib.cache_unregister(C.byref(self.ctx))
+            self.registered = False
+
+    def store(self, keys: Sequence[bytes], block_ids: Sequence[int]) -> int:
+        """cache_store: returns 0 or a negative errno (reference semantics)."""
+        kb = _keys_buffer(keys)
+        b = np.ascontiguousarray(np.asarray(block_ids, dtype=np.uint64))
+        return lib.cache_store(C.byref(self.ctx), kb, KEY_LEN, b.ctypes.data, len(b))
+
+    def load(self, keys: Sequence[bytes], block_ids: Sequence[int]) -> int:
+        kb = _keys_buffer(keys)
+        b = np.ascontiguousarray(np.asarray(block_ids, dtype=np.uint64))
+        return lib.cache_load(C.byref(self.ctx), kb, KEY_LEN, b.ctypes.data, len(b))
+
+    def lookup(self, keys: Sequence[bytes]) -> int:
+        """cache_lookup: byte offset of the first miss (hit keys * 32)."""
+        kb = _keys_buffer(keys)
+        return lib.cache_lookup(C.byref(self.ctx), kb, len(keys), KEY_LEN)
+
+    # -- additions ----------------------------------------------------------
+    def lookup_batch(self, keys_per_request: Sequence[Sequence[bytes]]) -> np.ndarray:
+        """cache_lookup_batch: leading hit keys per request."""
+        nums = np.array([len(k) for k in keys_per_request], dtype=np.uint32)
+        kb = b"".join(_keys_buffer(k) for k in keys_per_request)
+        out = np.zeros(len(nums), dtype=np.uint32)
+        ret = lib.cache_lookup_batch(C.byref(self.ctx), kb, nums.ctypes.data, len(nums), KEY_LEN,
+                                     out.ctypes.data)
+        if ret and ret != -errno.ENOENT:
+            raise CacheError("cache_lookup_batch", ret)
+        return out
+
+    def stats(self) -> dict:
+        s = CacheStats()
+        ret = lib.cache_get_stats(C.byref(self.ctx), C.byref(s))
+        if ret:
+            raise CacheError("cache_get_stats", ret)
+        return s.as_dict()
+
+    def clear(self) -> None:
+        ret = lib.cache_clear(C.byref(self.ctx))
+        if ret:
+            raise CacheError("cache_clear", ret)
+
+
+def layout_from_kv_tensors(kv_caches, tp_heads: int | None = None) -> tuple[KVLayout, list[int], list[int] | None]:
+    """Layout and per-layer K/V plane pointers of vLLM paged caches.
+
+    kv_caches: iterable of per-layer tensors shaped [2, num_blocks, block_size,
+    heads, head_dim] (FlashAttention NHD layout, K plane then V plane) or
+    [num_blocks, block_size, width] for a K-only MLA latent cache.
+    """
+    layers = list(kv_caches)
+    t0 = layers[0]
+    if t0.dim() == 5:
+        _, nb, bs, h, d = t0.shape
+        kv = 2
+        hidden = h * d
+    elif t0.dim() == 3:
+        nb, bs, hidden = t0.shape
+        kv = 1
+    else:
+        raise ValueError(f"unsupported KV tensor shape {tuple(t0.shape)}")
+    k, v = [], []
+    for t in layers:
+        if not t.is_contiguous() or t.shape != t0.shape or t.dtype != t0.dtype:
+            raise ValueError("KV layer tensors must be contiguous and identically shaped")
+        if kv == 2:
+            k.append(t[0].data_ptr())
+            v.append(t[1].data_ptr())
+        else:
+            k.append(t.data_ptr())
+    lay = KVLayout(num_layers=len(layers), num_blocks=int(nb), block_size=int(bs),
+                   hidden_dim_size=int(hidden), element_size=t0.element_size(), kv=kv)
+    return lay, k, (v if kv == 2 else None)
+
+
+__all__ = ["init", "exit", "Worker", "KVLayout", "layout_from_kv_tensors", "CacheError",
+           "CACHE_BACKEND_CUDA", "CACHE_BACKEND_MEM", "KEY_LEN"]

@@ -1,0 +1,747 @@
+/*
+ * CUDA backend of the device adaptor ABI (include/device.h).
+ *
+ * Replaces CrossCache's Ascend adaptor src/device/npu/npu.cpp:
+ *   AllocPinnedPtr  mmap + cudaHostRegister(MAPPED|PORTABLE)   (npu.cpp:49-90)
+ *   WrapperPtr      device copy of a host buffer               (npu.cpp:100-123)
+ *   OpenIPCKeys     per-layer handle -> device pointer array   (npu.cpp:131-180)
+ *                   per_len 8: raw pointers of this process; 64: a
+ *                   cudaIpcMemHandle_t; 72: handle + uint64 byte offset
+ *   TransferKVCache one record, synchronous                    (npu.cpp:188-251)
+ *   Reset           drains and frees this process's streams and staging
+ *                   buffers on the device.  It does NOT reset the GPU (the
+ *                   reference calls aclrtResetDeviceForce, npu.cpp:253-257).
+ *
+ * Transfers run on "lanes": per device a small pool of (kernel stream, copy
+ * stream, staging ring of NSUB sub-slots in HBM, events, metadata buffers),
+ * created once and reused, so no call allocates device memory or creates a
+ * stream (the reference creates a stream and allocates the slot map per
+ * chunk, npu.cpp:100-123,205).  A save gathers a group of records into a
+ * staging sub-slot with the kv_copy kernel, then a copy engine moves it to
+ * the pinned host records while the next group is gathered; a load is the
+ * mirror image.  Waits are host-side cudaEventQuery polls with a deadline
+ * (CROSSCACHE_TIMEOUT_MS, default 120000) that end in -ETIMEDOUT; no kernel
+ * spins on anything.
+ *
+ * CROSSCACHE_XFER_MODE=direct makes the kernels read/write the mapped pinned
+ * records over the host link instead (no staging, no copy engine).
+ */
+#include "adaptor.h"
+#include "kvcopy.h"
+
+extern "C" {
+#include "../infra/log.h"
+}
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cerrno>
+#include <chrono>
+#include <condition_variable>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <new>
+#include <sys/mman.h>
+#include <thread>
+#include <unistd.h>
+#include <vector>
+
+namespace {
+
+constexpr int kNumSub = 3;                       /* staging ring depth per lane */
+constexpr uint64_t kGroupTarget = 32ull << 20;   /* staging sub-slot target size */
+
+#define CU_OK(expr)                                                              \
+    ([&]() -> bool {                                                             \
+        cudaError_t _e = (expr);                                                 \
+        if (_e != cudaSuccess) {                                                 \
+            log_error("%s failed: %s", #expr, cudaGetErrorString(_e));           \
+            return false;                                                        \
+        }                                                                        \
+        return true;                                                             \
+    }())
+
+int env_int(const char *name, int dflt)
+{
+    const char *s = getenv(name);
+    return s ? atoi(s) : dflt;
+}
+
+/* poll an event until it completes or the deadline passes */
+int wait_event(cudaEvent_t ev, std::chrono::steady_clock::time_point deadline)
+{
+    int spins = 0;
+    for (;;) {
+        cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess)
+            return 0;
+        if (e != cudaErrorNotReady) {
+            log_error("event wait: %s", cudaGetErrorString(e));
+            return -EIO;
+        }
+        if (std::chrono::steady_clock::now() > deadline)
+            return -ETIMEDOUT;
+        if (++spins > 64)
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+struct Lane {
+    int dev = -1;
+    cudaStream_t ks = nullptr;   /* kernels */
+    cudaStream_t cs = nullptr;   /* copy engine */
+    cudaEvent_t kdone[kNumSub] = {};
+    cudaEvent_t cdone[kNumSub] = {};
+    cudaEvent_t fin = nullptr;
+    uint8_t *staging = nullptr;  /* kNumSub sub-slots of sub_bytes */
+    uint64_t sub_bytes = 0;
+    uint64_t *d_subrec = nullptr;  /* kNumSub x max_group record pointers */
+    uint32_t max_group = 0;
+    uint64_t cur_rec_bytes = 0;    /* record size d_subrec was built for */
+    uint64_t *d_meta = nullptr;    /* device metadata (block ids / records) */
+    uint64_t *h_meta = nullptr;    /* pinned host mirror */
+    uint64_t meta_cap = 0;         /* uint64 words */
+    int32_t *d_err = nullptr;
+    int32_t *h_err = nullptr;
+    bool poisoned = false;
+
+    bool init(int device)
+    {
+        dev = device;
+        if (!CU_OK(cudaStreamCreateWithFlags(&ks, cudaStreamNonBlocking)) ||
+            !CU_OK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking)))
+            return false;
+        for (int i = 0; i < kNumSub; i++)
+            if (!CU_OK(cudaEventCreateWithFlags(&kdone[i], cudaEventDisableTiming)) ||
+                !CU_OK(cudaEventCreateWithFlags(&cdone[i], cudaEventDisableTiming)))
+                return false;
+        if (!CU_OK(cudaEventCreateWithFlags(&fin, cudaEventDisableTiming)) ||
+            !CU_OK(cudaMalloc(&d_err, sizeof(int32_t))) ||
+            !CU_OK(cudaHostAlloc(&h_err, sizeof(int32_t), cudaHostAllocDefault)))
+            return false;
+        return ensure_meta(1 << 16);
+    }
+
+    bool ensure_meta(uint64_t words)
+    {
+        if (words <= meta_cap)
+            return true;
+        uint64_t cap = std::max<uint64_t>(words, meta_cap * 2);
+        if (d_meta)
+            cudaFree(d_meta);
+        if (h_meta)
+            cudaFreeHost(h_meta);
+        d_meta = nullptr;
+        h_meta = nullptr;
+        meta_cap = 0;
+        if (!CU_OK(cudaMalloc(&d_meta, cap * 8)) ||
+            !CU_OK(cudaHostAlloc(&h_meta, cap * 8, cudaHostAllocDefault)))
+            return false;
+        meta_cap = cap;
+        return true;
+    }
+
+    /* staging sub-slots able to hold `group` records of rec_bytes each */
+    bool ensure_staging(uint64_t rec_bytes, uint32_t *group)
+    {
+        uint64_t want = std::max(kGroupTarget, rec_bytes);
+        if (want > sub_bytes) {
+            if (staging)
+                cudaFree(staging);
+            if (d_subrec)
+                cudaFree(d_subrec);
+            staging = nullptr;
+            d_subrec = nullptr;
+            sub_bytes = 0;
+            max_group = 0;
+            cur_rec_bytes = 0;
+            if (!CU_OK(cudaMalloc(&staging, want * kNumSub)))
+                return false;
+            sub_bytes = want;
+        }
+        uint32_t g = (uint32_t)std::max<uint64_t>(1, sub_bytes / rec_bytes);
+        if (g > max_group) {
+            if (d_subrec)
+                cudaFree(d_subrec);
+            d_subrec = nullptr;
+            max_group = 0;
+            cur_rec_bytes = 0;
+            if (!CU_OK(cudaMalloc(&d_subrec, (uint64_t)kNumSub * g * 8)))
+                return false;
+            max_group = g;
+        }
+        *group = g;
+        if (rec_bytes == cur_rec_bytes)
+            return true;
+        /* record pointers of each sub-slot for this record size (tiny upload) */
+        std::vector<uint64_t> ptrs((size_t)kNumSub * max_group);
+        for (int s = 0; s < kNumSub; s++)
+            for (uint32_t j = 0; j < max_group; j++)
+                ptrs[(size_t)s * max_group + j] =
+                    (uint64_t)(uintptr_t)(staging + s * sub_bytes + (uint64_t)j * rec_bytes);
+        if (!CU_OK(cudaMemcpyAsync(d_subrec, ptrs.data(), ptrs.size() * 8,
+                                   cudaMemcpyHostToDevice, ks)) ||
+            !CU_OK(cudaStreamSynchronize(ks)))
+            return false;
+        cur_rec_bytes = rec_bytes;
+        return true;
+    }
+
+    void release()
+    {
+        if (dev < 0)
+            return;
+        cudaSetDevice(dev);
+        if (ks)
+            cudaStreamSynchronize(ks);
+        if (cs)
+            cudaStreamSynchronize(cs);
+        for (int i = 0; i < kNumSub; i++) {
+            if (kdone[i])
+                cudaEventDestroy(kdone[i]);
+            if (cdone[i])
+                cudaEventDestroy(cdone[i]);
+        }
+        if (fin)
+            cudaEventDestroy(fin);
+        if (staging)
+            cudaFree(staging);
+        if (d_subrec)
+            cudaFree(d_subrec);
+        if (d_meta)
+            cudaFree(d_meta);
+        if (h_meta)
+            cudaFreeHost(h_meta);
+        if (d_err)
+            cudaFree(d_err);
+        if (h_err)
+            cudaFreeHost(h_err);
+        if (ks)
+            cudaStreamDestroy(ks);
+        if (cs)
+            cudaStreamDestroy(cs);
+        *this = Lane();
+    }
+};
+
+struct DeviceCtx {
+    int dev;
+    std::mutex mu;
+    std::condition_variable cv;
+    std::vector<Lane *> all;
+    std::vector<Lane *> idle;
+    int max_lanes;
+    int host_ptr_ok = 0;   /* registered host memory usable at its host address */
+};
+
+struct IpcSet {
+    int dev;
+    std::vector<void *> opened;       /* cudaIpcOpenMemHandle bases */
+    std::vector<uint64_t> host_ptrs;  /* layer bases (host mirror) */
+};
+
+struct PinnedRegion {
+    uint64_t size;
+};
+
+class CudaAdaptor : public Adaptor
+{
+public:
+    CudaAdaptor()
+    {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+            log_error("cuda adaptor: no CUDA device visible");
+            throw std::bad_alloc();
+        }
+        num_devices_ = n;
+        timeout_ms_ = env_int("CROSSCACHE_TIMEOUT_MS", 120000);
+        lanes_per_dev_ = std::max(1, env_int("CROSSCACHE_LANES", 2));
+        const char *m = getenv("CROSSCACHE_XFER_MODE");
+        direct_ = m && !strcmp(m, "direct");
+    }
+
+    ~CudaAdaptor() override
+    {
+        std::lock_guard<std::mutex> g(reg_mu_);
+        for (auto &kv : devs_)
+            drain(kv.second.get());
+        for (auto &kv : ipc_) {
+            cudaSetDevice(kv.second.dev);
+            for (void *p : kv.second.opened)
+                cudaIpcCloseMemHandle(p);
+            cudaFree(kv.first);
+        }
+        for (auto &kv : pinned_) {
+            cudaHostUnregister(kv.first);
+            munmap(kv.first, kv.second.size);
+        }
+    }
+
+    void *AllocPinnedPtr(uint8_t nid, uint64_t size, unsigned int, void **daddr) override
+    {
+        if (!size || size % 4096) {
+            log_error("device(%u) pinned size %lu is not 4 KiB aligned", nid, (unsigned long)size);
+            return nullptr;
+        }
+        if (nid >= num_devices_ || !CU_OK(cudaSetDevice(nid)))
+            return nullptr;
+        void *addr = mmap(nullptr, size, PROT_READ | PROT_WRITE, MAP_PRIVATE | MAP_ANONYMOUS, -1, 0);
+        if (addr == MAP_FAILED) {
+            log_error("device(%u) mmap(%lu) failed errno %d", nid, (unsigned long)size, errno);
+            return nullptr;
+        }
+        madvise(addr, size, MADV_HUGEPAGE);
+        if (!CU_OK(cudaHostRegister(addr, size, cudaHostRegisterMapped | cudaHostRegisterPortable))) {
+            munmap(addr, size);
+            return nullptr;
+        }
+        void *dptr = nullptr;
+        if (!CU_OK(cudaHostGetDevicePointer(&dptr, addr, 0))) {
+            cudaHostUnregister(addr);
+            munmap(addr, size);
+            return nullptr;
+        }
+        {
+            std::lock_guard<std::mutex> g(reg_mu_);
+            pinned_[addr] = PinnedRegion{size};
+        }
+        if (daddr)
+            *daddr = dptr;
+        log_debug("device(%u) pinned %lu B host %p dev %p", nid, (unsigned long)size, addr, dptr);
+        return addr;
+    }
+
+    void FreePinnedPtr(void *addr, uint64_t size) override
+    {
+        {
+            std::lock_guard<std::mutex> g(reg_mu_);
+            pinned_.erase(addr);
+        }
+        cudaHostUnregister(addr);
+        munmap(addr, size);
+    }
+
+    void *WrapperPtr(uint8_t nid, void *addr, uint64_t size) override
+    {
+        void *d = nullptr;
+        if (nid >= num_devices_ || !CU_OK(cudaSetDevice(nid)) || !CU_OK(cudaMalloc(&d, size)))
+            return nullptr;
+        if (!CU_OK(cudaMemcpy(d, addr, size, cudaMemcpyHostToDevice))) {
+            cudaFree(d);
+            return nullptr;
+        }
+        return d;
+    }
+
+    void UnWrapperPtr(void *daddr) override
+    {
+        if (daddr)
+            cudaFree(daddr);
+    }
+
+    void *OpenIPCKeys(uint8_t nid, uint16_t per_len, uint16_t num, void *data) override
+    {
+        if (!num || !data || nid >= num_devices_ || !CU_OK(cudaSetDevice(nid)))
+            return nullptr;
+        if (per_len != 8 && per_len != sizeof(cudaIpcMemHandle_t) &&
+            per_len != sizeof(cudaIpcMemHandle_t) + 8) {
+            log_error("open_ipc_keys: unsupported per_len %u (8, 64 or 72)", per_len);
+            return nullptr;
+        }
+        IpcSet set;
+        set.dev = nid;
+        const uint8_t *p = static_cast<const uint8_t *>(data);
+        for (uint16_t i = 0; i < num; i++, p += per_len) {
+            uint64_t ptr = 0;
+            if (per_len == 8) {
+                memcpy(&ptr, p, 8);
+            } else {
+                cudaIpcMemHandle_t h;
+                uint64_t off = 0;
+                memcpy(&h, p, sizeof(h));
+                if (per_len > sizeof(h))
+                    memcpy(&off, p + sizeof(h), 8);
+                void *base = nullptr;
+                if (!CU_OK(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess))) {
+                    for (void *o : set.opened)
+                        cudaIpcCloseMemHandle(o);
+                    return nullptr;
+                }
+                set.opened.push_back(base);
+                ptr = (uint64_t)(uintptr_t)base + off;
+            }
+            set.host_ptrs.push_back(ptr);
+        }
+        void *d = nullptr;
+        if (!CU_OK(cudaMalloc(&d, (size_t)num * 8)) ||
+            !CU_OK(cudaMemcpy(d, set.host_ptrs.data(), (size_t)num * 8, cudaMemcpyHostToDevice))) {
+            if (d)
+                cudaFree(d);
+            for (void *o : set.opened)
+                cudaIpcCloseMemHandle(o);
+            return nullptr;
+        }
+        std::lock_guard<std::mutex> g(reg_mu_);
+        ipc_[d] = std::move(set);
+        return d;
+    }
+
+    void CloseIPCKeys(void *daddr) override
+    {
+        IpcSet set;
+        {
+            std::lock_guard<std::mutex> g(reg_mu_);
+            auto it = ipc_.find(daddr);
+            if (it == ipc_.end())
+                return;
+            set = std::move(it->second);
+            ipc_.erase(it);
+        }
+        cudaSetDevice(set.dev);
+        for (void *o : set.opened)
+            cudaIpcCloseMemHandle(o);
+        cudaFree(daddr);
+    }
+
+    int TransferKVCache(struct transfer_params *p) override;
+    int TransferKVCacheBatch(struct transfer_batch *b) override;
+
+    void Reset(uint8_t nid) override
+    {
+        std::unique_ptr<DeviceCtx> ctx;
+        {
+            std::lock_guard<std::mutex> g(reg_mu_);
+            auto it = devs_.find(nid);
+            if (it == devs_.end())
+                return;
+            ctx = std::move(it->second);
+            devs_.erase(it);
+        }
+        drain(ctx.get());
+    }
+
+private:
+    DeviceCtx *device(int dev)
+    {
+        std::lock_guard<std::mutex> g(reg_mu_);
+        auto &slot = devs_[dev];
+        if (!slot) {
+            slot.reset(new DeviceCtx());
+            slot->dev = dev;
+            slot->max_lanes = lanes_per_dev_;
+            int ok = 0;
+            cudaDeviceGetAttribute(&ok, cudaDevAttrCanUseHostPointerForRegisteredMem, dev);
+            slot->host_ptr_ok = ok;
+        }
+        return slot.get();
+    }
+
+    Lane *acquire(DeviceCtx *ctx)
+    {
+        std::unique_lock<std::mutex> lk(ctx->mu);
+        for (;;) {
+            if (!ctx->idle.empty()) {
+                Lane *l = ctx->idle.back();
+                ctx->idle.pop_back();
+                return l;
+            }
+            if ((int)ctx->all.size() < ctx->max_lanes) {
+                Lane *l = new (std::nothrow) Lane();
+                if (!l || !l->init(ctx->dev)) {
+                    if (l) {
+                        l->release();
+                        delete l;
+                    }
+                    return nullptr;
+                }
+                ctx->all.push_back(l);
+                return l;
+            }
+            if (ctx->cv.wait_for(lk, std::chrono::milliseconds(timeout_ms_)) == std::cv_status::timeout &&
+                ctx->idle.empty())
+                return nullptr;
+        }
+    }
+
+    void give_back(DeviceCtx *ctx, Lane *l)
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        if (l->poisoned)
+            return;   /* device work may still be in flight: never reuse */
+        ctx->idle.push_back(l);
+        ctx->cv.notify_one();
+    }
+
+    void drain(DeviceCtx *ctx)
+    {
+        if (!ctx)
+            return;
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        for (Lane *l : ctx->all) {
+            if (!l->poisoned) {
+                l->release();
+                delete l;
+            }
+        }
+        ctx->all.clear();
+        ctx->idle.clear();
+    }
+
+    std::chrono::steady_clock::time_point deadline() const
+    {
+        return std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms_);
+    }
+
+    int run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch *b);
+    int finish(Lane *l, cudaStream_t last, int ret);
+
+    int num_devices_ = 0;
+    int timeout_ms_ = 120000;
+    int lanes_per_dev_ = 2;
+    bool direct_ = false;
+    std::mutex reg_mu_;
+    std::map<int, std::unique_ptr<DeviceCtx>> devs_;
+    std::map<void *, IpcSet> ipc_;
+    std::map<void *, PinnedRegion> pinned_;
+};
+
+/* read back the error word after everything queued on `last`, then wait */
+int CudaAdaptor::finish(Lane *l, cudaStream_t last, int ret)
+{
+    if (ret == 0) {
+        if (last != l->ks && !CU_OK(cudaStreamWaitEvent(l->ks, l->fin, 0)))
+            ret = -EIO;
+    }
+    if (ret == 0 && (!CU_OK(cudaMemcpyAsync(l->h_err, l->d_err, 4, cudaMemcpyDeviceToHost, l->ks)) ||
+                     !CU_OK(cudaEventRecord(l->fin, l->ks))))
+        ret = -EIO;
+    if (ret == 0 || ret == -EIO) {
+        int w = wait_event(l->fin, deadline());
+        if (w == -ETIMEDOUT) {
+            log_error("device(%d) transfer timed out after %d ms", l->dev, timeout_ms_);
+            l->poisoned = true;
+            return -ETIMEDOUT;
+        }
+        if (w)
+            ret = w;
+    }
+    if (ret == 0 && *l->h_err) {
+        log_error("device(%d) kv copy reported error bits 0x%x", l->dev, *l->h_err);
+        ret = -EINVAL;
+    }
+    return ret;
+}
+
+int CudaAdaptor::run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch *b)
+{
+    const uint32_t R = b->num_records;
+    const uint32_t bpr = b->num_tokens / b->block_size;
+    const uint64_t unit = (uint64_t)b->hidden_dim_size * b->caches_element_size;
+    const uint64_t rec_bytes = (uint64_t)(b->value_ptrs ? 2 : 1) * b->num_layers * b->num_tokens * unit;
+    const bool save = b->direction;
+    const bool device_recs = b->record_on_device != 0;
+    const bool direct = device_recs || direct_;
+
+    /* metadata: block ids, then (direct modes) record addresses */
+    uint64_t words = (uint64_t)R * bpr + (direct ? R : 0);
+    if (!l->ensure_meta(words))
+        return -ENOMEM;
+    memcpy(l->h_meta, b->block_ids, (uint64_t)R * bpr * 8);
+    if (direct) {
+        for (uint32_t r = 0; r < R; r++) {
+            void *p = b->records[r];
+            if (!device_recs && !ctx->host_ptr_ok) {
+                void *dp = nullptr;
+                if (!CU_OK(cudaHostGetDevicePointer(&dp, p, 0)))
+                    return -EINVAL;
+                p = dp;
+            }
+            l->h_meta[(uint64_t)R * bpr + r] = (uint64_t)(uintptr_t)p;
+        }
+    }
+    if (!CU_OK(cudaMemsetAsync(l->d_err, 0, 4, l->ks)) ||
+        !CU_OK(cudaMemcpyAsync(l->d_meta, l->h_meta, words * 8, cudaMemcpyHostToDevice, l->ks)))
+        return -EIO;
+
+    kv_copy_desc d{};
+    d.layer_k = static_cast<const uint64_t *>(b->keys_ptrs);
+    d.layer_v = static_cast<const uint64_t *>(b->value_ptrs);
+    d.error = l->d_err;
+    d.page_buffer_size = b->page_buffer_size;
+    d.unit_bytes = (uint32_t)unit;
+    d.num_tokens = b->num_tokens;
+    d.block_size = b->block_size;
+    d.num_layers = b->num_layers;
+    d.direction = save ? 1 : 0;
+
+    if (direct) {
+        d.block_ids = l->d_meta;
+        d.records = l->d_meta + (uint64_t)R * bpr;
+        d.num_records = R;
+        int ret = kv_copy_launch(&d, l->ks);
+        if (ret)
+            return ret;
+        return finish(l, l->ks, 0);
+    }
+
+    uint32_t G = 1;
+    if (!l->ensure_staging(rec_bytes, &G))
+        return -ENOMEM;
+    const uint32_t ngroups = (R + G - 1) / G;
+    for (uint32_t gi = 0; gi < ngroups; gi++) {
+        const int s = gi % kNumSub;
+        const uint32_t r0 = gi * G;
+        const uint32_t n = std::min(G, R - r0);
+        uint8_t *sub = l->staging + s * l->sub_bytes;
+        d.block_ids = l->d_meta + (uint64_t)r0 * bpr;
+        d.records = l->d_subrec + (uint64_t)s * l->max_group;
+        d.num_records = n;
+        if (save) {
+            if (gi >= (uint32_t)kNumSub && !CU_OK(cudaStreamWaitEvent(l->ks, l->cdone[s], 0)))
+                return -EIO;
+            if (kv_copy_launch(&d, l->ks))
+                return -EIO;
+            if (!CU_OK(cudaEventRecord(l->kdone[s], l->ks)) ||
+                !CU_OK(cudaStreamWaitEvent(l->cs, l->kdone[s], 0)))
+                return -EIO;
+            for (uint32_t j = 0; j < n; j++)
+                if (!CU_OK(cudaMemcpyAsync(b->records[r0 + j], sub + j * rec_bytes, rec_bytes,
+                                           cudaMemcpyDeviceToHost, l->cs)))
+                    return -EIO;
+            if (!CU_OK(cudaEventRecord(l->cdone[s], l->cs)))
+                return -EIO;
+        } else {
+            if (gi >= (uint32_t)kNumSub && !CU_OK(cudaStreamWaitEvent(l->cs, l->kdone[s], 0)))
+                return -EIO;
+            for (uint32_t j = 0; j < n; j++)
+                if (!CU_OK(cudaMemcpyAsync(sub + j * rec_bytes, b->records[r0 + j], rec_bytes,
+                                           cudaMemcpyHostToDevice, l->cs)))
+                    return -EIO;
+            if (!CU_OK(cudaEventRecord(l->cdone[s], l->cs)) ||
+                !CU_OK(cudaStreamWaitEvent(l->ks, l->cdone[s], 0)))
+                return -EIO;
+            if (kv_copy_launch(&d, l->ks))
+                return -EIO;
+            if (!CU_OK(cudaEventRecord(l->kdone[s], l->ks)))
+                return -EIO;
+        }
+    }
+    if (save) {
+        /* the last copies were queued on cs: make ks wait for them */
+        if (!CU_OK(cudaEventRecord(l->fin, l->cs)))
+            return -EIO;
+        return finish(l, l->cs, 0);
+    }
+    return finish(l, l->ks, 0);
+}
+
+int CudaAdaptor::TransferKVCacheBatch(struct transfer_batch *b)
+{
+    if (!b->num_records)
+        return 0;
+    if (!b->keys_ptrs || !b->records || !b->block_ids || !b->block_size || !b->num_layers ||
+        !b->num_tokens || b->num_tokens % b->block_size || !b->hidden_dim_size ||
+        !b->caches_element_size || b->devid >= num_devices_)
+        return -EINVAL;
+    if (!CU_OK(cudaSetDevice(b->devid)))
+        return -EIO;
+    DeviceCtx *ctx = device(b->devid);
+    Lane *l = acquire(ctx);
+    if (!l)
+        return -EBUSY;
+    int ret = run_batch(l, ctx, b);
+    if (ret && ret != -ETIMEDOUT && !l->poisoned) {
+        /* drain whatever was queued before the failure */
+        cudaStreamSynchronize(l->ks);
+        cudaStreamSynchronize(l->cs);
+    }
+    give_back(ctx, l);
+    return ret;
+}
+
+int CudaAdaptor::TransferKVCache(struct transfer_params *p)
+{
+    if (!p->caches || !p->keys_ptrs || !p->slot_mapping || !p->num_tokens || !p->num_layers ||
+        !p->hidden_dim_size || !p->caches_element_size || p->devid >= num_devices_)
+        return -EINVAL;
+    if (!CU_OK(cudaSetDevice(p->devid)))
+        return -EIO;
+    cudaPointerAttributes attr{};
+    if (!CU_OK(cudaPointerGetAttributes(&attr, p->caches)))
+        return -EINVAL;
+    const bool on_device = attr.type == cudaMemoryTypeDevice;
+    const uint64_t unit = (uint64_t)p->hidden_dim_size * p->caches_element_size;
+    const uint64_t rec_bytes = (uint64_t)(p->value_ptrs ? 2 : 1) * p->num_layers * p->num_tokens * unit;
+    void *host = p->caches_h ? p->caches_h : p->caches;
+
+    DeviceCtx *ctx = device(p->devid);
+    Lane *l = acquire(ctx);
+    if (!l)
+        return -EBUSY;
+    int ret = 0;
+    kv_copy_desc d{};
+    d.layer_k = static_cast<const uint64_t *>(p->keys_ptrs);
+    d.layer_v = static_cast<const uint64_t *>(p->value_ptrs);
+    d.slots = static_cast<const int64_t *>(p->slot_mapping);
+    d.error = l->d_err;
+    d.page_buffer_size = p->page_buffer_size;
+    d.unit_bytes = (uint32_t)unit;
+    d.num_tokens = p->num_tokens;
+    d.block_size = 1;
+    d.num_layers = p->num_layers;
+    d.num_records = 1;
+    d.direction = p->direction ? 1 : 0;
+
+    if (!l->ensure_meta(1) || !CU_OK(cudaMemsetAsync(l->d_err, 0, 4, l->ks))) {
+        ret = -EIO;
+    } else if (on_device || direct_) {
+        l->h_meta[0] = (uint64_t)(uintptr_t)p->caches;
+        if (!CU_OK(cudaMemcpyAsync(l->d_meta, l->h_meta, 8, cudaMemcpyHostToDevice, l->ks)))
+            ret = -EIO;
+        d.records = l->d_meta;
+        if (!ret)
+            ret = kv_copy_launch(&d, l->ks);
+        ret = finish(l, l->ks, ret);
+    } else {
+        uint32_t G = 1;
+        if (!l->ensure_staging(rec_bytes, &G)) {
+            ret = -ENOMEM;
+        } else {
+            d.records = l->d_subrec;   /* sub-slot 0, first record */
+            if (p->direction) {
+                ret = kv_copy_launch(&d, l->ks);
+                if (!ret && !CU_OK(cudaMemcpyAsync(host, l->staging, rec_bytes, cudaMemcpyDeviceToHost, l->ks)))
+                    ret = -EIO;
+            } else {
+                if (!CU_OK(cudaMemcpyAsync(l->staging, host, rec_bytes, cudaMemcpyHostToDevice, l->ks)))
+                    ret = -EIO;
+                if (!ret)
+                    ret = kv_copy_launch(&d, l->ks);
+            }
+            ret = finish(l, l->ks, ret);
+        }
+    }
+    if (ret && ret != -ETIMEDOUT && !l->poisoned)
+        cudaStreamSynchronize(l->ks);
+    give_back(ctx, l);
+    return ret;
+}
+
+}  // namespace
+
+adaptor_t *cuda_adaptor_create(void)
+{
+    try {
+        return new CudaAdaptor();
+    } catch (...) {
+        log_error("cuda adaptor create failed");
+        return nullptr;
+    }
+}
+
+void cuda_adaptor_destroy(adaptor_t *adaptor) { delete adaptor; }

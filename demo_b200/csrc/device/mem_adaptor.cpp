@@ -1,0 +1,194 @@
+/*
+ * CPU memcpy backend (CACHE_BACKEND_MEM).
+ *
+ * The host-only counterpart of CrossCache's MemAdaptor
+ * (src/device/mem/mem.cpp:17-191): the "paged cache" and the records are host
+ * memory and a transfer is a memcpy per contiguous slot run with the record
+ * byte layout of mem.cpp:136-167.  Unlike the reference it uses the caller's
+ * layer pointers (the reference maps fake /fakekv:<i> shm files instead,
+ * mem.cpp:80-107) and does not build a per-token log string.  It is selected
+ * only explicitly (cache_init_backend(..., CACHE_BACKEND_MEM)) and never
+ * stands in for the CUDA backend.
+ */
+#include "adaptor.h"
+
+extern "C" {
+#include "../infra/log.h"
+#include "../infra/threadpool.h"
+}
+
+#include <cerrno>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <sys/mman.h>
+
+namespace {
+
+struct RecordJob {
+    const struct transfer_batch *tb;
+    uint32_t r;
+    cc_latch_t *latch;
+};
+
+/* copy one record; slot(t) from per-token slots or from block ids */
+int copy_record(uint8_t *rec, const uint64_t *kl, const uint64_t *vl,
+                const int64_t *slots, const uint64_t *bids, uint32_t bs,
+                uint64_t page_buffer_size, uint32_t L, uint32_t C,
+                uint64_t unit, bool to_record)
+{
+    const int nkv = vl ? 2 : 1;
+    for (int kv = 0; kv < nkv; kv++) {
+        const uint64_t *layers = kv ? vl : kl;
+        for (uint32_t l = 0; l < L; l++) {
+            uint8_t *base = reinterpret_cast<uint8_t *>(layers[l]);
+            uint8_t *rl = rec + ((uint64_t)kv * L + l) * C * unit;
+            if (!base)
+                return -EINVAL;
+            uint32_t t = 0;
+            while (t < C) {
+                int64_t s0 = slots ? slots[t] : (int64_t)(bids[t / bs] * bs + t % bs);
+                uint32_t n = 1;
+                for (;;) {
+                    if (t + n >= C)
+                        break;
+                    int64_t sn = slots ? slots[t + n]
+                                       : (int64_t)(bids[(t + n) / bs] * bs + (t + n) % bs);
+                    if (sn != s0 + (int64_t)n)
+                        break;
+                    n++;
+                }
+                if (s0 < 0 || (uint64_t)s0 + n > page_buffer_size)
+                    return -EINVAL;
+                uint8_t *p = base + (uint64_t)s0 * unit;
+                uint8_t *c = rl + (uint64_t)t * unit;
+                if (to_record)
+                    memcpy(c, p, n * unit);
+                else
+                    memcpy(p, c, n * unit);
+                t += n;
+            }
+        }
+    }
+    return 0;
+}
+
+void record_job(void *arg)
+{
+    RecordJob *j = static_cast<RecordJob *>(arg);
+    const struct transfer_batch *tb = j->tb;
+    uint32_t bpr = tb->num_tokens / tb->block_size;
+    int ret = copy_record(static_cast<uint8_t *>(tb->records[j->r]),
+                          static_cast<const uint64_t *>(tb->keys_ptrs),
+                          static_cast<const uint64_t *>(tb->value_ptrs), nullptr,
+                          tb->block_ids + (uint64_t)j->r * bpr, tb->block_size,
+                          tb->page_buffer_size, tb->num_layers, tb->num_tokens,
+                          (uint64_t)tb->hidden_dim_size * tb->caches_element_size,
+                          tb->direction);
+    cc_latch_done(j->latch, ret);
+}
+
+class MemAdaptor : public Adaptor
+{
+public:
+    MemAdaptor()
+    {
+        const char *s = getenv("CROSSCACHE_MEM_THREADS");
+        int n = s ? atoi(s) : 4;   /* the reference's CaCopy pool size */
+        pool_ = threadpool_create("CaCopy", n > 0 ? n : 4);
+        if (!pool_)
+            throw std::bad_alloc();
+    }
+    ~MemAdaptor() override { threadpool_destroy(pool_); }
+
+    void *AllocPinnedPtr(uint8_t nid, uint64_t size, unsigned int, void **daddr) override
+    {
+        if (!size || size % 4096) {
+            log_error("nid(%u) pool size %lu is not 4 KiB aligned", nid, (unsigned long)size);
+            return nullptr;
+        }
+        void *addr = mmap(nullptr, size, PROT_READ | PROT_WRITE,
+                          MAP_PRIVATE | MAP_ANONYMOUS | MAP_POPULATE, -1, 0);
+        if (addr == MAP_FAILED)
+            return nullptr;
+        if (daddr)
+            *daddr = addr;
+        return addr;
+    }
+    void FreePinnedPtr(void *addr, uint64_t size) override { munmap(addr, size); }
+    void *WrapperPtr(uint8_t, void *addr, uint64_t size) override
+    {
+        void *d = malloc(size);
+        if (d)
+            memcpy(d, addr, size);
+        return d;
+    }
+    void UnWrapperPtr(void *daddr) override { free(daddr); }
+    void *OpenIPCKeys(uint8_t, uint16_t per_len, uint16_t num, void *data) override
+    {
+        if (per_len != sizeof(uint64_t) || !num || !data) {
+            log_error("mem backend takes raw host pointers (per_len 8), got %u", per_len);
+            return nullptr;
+        }
+        void *a = malloc((size_t)num * sizeof(uint64_t));
+        if (a)
+            memcpy(a, data, (size_t)num * sizeof(uint64_t));
+        return a;
+    }
+    void CloseIPCKeys(void *daddr) override { free(daddr); }
+
+    int TransferKVCache(struct transfer_params *p) override
+    {
+        if (!p->caches || !p->keys_ptrs || !p->slot_mapping)
+            return -EINVAL;
+        return copy_record(static_cast<uint8_t *>(p->caches),
+                           static_cast<const uint64_t *>(p->keys_ptrs),
+                           static_cast<const uint64_t *>(p->value_ptrs),
+                           static_cast<const int64_t *>(p->slot_mapping), nullptr, 1,
+                           p->page_buffer_size, p->num_layers, p->num_tokens,
+                           (uint64_t)p->hidden_dim_size * p->caches_element_size,
+                           p->direction);
+    }
+
+    int TransferKVCacheBatch(struct transfer_batch *tb) override
+    {
+        if (!tb->num_records)
+            return 0;
+        if (!tb->records || !tb->block_ids || !tb->keys_ptrs || !tb->block_size ||
+            tb->num_tokens % tb->block_size)
+            return -EINVAL;
+        RecordJob *jobs = new (std::nothrow) RecordJob[tb->num_records];
+        if (!jobs)
+            return -ENOMEM;
+        cc_latch_t latch;
+        cc_latch_init(&latch, tb->num_records);
+        for (uint32_t r = 0; r < tb->num_records; r++) {
+            jobs[r] = RecordJob{tb, r, &latch};
+            if (threadpool_submit(pool_, &jobs[r], record_job))
+                record_job(&jobs[r]);
+        }
+        int ret = cc_latch_wait(&latch);
+        cc_latch_fini(&latch);
+        delete[] jobs;
+        return ret;
+    }
+
+    void Reset(uint8_t) override {}
+
+private:
+    threadpool_t *pool_;
+};
+
+}  // namespace
+
+adaptor_t *mem_adaptor_create(void)
+{
+    try {
+        return new MemAdaptor();
+    } catch (...) {
+        log_error("mem adaptor create failed");
+        return nullptr;
+    }
+}
+
+void mem_adaptor_destroy(adaptor_t *adaptor) { delete adaptor; }

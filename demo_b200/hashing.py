@@ -1,0 +1,81 @@
+"""Device block hashing (include/kvhash.h) for torch token tensors.
+
+block_hashes() returns the same bytes as vLLM's hash_block_tokens with the
+sha256 hash function (vllm/v1/core/kv_cache_utils.py:541-570) for every full
+block of every request; chunk_keys() strides them the way CrossCache's
+adaptor does (python/adaptor.py:32-40).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import hashlib
+import os
+from typing import Sequence
+
+import torch
+
+from ._lib import lib
+
+
+def none_hash_for_seed(seed: str | None = None) -> bytes:
+    """NONE_HASH as vLLM's init_none_hash derives it from PYTHONHASHSEED
+    (kv_cache_utils.py:97-112): sha256 of the pickled seed string; random
+    when no seed is set."""
+    import pickle
+
+    seed = os.getenv("PYTHONHASHSEED") if seed is None else seed
+    if seed is None:
+        return os.urandom(32)
+    return hashlib.sha256(pickle.dumps(seed, protocol=pickle.HIGHEST_PROTOCOL)).digest()
+
+
+def block_hashes_device(tokens: torch.Tensor, tok_offsets: torch.Tensor, num_blocks: torch.Tensor,
+                        out_offsets: torch.Tensor, block_size: int, none_hash: bytes,
+                        out: torch.Tensor, parents: torch.Tensor | None = None,
+                        stream: torch.cuda.Stream | None = None) -> None:
+    """Launch the hash kernel on device tensors (int32 tokens, int64 offsets,
+    int32 block counts, uint8 [total, 32] output).  Asynchronous."""
+    for t, dt in ((tokens, torch.int32), (tok_offsets, torch.int64), (num_blocks, torch.int32),
+                  (out_offsets, torch.int64), (out, torch.uint8)):
+        if t.dtype != dt or not t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"expected contiguous CUDA {dt}")
+    if len(none_hash) != 32:
+        raise ValueError("none_hash must be 32 bytes")
+    s = stream if stream is not None else torch.cuda.current_stream(tokens.device)
+    ret = lib.kv_block_hash_launch(tokens.data_ptr(), tok_offsets.data_ptr(), num_blocks.data_ptr(),
+                                   out_offsets.data_ptr(),
+                                   parents.data_ptr() if parents is not None else None,
+                                   tok_offsets.numel(), block_size, none_hash, out.data_ptr(),
+                                   C.c_void_p(s.cuda_stream))
+    if ret:
+        raise RuntimeError(f"kv_block_hash_launch failed: {ret}")
+
+
+def block_hashes(token_lists: Sequence[Sequence[int]], block_size: int, none_hash: bytes,
+                 device: int = 0) -> list[list[bytes]]:
+    """Chained block hashes of each request (host lists in, host bytes out),
+    computed on `device` through kv_block_hash_host."""
+    import numpy as np
+
+    lens = np.array([len(t) for t in token_lists], dtype=np.int64)
+    flat = np.ascontiguousarray(np.concatenate([np.asarray(t, dtype=np.int64) for t in token_lists])
+                                if len(token_lists) else np.zeros(0, np.int64))
+    if flat.size and (flat.min() < -2**31 or flat.max() >= 2**31):
+        raise ValueError("token ids must fit in int32")
+    flat = flat.astype(np.int32)
+    nblk = lens // block_size
+    out = np.zeros((int(nblk.sum()), 32), dtype=np.uint8)
+    ret = lib.kv_block_hash_host(device, flat.ctypes.data, lens.ctypes.data, len(lens), block_size,
+                                 none_hash, out.ctypes.data)
+    if ret < 0:
+        raise RuntimeError(f"kv_block_hash_host failed: {ret}")
+    res, off = [], 0
+    for n in nblk:
+        res.append([bytes(out[off + i]) for i in range(int(n))])
+        off += int(n)
+    return res
+
+
+def chunk_keys(hashes: Sequence[bytes], blocks_in_chunk: int) -> list[bytes]:
+    """Every blocks_in_chunk-th hash (CrossCache python/adaptor.py:32-40)."""
+    return list(hashes[blocks_in_chunk - 1::blocks_in_chunk])

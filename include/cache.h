@@ -1,0 +1,95 @@
+/*
+ * Cache-manager C API.
+ *
+ * The seven reference entry points keep the names, arguments, return
+ * conventions and semantics of CrossCache's include/cache/cache.h:8-23
+ * (implemented there in src/cache/cache.c:598-802):
+ *
+ *   cache_init        chunk_size tokens per record, pool_size bytes of pinned
+ *                     host memory per registered (model, tp_size, tp_rank),
+ *                     root_dir for the disk tier.  CUDA backend.
+ *   cache_register    import the worker's per-layer KV handles, allocate and
+ *                     pin the record pool.  0 or -ENOMEM/-EINVAL.
+ *   cache_lookup      walk keys in order and stop at the first key that is
+ *                     not cached; returns the BYTE OFFSET i * key_len of the
+ *                     first miss (reference cache.c:712-745).
+ *   cache_store       save bnum blocks as bnum / (chunk_size / block_size)
+ *                     records, one 32-byte key per record (cache.c:513-593).
+ *   cache_load        restore records for the keys into the given blocks.
+ *
+ * Additions (new, no reference counterpart) are listed after them.
+ */
+#ifndef __CACHE_H__
+#define __CACHE_H__
+
+#include "inner.h"
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+int cache_register(struct worker_context *wctx);
+
+void cache_unregister(struct worker_context *wctx);
+
+int cache_lookup(struct worker_context *wctx, uint8_t *keys,
+                 uint32_t key_num, uint32_t key_len);
+
+int cache_store(struct worker_context *wctx, uint8_t *keys,
+                uint32_t key_len, uint64_t *bids, uint32_t bnum);
+
+int cache_load(struct worker_context *wctx, uint8_t *keys,
+               uint32_t key_len, uint64_t *bids, uint32_t bnum);
+
+int cache_init(uint32_t chunk_size, uint64_t pool_size, const char *root_dir);
+
+void cache_exit();
+
+/* ---- new -------------------------------------------------------------- */
+
+#define CACHE_BACKEND_CUDA 0   /* sm_100a kernels + copy engines (default) */
+#define CACHE_BACKEND_MEM  1   /* host memcpy; paged cache in host memory   */
+
+/* cache_init with an explicit device backend.  cache_init() is
+ * cache_init_backend(..., CACHE_BACKEND_CUDA). */
+int cache_init_backend(uint32_t chunk_size, uint64_t pool_size,
+                       const char *root_dir, int backend);
+
+/* Batched prefix lookup over num_req requests.  Request r owns key_nums[r]
+ * consecutive keys of key_len bytes (requests are packed back to back in
+ * keys).  hit_keys[r] receives the number of leading keys of request r that
+ * are cached -- the value cache_lookup would return divided by key_len.
+ * Hits refresh the LRU position of their records.  Returns 0 or -ENOENT when
+ * the worker is not registered (then every hit_keys[r] is 0). */
+int cache_lookup_batch(struct worker_context *wctx, const uint8_t *keys,
+                       const uint32_t *key_nums, uint32_t num_req,
+                       uint32_t key_len, uint32_t *hit_keys);
+
+struct cache_stats {
+    uint64_t records_total;     /* records the pinned pool holds          */
+    uint64_t records_used;      /* records currently mapped to a key      */
+    uint64_t lookups;           /* keys examined by lookups               */
+    uint64_t lookup_hits;       /* ... of which cached                    */
+    uint64_t stored;            /* records written by cache_store         */
+    uint64_t store_dedup;       /* store keys already cached (no copy)    */
+    uint64_t loaded;            /* records restored by cache_load         */
+    uint64_t load_misses;       /* load keys that were not cached         */
+    uint64_t evictions;         /* records reclaimed by LRU eviction      */
+    uint64_t bytes_saved;
+    uint64_t bytes_loaded;
+};
+
+/* Counters of the (model, world_size, rank_id) entry of wctx.  0 or -ENOENT. */
+int cache_get_stats(struct worker_context *wctx, struct cache_stats *out);
+
+/* Drop every cached record of wctx's entry (the pool stays pinned).
+ * 0 or -ENOENT. */
+int cache_clear(struct worker_context *wctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

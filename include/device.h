@@ -1,0 +1,119 @@
+/*
+ * Device adaptor C ABI.
+ *
+ * struct transfer_params and the eight adaptor entry points keep the layout,
+ * names and semantics of CrossCache's include/inner_h/device.h:13-50, so the
+ * cache manager (or any caller written against the reference header) links
+ * against this library unchanged.  The reference selects the NPU, NPU-SDK or
+ * CPU-memcpy backend at compile time (device.h:32-41); this build adds the
+ * CUDA backend (cuda_adaptor_create) and keeps a CPU memcpy backend
+ * (mem_adaptor_create) for host-only operation.
+ *
+ * Additions beyond the reference ABI (marked "new" below) sit beside the
+ * reference entry points and never change them.
+ */
+#ifndef __DEVICE_H__
+#define __DEVICE_H__
+
+#include <stdint.h>
+#include <stdbool.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DEV_PTR
+
+/* One record (chunk) transfer; reference device.h:13-28.
+ *   caches            device-usable address of the record (pinned host alias
+ *                     from alloc_pinned_ptr, or device memory)
+ *   caches_h          host address of the same record
+ *   keys_ptrs         device array of num_layers uint64 K layer bases
+ *   value_ptrs        same for V, or NULL for a K-only (MLA) cache
+ *   page_buffer_size  slots per layer (num_blocks * block_size)
+ *   slot_mapping      device array of num_tokens int64 slots
+ *   direction         true: paged cache -> record (save, D->H);
+ *                     false: record -> paged cache (load, H->D)
+ * Record layout: K part [num_layers][num_tokens][unit] followed by the V part
+ * with the same shape, unit = hidden_dim_size * caches_element_size bytes
+ * (reference mem.cpp:141-157). */
+struct transfer_params {
+    void *caches, *caches_h;
+
+    void DEV_PTR *keys_ptrs;
+    void DEV_PTR *value_ptrs;
+    uint64_t page_buffer_size;
+    void DEV_PTR *slot_mapping;
+
+    uint8_t devid;
+    uint8_t caches_element_size;
+
+    uint16_t num_layers;
+    uint16_t num_tokens;
+    uint32_t hidden_dim_size;
+    bool direction;
+};
+
+typedef struct Adaptor adaptor_t;
+
+/* CUDA backend (sm_100a kernels, copy engines, pinned host pool).
+ * Replaces npu_adaptor_create/npu_adaptor_destroy (reference device.h:32-35,
+ * src/device/npu/npu.cpp:259-275). */
+adaptor_t *cuda_adaptor_create(void);
+void cuda_adaptor_destroy(adaptor_t *adaptor);
+
+/* CPU memcpy backend (reference device.h:39-40, src/device/mem/mem.cpp:175-191):
+ * only used when the caller asks for it explicitly (cache_init_backend with
+ * CACHE_BACKEND_MEM); pointers in open_ipc_keys must then be host addresses. */
+adaptor_t *mem_adaptor_create(void);
+void mem_adaptor_destroy(adaptor_t *adaptor);
+
+/* Reference device.h:43-50 (semantics of src/device/npu/npu.cpp:49-257). */
+void *alloc_pinned_ptr(adaptor_t *adaptor, uint8_t nid, uint64_t size, unsigned int flags, void **daddr);
+void free_pinned_ptr(adaptor_t *adaptor, void *addr, uint64_t size);
+void *wrapper_ptr(adaptor_t *adaptor, uint8_t nid, void *addr, uint64_t size);
+void unwrapper_ptr(adaptor_t *adaptor, void *daddr);
+void *open_ipc_keys(adaptor_t *adaptor, uint8_t nid, uint16_t per_len, uint16_t num, void *data);
+void close_ipc_keys(adaptor_t *adaptor, void *daddr);
+int transfer_kvcache(adaptor_t *adaptor, struct transfer_params *params);
+void reset_device(adaptor_t *adaptor, uint8_t nid);
+
+/* ---- new: batched transfer of many records in one call ----------------
+ * Moves num_records records between the paged cache and records[] with one
+ * metadata upload and a pipelined sequence of kernels and copy-engine
+ * transfers.  Record r holds the blocks
+ *   block_ids[r * (num_tokens / block_size) ... + (num_tokens / block_size) - 1]
+ * in the record layout of struct transfer_params.  records[] are host
+ * addresses inside a pool returned by alloc_pinned_ptr (record_on_device = 0)
+ * or device addresses (record_on_device = 1).  Synchronous: returns 0 after
+ * every byte has landed, a negative errno otherwise (-EINVAL for a block id
+ * outside the paged cache, -ETIMEDOUT when the device did not finish within
+ * the adaptor's deadline).  Thread-safe. */
+struct transfer_batch {
+    void DEV_PTR *keys_ptrs;
+    void DEV_PTR *value_ptrs;
+    uint64_t page_buffer_size;
+    void **records;
+    const uint64_t *block_ids;
+    uint32_t num_records;
+    uint32_t block_size;
+    uint32_t hidden_dim_size;
+    uint16_t num_layers;
+    uint16_t num_tokens;
+    uint8_t devid;
+    uint8_t caches_element_size;
+    uint8_t record_on_device;
+    bool direction;
+};
+
+int transfer_kvcache_batch(adaptor_t *adaptor, struct transfer_batch *batch);
+
+/* new: number of device kernels this library has launched since load
+ * (every backend; the CPU backend never launches any). */
+uint64_t crosscache_kernel_launches(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

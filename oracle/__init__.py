@@ -1,0 +1,15 @@
+"""ORACLE -- test infrastructure only.
+
+CPU restatements of CrossCache's hot path used as the parity checker by
+tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs.
+Nothing in the demo_b200 product package imports this package.
+
+  kvcopy.py       record gather/scatter: C restatement (liboracle.so) of
+                  src/device/mem/mem.cpp:114-173 + src/cache/cache.c:345-398,
+                  513-593, and a loader for the reference's own mem.cpp
+                  compiled into _ref/libref_mem.so (Makefile target `ref`)
+  blockhash.py    vLLM's chained sha256 block hash (pickle protocol 5 framing
+                  restated byte by byte + hashlib SHA-256)
+  cache_model.py  prefix lookup (cache.c:712-745) and a deterministic LRU
+                  record-pool model
+"""

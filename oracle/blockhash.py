@@ -1,0 +1,82 @@
+"""ORACLE -- test infrastructure only.  Restatement of vLLM's default prefix
+block hash, the key CrossCache stores records under:
+
+  vllm/v1/core/kv_cache_utils.py:541-570  hash_block_tokens:
+      h_i = hash_fn((parent or NONE_HASH, tuple(block tokens), extra_keys))
+  vllm/utils/hashing.py:26-41  sha256: SHA-256 of pickle.dumps(obj, protocol=5)
+  vllm/v1/core/kv_cache_utils.py:97-112  init_none_hash:
+      NONE_HASH = hash_fn(PYTHONHASHSEED string)
+  CrossCache python/adaptor.py:32-40  striding_block_hashes: chunk keys are
+      the hashes of blocks bpc-1, 2*bpc-1, ...
+
+The pickle byte stream is written out here opcode by opcode (CPython
+_pickle.c: PROTO, FRAME, SHORT_BINBYTES, MEMOIZE, MARK, BININT1/BININT2/
+BININT, TUPLE or TUPLE1..3, NONE, TUPLE3, STOP) instead of calling pickle, so
+that this file states the exact bytes the device kernel must produce; tests
+check it against pickle and against golden vectors produced by vLLM itself.
+"""
+from __future__ import annotations
+
+import hashlib
+import struct
+from typing import Iterable, Sequence
+
+PROTO, FRAME, SHORT_BINBYTES, MEMOIZE, MARK = 0x80, 0x95, 0x43, 0x94, 0x28
+BININT1, BININT2, BININT, TUPLE, NONE, TUPLE3, STOP = 0x4B, 0x4D, 0x4A, 0x74, 0x4E, 0x87, 0x2E
+TUPLE_N = {1: 0x85, 2: 0x86, 3: 0x87}
+
+
+def _int_op(v: int) -> bytes:
+    if 0 <= v <= 0xFF:
+        return bytes([BININT1, v])
+    if 0 <= v <= 0xFFFF:
+        return bytes([BININT2]) + struct.pack("<H", v)
+    if -0x80000000 <= v <= 0x7FFFFFFF:
+        return bytes([BININT]) + struct.pack("<i", v)
+    raise ValueError("token id outside int32")
+
+
+def pickle_block(parent: bytes, tokens: Sequence[int]) -> bytes:
+    """pickle.dumps((parent, tuple(tokens), None), protocol=5) for a 32-byte
+    parent and 1 <= len(tokens) <= 8192 (a single pickle frame)."""
+    if len(parent) != 32 or not 1 <= len(tokens) <= 8192:
+        raise ValueError("unsupported block")
+    body = bytearray([SHORT_BINBYTES, 32]) + parent + bytes([MEMOIZE])
+    n = len(tokens)
+    if n > 3:
+        body.append(MARK)
+    for v in tokens:
+        body += _int_op(int(v))
+    body.append(TUPLE if n > 3 else TUPLE_N[n])
+    body += bytes([MEMOIZE, NONE, TUPLE3, MEMOIZE, STOP])
+    return bytes([PROTO, 5, FRAME]) + struct.pack("<Q", len(body)) + bytes(body)
+
+
+def none_hash(seed: str) -> bytes:
+    """NONE_HASH for PYTHONHASHSEED=seed: sha256(pickle.dumps(seed, 5))."""
+    b = seed.encode()
+    if len(b) >= 256:
+        raise ValueError("seed too long for this restatement")
+    # PROTO 5, FRAME, SHORT_BINUNICODE len data, MEMOIZE, STOP
+    body = bytes([0x8C, len(b)]) + b + bytes([MEMOIZE, STOP])
+    msg = bytes([PROTO, 5, FRAME]) + struct.pack("<Q", len(body)) + body
+    return hashlib.sha256(msg).digest()
+
+
+def block_hashes(tokens: Sequence[int], block_size: int, parent: bytes) -> list[bytes]:
+    """Chained hashes of the full blocks of `tokens` starting from `parent`."""
+    out = []
+    h = parent
+    for i in range(len(tokens) // block_size):
+        h = hashlib.sha256(pickle_block(h, tokens[i * block_size:(i + 1) * block_size])).digest()
+        out.append(h)
+    return out
+
+
+def chunk_keys(hashes: Sequence[bytes], blocks_in_chunk: int) -> list[bytes]:
+    """python/adaptor.py:32-40 striding_block_hashes."""
+    return list(hashes[blocks_in_chunk - 1::blocks_in_chunk])
+
+
+def batch_block_hashes(requests: Iterable[Sequence[int]], block_size: int, parent: bytes) -> list[list[bytes]]:
+    return [block_hashes(t, block_size, parent) for t in requests]

@@ -1,0 +1,94 @@
+"""Seeded input generators shared by make_golden.py and the tests.
+
+Every paged layer and record is a deterministic function of a seed (numpy
+PCG64), so fixtures store only seeds, shapes and SHA-256 digests of outputs.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+
+# cases pinned by make_golden.py (names are stable fixture keys)
+KV_CASES = [
+    # CrossCache tests/test_copy.cpp:95-105 defaults: 40 blocks of 2 tokens,
+    # 4-token chunks, 2 layers, hidden 4096, 2-byte elements, K and V
+    dict(name="test_copy_defaults", num_blocks=40, block_size=2, chunk_size=4, num_layers=2,
+         hidden=4096, elt=2, kv=2, chunks=1, seed=11),
+    # Llama-3-8B GQA shapes scaled down: 8 KV heads x 128, bf16, block 16, chunk 256
+    dict(name="gqa_bs16", num_blocks=64, block_size=16, chunk_size=256, num_layers=4,
+         hidden=1024, elt=2, kv=2, chunks=3, seed=12),
+    # DeepSeek-V2-Lite MLA latent (K only), width 576, bf16, block 64
+    dict(name="mla_bs64", num_blocks=32, block_size=64, chunk_size=256, num_layers=3,
+         hidden=576, elt=2, kv=1, chunks=2, seed=13),
+    # unit of 6 bytes (not a multiple of 4): exercises the narrow-vector path
+    dict(name="odd_unit", num_blocks=16, block_size=4, chunk_size=8, num_layers=2,
+         hidden=3, elt=2, kv=2, chunks=3, seed=14),
+    # TP=8 head shard of Llama-3: one head x 128 x bf16 = 256-byte unit
+    dict(name="tp8_shard", num_blocks=128, block_size=16, chunk_size=256, num_layers=5,
+         hidden=128, elt=2, kv=2, chunks=4, seed=15),
+]
+
+
+def unit_of(case: dict) -> int:
+    return case["hidden"] * case["elt"]
+
+
+def record_bytes(case: dict) -> int:
+    return case["kv"] * case["num_layers"] * case["chunk_size"] * unit_of(case)
+
+
+def paged_layers(case: dict, seed: int | None = None, zero: bool = False):
+    """(k_layers, v_layers or None): per-layer uint8 arrays of
+    num_blocks * block_size * unit bytes, K layers first then V layers."""
+    n = case["num_blocks"] * case["block_size"] * unit_of(case)
+    rng = np.random.default_rng(case["seed"] if seed is None else seed)
+    layers = []
+    for _ in range(case["kv"] * case["num_layers"]):
+        layers.append(np.zeros(n, np.uint8) if zero else rng.integers(0, 256, n, dtype=np.uint8))
+    L = case["num_layers"]
+    return layers[:L], (layers[L:] if case["kv"] == 2 else None)
+
+
+def block_ids(case: dict, seed_offset: int = 0) -> np.ndarray:
+    """distinct block ids for case['chunks'] chunks, a seeded permutation"""
+    bpc = case["chunk_size"] // case["block_size"]
+    rng = np.random.default_rng(case["seed"] * 1000 + 7 + seed_offset)
+    return rng.permutation(case["num_blocks"])[: bpc * case["chunks"]].astype(np.uint64)
+
+
+def records_for_scatter(case: dict) -> list[np.ndarray]:
+    rng = np.random.default_rng(case["seed"] * 1000 + 99)
+    return [rng.integers(0, 256, record_bytes(case), dtype=np.uint8) for _ in range(case["chunks"])]
+
+
+def sha(a) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+# block-hash cases: (name, block_size, seed string, token generator spec)
+HASH_CASES = [
+    ("bs16_small_ids", 16, "0", (0, 256, 5 * 16 + 7)),
+    ("bs16_mid_ids", 16, "0", (0, 65536, 6 * 16)),
+    ("bs16_llama3_vocab", 16, "0", (0, 128256, 8 * 16 + 3)),
+    ("bs16_boundaries", 16, "1234", "boundaries"),
+    ("bs64_llama3_vocab", 64, "0", (0, 128256, 4 * 64)),
+    ("bs1", 1, "0", (0, 128256, 9)),
+    ("bs2", 2, "7", (0, 70000, 10)),
+    ("bs3", 3, "7", (0, 70000, 12)),
+    ("bs4", 4, "7", (0, 70000, 16)),
+    ("bs16_int32_extremes", 16, "42", "extremes"),
+    ("bs128_mixed", 128, "3", (0, 300000, 3 * 128)),
+]
+
+
+def hash_tokens(spec, case_index: int) -> list[int]:
+    rng = np.random.default_rng(5000 + case_index)
+    if spec == "boundaries":
+        base = [0, 1, 254, 255, 256, 257, 65534, 65535, 65536, 65537, 128255, 127, 128, 300, 70000, 5]
+        return base * 4
+    if spec == "extremes":
+        return [-2**31, -1, 2**31 - 1, 0, -256, 256, -65536, 65536,
+                -2, 2, 2**31 - 2, -(2**31) + 1, 255, -255, 65535, -65535] * 2
+    lo, hi, n = spec
+    return rng.integers(lo, hi, n).astype(np.int64).tolist()
