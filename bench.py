@@ -255,6 +255,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=L, help="smaller cases for ncu captures only")
+    ap.add_argument("--requests", type=int, default=REQS)
+    ap.add_argument("--blocks-per-layer", type=int, default=NUM_BLOCKS)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
@@ -297,29 +300,37 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
+    n_layers, n_req, n_blocks = args.layers, args.requests, args.blocks_per_layer
     heads = KV_HEADS // world
     hidden = heads * HEAD_DIM
     unit = hidden * ELT
     bpc = CHUNK // BS
-    nblk = REQS * TOKENS // BS                 # 8192 blocks
+    nblk = n_req * TOKENS // BS                # 8192 blocks
     nrec = nblk // bpc                         # 512 records
-    rec_bytes = 2 * L * CHUNK * unit
+    rec_bytes = 2 * n_layers * CHUNK * unit
     payload = nrec * rec_bytes                 # one direction, this rank
 
     # paged cache: this rank's head shard of N(0,1) bf16 values (seed 0)
     g = torch.Generator(device=dev).manual_seed(0)
     layers = []
-    for _ in range(L):
-        full = torch.randn(2, NUM_BLOCKS, BS, KV_HEADS, HEAD_DIM, generator=g, device=dev,
+    for _ in range(n_layers):
+        full = torch.randn(2, n_blocks, BS, KV_HEADS, HEAD_DIM, generator=g, device=dev,
                            dtype=torch.float32).to(torch.bfloat16)
         layers.append(full[:, :, :, rank * heads:(rank + 1) * heads].contiguous())
         del full
     torch.cuda.empty_cache()
     layout, kp, vp = cc.layout_from_kv_tensors(layers)
-    # block tables: seeded permutations of free block ids (save: seed 2, reload: seed 3)
-    bt_save = torch.randperm(NUM_BLOCKS, generator=torch.Generator().manual_seed(2))[:nblk].numpy().astype(np.uint64)
-    bt_load = torch.randperm(NUM_BLOCKS, generator=torch.Generator().manual_seed(3))[:nblk].numpy().astype(np.uint64)
-    tokens = torch.randint(0, VOCAB, (REQS, TOKENS), generator=torch.Generator().manual_seed(1),
+    # block tables: a seeded permutation of free block ids for the save (seed 2);
+    # the reload goes to a fresh seeded permutation (seed 3) of the blocks the
+    # save did not use, so repeated steps never overwrite a block a later
+    # gather reads and the final bytes can be compared exactly
+    if 2 * nblk > n_blocks:
+        raise SystemExit("blocks per layer must hold the save and the reload tables")
+    perm = torch.randperm(n_blocks, generator=torch.Generator().manual_seed(2))
+    bt_save = perm[:nblk].numpy().astype(np.uint64)
+    free = perm[nblk:]
+    bt_load = free[torch.randperm(free.numel(), generator=torch.Generator().manual_seed(3))][:nblk].numpy().astype(np.uint64)
+    tokens = torch.randint(0, VOCAB, (n_req, TOKENS), generator=torch.Generator().manual_seed(1),
                            dtype=torch.int64).to(torch.int32).numpy()
 
     # ---------------- value: device-resident records, kernel path ----------
@@ -334,8 +345,8 @@ def main() -> None:
     def desc(bids, direction):
         return KvCopyDesc(layer_k=kp_d.data_ptr(), layer_v=vp_d.data_ptr(), records=rec_ptrs.data_ptr(),
                           slots=None, block_ids=bids.data_ptr(), error=err.data_ptr(),
-                          page_buffer_size=NUM_BLOCKS * BS, unit_bytes=unit, num_tokens=CHUNK,
-                          block_size=BS, num_layers=L, num_records=nrec, direction=direction)
+                          page_buffer_size=n_blocks * BS, unit_bytes=unit, num_tokens=CHUNK,
+                          block_size=BS, num_layers=n_layers, num_records=nrec, direction=direction)
 
     d_gather, d_scatter = desc(b_save, 1), desc(b_load, 0)
     assert lib.kv_copy_payload_bytes(C.byref(d_gather)) == payload
@@ -359,7 +370,8 @@ def main() -> None:
     l0 = lib.crosscache_kernel_launches()
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
+    clocks = ClockSampler(local).__enter__()
+    if True:
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
@@ -409,20 +421,21 @@ def main() -> None:
         w = cc.Worker("llama-3-8b", layout, kp, vp, node_id=local, world_size=world, rank=rank)
         w.register()
         from demo_b200._lib import lib as L_
+        from demo_b200.tp import agree_min_hits
         flat_tok = np.ascontiguousarray(tokens.reshape(-1))
-        tok_lens = np.full(REQS, TOKENS, dtype=np.int64)
+        tok_lens = np.full(n_req, TOKENS, dtype=np.int64)
         none_hash = __import__("hashlib").sha256(__import__("pickle").dumps("0", protocol=5)).digest()
         hashes = np.zeros((nblk, 32), dtype=np.uint8)
-        key_nums = np.full(REQS, TOKENS // CHUNK, dtype=np.uint32)
-        hits = np.zeros(REQS, dtype=np.uint32)
+        key_nums = np.full(n_req, TOKENS // CHUNK, dtype=np.uint32)
+        hits = np.zeros(n_req, dtype=np.uint32)
         bt_save_c = np.ascontiguousarray(bt_save)
         per_req_blocks = TOKENS // BS
-        load_bids = [np.ascontiguousarray(bt_load[r * per_req_blocks:(r + 1) * per_req_blocks]) for r in range(REQS)]
+        load_bids = [np.ascontiguousarray(bt_load[r * per_req_blocks:(r + 1) * per_req_blocks]) for r in range(n_req)]
 
         def e2e_step(lat: list | None):
             t_a = time.perf_counter()
             w.clear()
-            n = L_.kv_block_hash_host(local, flat_tok.ctypes.data, tok_lens.ctypes.data, REQS, BS, none_hash,
+            n = L_.kv_block_hash_host(local, flat_tok.ctypes.data, tok_lens.ctypes.data, n_req, BS, none_hash,
                                       hashes.ctypes.data)
             assert n == nblk
             keys = np.ascontiguousarray(hashes[bpc - 1::bpc])              # 512 chunk keys
@@ -431,15 +444,11 @@ def main() -> None:
             ret = L_.cache_store(C.byref(w.ctx), kb, 32, bt_save_c.ctypes.data, nblk)
             assert ret == 0, ret
             t_c = time.perf_counter()
-            ret = L_.cache_lookup_batch(C.byref(w.ctx), kb, key_nums.ctypes.data, REQS, 32, hits.ctypes.data)
+            ret = L_.cache_lookup_batch(C.byref(w.ctx), kb, key_nums.ctypes.data, n_req, 32, hits.ctypes.data)
             assert ret == 0
-            hit = hits
-            if world > 1:
-                ht = torch.from_numpy(hits.astype(np.int32)).to(dev)
-                dist.all_reduce(ht, op=dist.ReduceOp.MIN)
-                hit = ht.cpu().numpy()
+            hit = agree_min_hits(hits, device=dev)       # NCCL all-reduce(min) under TP
             per_req_keys = TOKENS // CHUNK
-            for r in range(REQS):
+            for r in range(n_req):
                 h = int(hit[r])
                 ts = time.perf_counter()
                 kr = kb[r * per_req_keys * 32:(r * per_req_keys + h) * 32]
@@ -454,7 +463,6 @@ def main() -> None:
             t[:, b_load] = 0
         for _ in range(args.warmup):
             e2e_step(None)
-        ok_e2e = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers)
         lat: list[float] = []
         parts = []
         l1 = lib.crosscache_kernel_launches()
@@ -467,6 +475,7 @@ def main() -> None:
         te = max_over_ranks(time.perf_counter() - ts0)
         barrier()
         e2e_launches = lib.crosscache_kernel_launches() - l1
+        ok_e2e = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers)
         st = w.stats()
         w.unregister()
         cc.exit()
@@ -484,13 +493,14 @@ def main() -> None:
                "load_gbs_per_gpu": round(payload / load_s / GB, 3),
                "hash_ms": round(hash_s * 1e3, 3), "p50_load_latency_ms": round(p50, 3),
                "p90_load_latency_ms": round(float(np.percentile(lat, 90)) * 1e3, 3),
-               "hit_blocks_per_request": hit_blocks // REQS, "gpu_launches": int(e2e_launches),
+               "hit_blocks_per_request": hit_blocks // n_req, "gpu_launches": int(e2e_launches),
                "verified_bytes": bool(ok_e2e), "evictions": st["evictions"]}
         link = {"d2h_peak_gbs": round(link_peak["d2h"], 2), "h2d_peak_gbs": round(link_peak["h2d"], 2),
                 "save_frac": round(payload / save_s / GB / link_peak["d2h"], 4),
                 "load_frac": round(payload / load_s / GB / link_peak["h2d"], 4),
                 "note": "per GPU; pinned 256 MiB cudaMemcpyAsync measured in this run"}
 
+    clocks.__exit__(None, None, None)
     cpu = None
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         cpu = cpu_sample_run("port", args.cpu_seconds, None, os.cpu_count() or 1)
@@ -502,7 +512,10 @@ def main() -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic (seeded N(0,1) bf16 KV, uniform token ids, random block tables)",
-            "config": workload_config(world),
+            "config": workload_config(world) if (n_layers, n_req, n_blocks) == (L, REQS, NUM_BLOCKS) else
+            {**workload_config(world), "workload": f"reduced case for profiling: {n_layers} layers, {n_req} requests, "
+                                                    f"{n_blocks} blocks/layer", "layers": n_layers,
+             "requests": n_req, "blocks_per_layer": n_blocks},
             "roofline": {"bound": "hbm", "kernel": "kv_copy gather (save)", "achieved": round(achieved, 1),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "peak_kind": peak_kind, "traffic": ncu_traffic(),

@@ -1,0 +1,215 @@
+"""SchedulerAdapter / WorkerAdapter with the interface of CrossCache's
+python/adaptor.py:43-291, running the cache manager in-process.
+
+The reference adapters serialise every call into ZeroMQ messages for the C
+server (register / lookup / store / load, python/utils/protocol.py) and wait
+on futures.  Here the same calls go straight to the C API of
+libcrosscache.so: lookups answer immediately, stores and loads run on a
+worker thread so that wait_for_save / start_load_kv return at once and
+get_finished reports completion, exactly as the reference's futures do.
+"""
+from __future__ import annotations
+
+import threading
+from concurrent.futures import Future, ThreadPoolExecutor
+from dataclasses import dataclass
+from itertools import islice
+from typing import Iterable
+
+import numpy as np
+import torch
+
+from . import cache as cc
+from .tp import agree_min_hits
+
+CHUNK_SIZE = 256          # tokens per record (python/adaptor.py:74,133)
+
+_service_lock = threading.Lock()
+_service_refs = 0
+
+
+def ensure_cache(pool_size: int, chunk_size: int = CHUNK_SIZE) -> None:
+    """Process-wide cache_init on first use (the reference's server does
+    cache_init once at start-up, src/main.c:388-413)."""
+    global _service_refs
+    with _service_lock:
+        if _service_refs == 0:
+            cc.init(chunk_size, pool_size, None)
+        _service_refs += 1
+
+
+def release_cache() -> None:
+    global _service_refs
+    with _service_lock:
+        _service_refs -= 1
+        if _service_refs == 0:
+            cc.exit()
+
+
+def striding_block_hashes(block_hashes: list[bytes], blocks_in_chunk: int) -> Iterable[bytes]:
+    """Hashes of blocks blocks_in_chunk-1, 2*blocks_in_chunk-1, ...
+    (python/adaptor.py:32-40): one key per 256-token record."""
+    return islice(block_hashes, blocks_in_chunk - 1, None, blocks_in_chunk)
+
+
+@dataclass
+class LoadStoreOp:
+    block_hashes: list[bytes]
+    block_ids: list[int]
+
+    def __len__(self) -> int:
+        return len(self.block_hashes)
+
+    def __post_init__(self):
+        assert len(self.block_hashes) == len(self.block_ids), (
+            "The number of block hashes should be equal to the number of block ids "
+            f"But got {len(self.block_hashes)} and {len(self.block_ids)}")
+
+
+class SchedulerAdapter:
+    """python/adaptor.py:58-114.  try_lookup / check_lookup_result give the
+    number of cached tokens of a request's prefix (hit records x 256)."""
+
+    def __init__(self, model_name: str, world_size: int, kv_rank: int, vllm_block_size: int,
+                 lookup_worker: "cc.Worker | None" = None):
+        self.model_name = model_name
+        self.world_size = world_size
+        self.worker_id = kv_rank
+        self.chunk_size = CHUNK_SIZE
+        self.blocks_in_chunk = self.chunk_size // vllm_block_size
+        self.lookup_results: dict[str, int] = {}
+        self._worker = lookup_worker
+
+    def bind_worker(self, worker: "cc.Worker") -> None:
+        self._worker = worker
+
+    def try_lookup(self, request_id: str, block_hashes: list[bytes]) -> None:
+        if request_id in self.lookup_results:
+            return
+        keys = list(striding_block_hashes(block_hashes, self.blocks_in_chunk))
+        if self._worker is None or not keys:
+            self.lookup_results[request_id] = 0
+            return
+        hit_bytes = self._worker.lookup(keys)
+        # src/main.c:140: (hit bytes / key_len) * chunk_size tokens
+        self.lookup_results[request_id] = (hit_bytes // cc.KEY_LEN) * self.chunk_size
+
+    def check_lookup_result(self, request_id: str) -> int | None:
+        assert request_id in self.lookup_results, (
+            f"Lookup request for request_id={request_id} has not been submitted")
+        return self.lookup_results[request_id]
+
+    def cleanup_lookup_result(self, request_id: str) -> None:
+        self.lookup_results.pop(request_id, None)
+
+    def num_blocks_per_chunk(self) -> int:
+        return self.blocks_in_chunk
+
+
+class WorkerAdapter:
+    """python/adaptor.py:117-291 with the same store/load/get_finished
+    bookkeeping; the transfers run in this process on a worker thread."""
+
+    def __init__(self, model_name: str, world_size: int, kv_rank: int, vllm_block_size: int,
+                 pool_size: int = 4 << 30, device: int | None = None, tp_group=None):
+        self.model_name = model_name
+        self.world_size = world_size
+        self.worker_id = kv_rank
+        self.chunk_size = CHUNK_SIZE
+        self.blocks_in_chunk = self.chunk_size // vllm_block_size
+        self.pool_size = pool_size
+        self.device = torch.cuda.current_device() if device is None else device
+        self.tp_group = tp_group
+        self.worker: cc.Worker | None = None
+        self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="CrossCacheXfer")
+        self.store_futures: dict[str, tuple[Future, list[str]]] = {}
+        self.load_futures: dict[str, tuple[Future, list[str]]] = {}
+        self.finished_stores: set[str] = set()
+        self.previously_finished: set[str] = set()
+
+    def _block_hashes_to_keys(self, block_hashes: list[bytes]) -> list[bytes]:
+        return list(striding_block_hashes(block_hashes, self.blocks_in_chunk))
+
+    def register(self, kv_caches: dict[str, torch.Tensor]) -> None:
+        layout, kp, vp = cc.layout_from_kv_tensors(kv_caches.values())
+        ensure_cache(self.pool_size)
+        self.worker = cc.Worker(self.model_name, layout, kp, vp, node_id=self.device,
+                                world_size=self.world_size, rank=self.worker_id)
+        self.worker.register()
+
+    def unregister(self) -> None:
+        self._pool.shutdown(wait=True)
+        if self.worker is not None:
+            self.worker.unregister()
+            self.worker = None
+            release_cache()
+
+    def _submit(self, fn, *args) -> Future:
+        # the transfer must see every KV write queued on the compute stream
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+
+        def run():
+            ev.synchronize()
+            return fn(*args)
+        return self._pool.submit(run)
+
+    def store_requests(self, request_ids: list[str], ops: list[LoadStoreOp]) -> None:
+        keys, block_ids = [], []
+        for op in ops:
+            keys.extend(self._block_hashes_to_keys(op.block_hashes))
+            block_ids.extend(op.block_ids)
+        fut = self._submit(self.worker.store, keys, block_ids)
+        self.store_futures[request_ids[0]] = (fut, request_ids[1:])
+
+    def load_requests(self, request_ids: list[str], ops: list[LoadStoreOp]) -> None:
+        keys, block_ids = [], []
+        for op in ops:
+            keys.extend(self._block_hashes_to_keys(op.block_hashes))
+            block_ids.extend(op.block_ids)
+        fut = self._submit(self.worker.load, keys, block_ids)
+        self.load_futures[request_ids[0]] = (fut, request_ids[1:])
+
+    def lookup_agreed(self, keys_per_request: list[list[bytes]]) -> np.ndarray:
+        """Per-request hit keys on this rank, min-reduced over the TP group."""
+        hits = self.worker.lookup_batch(keys_per_request)
+        return agree_min_hits(hits, self.tp_group)
+
+    def _update_and_get_finished_store(self) -> set[str]:
+        safe = self.finished_stores.intersection(self.previously_finished)
+        self.finished_stores.difference_update(self.previously_finished)
+        self.previously_finished.difference_update(safe)
+        return safe
+
+    def get_finished(self, finished_req_ids: set[str]) -> tuple[set[str] | None, set[str] | None]:
+        finished_stores: set[str] = set()
+        finished_loads: set[str] = set()
+        for rid, (fut, others) in list(self.store_futures.items()):
+            if fut.done():
+                finished_stores.add(rid)
+                finished_stores.update(others)
+        for rid, (fut, others) in list(self.load_futures.items()):
+            if fut.done():
+                finished_loads.add(rid)
+                finished_loads.update(others)
+        for rid in finished_stores:
+            self.store_futures.pop(rid, None)
+        for rid in finished_loads:
+            self.load_futures.pop(rid, None)
+        self.finished_stores.update(finished_stores)
+        ret_stores = set()
+        for rid in finished_req_ids:
+            if rid in self.finished_stores or rid in self.store_futures:
+                self.previously_finished.add(rid)
+            else:
+                ret_stores.add(rid)
+        ret_stores.update(self._update_and_get_finished_store())
+        return ret_stores.intersection(finished_req_ids), finished_loads
+
+    def wait_all(self, timeout: float | None = None) -> list[int]:
+        """Block until every submitted store/load finished; their return codes."""
+        out = []
+        for d in (self.store_futures, self.load_futures):
+            for fut, _ in d.values():
+                out.append(fut.result(timeout=timeout))
+        return out
