@@ -42,6 +42,7 @@ extern "C" {
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <string>
 #include <memory>
 #include <mutex>
 #include <new>
@@ -240,8 +241,16 @@ struct DeviceCtx {
 
 struct IpcSet {
     int dev;
-    std::vector<void *> opened;       /* cudaIpcOpenMemHandle bases */
+    std::vector<std::string> opened;  /* handles this set holds a reference on */
     std::vector<uint64_t> host_ptrs;  /* layer bases (host mirror) */
+};
+
+/* one mapping per (device, handle): PyTorch sub-allocates several layer
+ * tensors from one cudaMalloc block, so several keys can name the same
+ * handle; it is opened once and reference counted */
+struct IpcMapping {
+    void *base;
+    int refs;
 };
 
 struct PinnedRegion {
@@ -272,8 +281,7 @@ public:
             drain(kv.second.get());
         for (auto &kv : ipc_) {
             cudaSetDevice(kv.second.dev);
-            for (void *p : kv.second.opened)
-                cudaIpcCloseMemHandle(p);
+            release_handles_locked(kv.second);
             cudaFree(kv.first);
         }
         for (auto &kv : pinned_) {
@@ -356,6 +364,7 @@ public:
         IpcSet set;
         set.dev = nid;
         const uint8_t *p = static_cast<const uint8_t *>(data);
+        std::unique_lock<std::mutex> lk(reg_mu_);
         for (uint16_t i = 0; i < num; i++, p += per_len) {
             uint64_t ptr = 0;
             if (per_len == 8) {
@@ -366,13 +375,21 @@ public:
                 memcpy(&h, p, sizeof(h));
                 if (per_len > sizeof(h))
                     memcpy(&off, p + sizeof(h), 8);
+                std::string key(reinterpret_cast<const char *>(p), sizeof(h));
+                key.push_back((char)nid);
+                auto it = ipc_maps_.find(key);
                 void *base = nullptr;
-                if (!CU_OK(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess))) {
-                    for (void *o : set.opened)
-                        cudaIpcCloseMemHandle(o);
-                    return nullptr;
+                if (it != ipc_maps_.end()) {
+                    it->second.refs++;
+                    base = it->second.base;
+                } else {
+                    if (!CU_OK(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess))) {
+                        release_handles_locked(set);
+                        return nullptr;
+                    }
+                    ipc_maps_[key] = IpcMapping{base, 1};
                 }
-                set.opened.push_back(base);
+                set.opened.push_back(key);
                 ptr = (uint64_t)(uintptr_t)base + off;
             }
             set.host_ptrs.push_back(ptr);
@@ -382,29 +399,22 @@ public:
             !CU_OK(cudaMemcpy(d, set.host_ptrs.data(), (size_t)num * 8, cudaMemcpyHostToDevice))) {
             if (d)
                 cudaFree(d);
-            for (void *o : set.opened)
-                cudaIpcCloseMemHandle(o);
+            release_handles_locked(set);
             return nullptr;
         }
-        std::lock_guard<std::mutex> g(reg_mu_);
         ipc_[d] = std::move(set);
         return d;
     }
 
     void CloseIPCKeys(void *daddr) override
     {
-        IpcSet set;
-        {
-            std::lock_guard<std::mutex> g(reg_mu_);
-            auto it = ipc_.find(daddr);
-            if (it == ipc_.end())
-                return;
-            set = std::move(it->second);
-            ipc_.erase(it);
-        }
-        cudaSetDevice(set.dev);
-        for (void *o : set.opened)
-            cudaIpcCloseMemHandle(o);
+        std::lock_guard<std::mutex> g(reg_mu_);
+        auto it = ipc_.find(daddr);
+        if (it == ipc_.end())
+            return;
+        cudaSetDevice(it->second.dev);
+        release_handles_locked(it->second);
+        ipc_.erase(it);
         cudaFree(daddr);
     }
 
@@ -497,6 +507,20 @@ private:
         return std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms_);
     }
 
+    void release_handles_locked(IpcSet &set)
+    {
+        for (const std::string &key : set.opened) {
+            auto it = ipc_maps_.find(key);
+            if (it == ipc_maps_.end())
+                continue;
+            if (--it->second.refs == 0) {
+                cudaIpcCloseMemHandle(it->second.base);
+                ipc_maps_.erase(it);
+            }
+        }
+        set.opened.clear();
+    }
+
     int run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch *b);
     int finish(Lane *l, cudaStream_t last, int ret);
 
@@ -507,6 +531,7 @@ private:
     std::mutex reg_mu_;
     std::map<int, std::unique_ptr<DeviceCtx>> devs_;
     std::map<void *, IpcSet> ipc_;
+    std::map<std::string, IpcMapping> ipc_maps_;
     std::map<void *, PinnedRegion> pinned_;
 };
 
