@@ -151,6 +151,9 @@ SIGNATURES: dict[str, tuple] = {
     # include/kvcopy.h
     "kv_copy_launch": (C.c_int, [C.POINTER(KvCopyDesc), C.c_void_p]),
     "kv_copy_payload_bytes": (C.c_uint64, [C.POINTER(KvCopyDesc)]),
+    "kv_copy_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32,
+                                  C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int32,
+                                  C.c_void_p]),
     # include/kvhash.h
     "kv_block_hash_launch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p]),

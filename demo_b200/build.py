@@ -38,6 +38,7 @@ CU_SOURCES = [
     "device/kv_copy.cu",
     "device/cuda_adaptor.cu",
     "device/block_hash.cu",
+    "device/kv_copy_noalloc.cu",
 ]
 HEADERS = sorted(str(p) for p in list(INCLUDE.glob("*.h")) + list(CSRC.rglob("*.h")))
 

@@ -58,6 +58,38 @@ int kv_copy_launch(const struct kv_copy_desc *desc, void *stream);
  * * num_records (each byte is read once and written once). */
 uint64_t kv_copy_payload_bytes(const struct kv_copy_desc *desc);
 
+/* ---- no-allocation variant -------------------------------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory -- an engine that has handed all free HBM to its paged KV cache and
+ * caching allocator, or an embedder whose allocator owns every device byte --
+ * this entry point runs the same gather (direction 1) / scatter (0) without
+ * calling cudaMalloc, cudaFree or any allocating library routine.  Its scratch
+ * (layer bases, record addresses, block ids, error word) is one static device
+ * array of about 548 KiB that every GPU loading the library holds until exit;
+ * requests beyond the limits below return -E2BIG.
+ *   layer_k / layer_v  HOST arrays of num_layers layer base addresses
+ *                      (layer_v NULL for a K-only cache)
+ *   records            HOST array of num_records device-accessible record
+ *                      addresses (HBM, or mapped pinned host memory)
+ *   block_ids          HOST array, num_tokens / block_size ids per record
+ * Synchronous on `stream`: returns 0 once the kernel finished, -EINVAL for a
+ * bad argument or a block id outside the paged cache, -E2BIG, -ETIMEDOUT
+ * (deadline CROSSCACHE_TIMEOUT_MS) or -EIO.  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) and must come before
+ * any stream capture.  Every call shares the array, which keeps the last
+ * call's contents (the error word is cleared per call); calls that overlap on
+ * the GPU race -- calls through this entry point in one process are
+ * serialised, but one that returned -ETIMEDOUT may still be running. */
+#define KVCOPY_NOALLOC_MAX_LAYERS  256
+#define KVCOPY_NOALLOC_MAX_RECORDS 4096
+#define KVCOPY_NOALLOC_MAX_BLOCKS  65536
+
+int kv_copy_noalloc(int device, const uint64_t *layer_k, const uint64_t *layer_v,
+                    const uint64_t *records, const uint64_t *block_ids,
+                    uint32_t num_records, uint64_t page_buffer_size, uint32_t unit_bytes,
+                    uint32_t num_tokens, uint32_t block_size, uint32_t num_layers,
+                    int32_t direction, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
