@@ -394,6 +394,30 @@ def main() -> None:
     del records
     torch.cuda.empty_cache()
 
+    # ---------------- block-hash kernel, tokens resident in HBM --------------
+    from demo_b200.hashing import block_hashes_device
+    none_hash_h = __import__("hashlib").sha256(__import__("pickle").dumps("0", protocol=5)).digest()
+    tok_d = torch.from_numpy(tokens.reshape(-1).copy()).to(dev)
+    toff_d = torch.arange(n_req, dtype=torch.int64, device=dev) * TOKENS
+    ooff_d = torch.arange(n_req, dtype=torch.int64, device=dev) * (TOKENS // BS)
+    nb_d = torch.full((n_req,), TOKENS // BS, dtype=torch.int32, device=dev)
+    hout = torch.empty(nblk, 32, dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            block_hashes_device(tok_d, toff_d, nb_d, ooff_d, BS, none_hash_h, hout, stream=stream)
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(stream)
+        for _ in range(args.steps):
+            block_hashes_device(tok_d, toff_d, nb_d, ooff_d, BS, none_hash_h, hout, stream=stream)
+        h1.record(stream)
+    torch.cuda.synchronize()
+    hash_ms = h0.elapsed_time(h1) / args.steps
+    hash_info = {"kernel_ms": round(hash_ms, 4), "blocks": nblk, "chains": n_req,
+                 "blocks_per_s": round(nblk / (hash_ms / 1e3), 1),
+                 "sha256_compressions_per_s": round(3 * nblk / (hash_ms / 1e3), 1),
+                 "us_per_block_along_a_chain": round(hash_ms * 1e3 / (TOKENS // BS), 3),
+                 "bound": "integer latency along each chain (3 SHA-256 compressions per 16-token block)"}
+
     # ---------------- e2e: public C API, pinned host pool -------------------
     e2e = None
     link = None
@@ -523,6 +547,7 @@ def main() -> None:
                          "gather_ms": round(gather_ms, 4), "scatter_ms": round(scatter_ms, 4),
                          "scatter_frac": round(2 * payload / (scatter_ms / 1e3) / GB / hbm_peak, 4)},
             "e2e": e2e, "link": link, "p50_load_latency_ms": round(p50, 3) if p50 is not None else None,
+            "block_hash": hash_info,
             "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": clocks.summary(),
             "verified_bytes": bool(ok_value),
         }

@@ -148,6 +148,7 @@ SIGNATURES: dict[str, tuple] = {
     "transfer_kvcache_batch": (C.c_int, [C.c_void_p, C.POINTER(TransferBatch)]),
     "reset_device": (None, [C.c_void_p, C.c_uint8]),
     "crosscache_kernel_launches": (C.c_uint64, []),
+    "ipc_export_key": (C.c_int, [C.c_void_p, C.c_void_p]),
     # include/kvcopy.h
     "kv_copy_launch": (C.c_int, [C.POINTER(KvCopyDesc), C.c_void_p]),
     "kv_copy_payload_bytes": (C.c_uint64, [C.POINTER(KvCopyDesc)]),

@@ -24,10 +24,12 @@
  *
  * SHA-256 is FIPS 180-4.  One thread follows one request's chain (the chain
  * is serial: block i's first message block holds h_{i-1}); requests run in
- * parallel.  Each thread streams its message bytes into a 64-byte block held
- * in shared memory (word-interleaved across the warp to avoid bank
- * conflicts) and compresses whenever the block fills, so no message buffer
- * of block_size-dependent size is needed.
+ * parallel, one warp per CTA so that chains spread over SMs.  Each thread
+ * streams its message bytes into a 64-byte block held in shared memory
+ * (word-interleaved across the warp to avoid bank conflicts) and compresses
+ * whenever the block fills, so no message buffer of block_size-dependent
+ * size is needed; the SHA state also lives in shared memory so that the
+ * byte counters stay in registers around the out-of-line compression.
  */
 #include "kvhash.h"
 #include "adaptor.h"
@@ -41,7 +43,7 @@
 
 namespace {
 
-constexpr int kHashThreads = 64;
+constexpr int kHashThreads = 32;   /* one warp per CTA: chains spread over SMs */
 
 /* FIPS 180-4 section 4.2.2: first 32 bits of the fractional parts of the cube
  * roots of the first 64 primes */
@@ -55,24 +57,29 @@ __constant__ uint32_t kRound[64] = {
     0x19a4c116, 0x1e376c08, 0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a, 0x5b9cca4f, 0x682e6ff3,
     0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208, 0x90befffa, 0xa4506ceb, 0xbef9a3f7, 0xc67178f2};
 
-/* FIPS 180-4 section 5.3.3: initial hash value */
-__device__ __forceinline__ void sha_init(uint32_t st[8])
+/* FIPS 180-4 section 5.3.3: initial hash value (state column stride kHashThreads) */
+__device__ __forceinline__ void sha_init(uint32_t *st)
 {
-    st[0] = 0x6a09e667; st[1] = 0xbb67ae85; st[2] = 0x3c6ef372; st[3] = 0xa54ff53a;
-    st[4] = 0x510e527f; st[5] = 0x9b05688c; st[6] = 0x1f83d9ab; st[7] = 0x5be0cd19;
+    st[0] = 0x6a09e667; st[kHashThreads] = 0xbb67ae85; st[2 * kHashThreads] = 0x3c6ef372;
+    st[3 * kHashThreads] = 0xa54ff53a; st[4 * kHashThreads] = 0x510e527f;
+    st[5 * kHashThreads] = 0x9b05688c; st[6 * kHashThreads] = 0x1f83d9ab;
+    st[7 * kHashThreads] = 0x5be0cd19;
 }
 
 __device__ __forceinline__ uint32_t rotr(uint32_t x, int n) { return __funnelshift_r(x, x, n); }
 
-/* one compression over the 16 big-endian words at w[k * kHashThreads] */
-__device__ __noinline__ void sha_compress(uint32_t st[8], const uint32_t *w)
+/* one compression: state st[k * kHashThreads] (shared memory), message words
+ * w[k * kHashThreads].  Not inlined: the byte streamer calls it from many
+ * places, and keeping it out of line keeps the kernel small; all of its
+ * operands are in shared memory so the caller's registers stay registers. */
+__device__ __noinline__ void sha_compress(uint32_t *st, const uint32_t *w)
 {
     uint32_t m[16];
 #pragma unroll
     for (int k = 0; k < 16; k++)
         m[k] = w[k * kHashThreads];
-    uint32_t a = st[0], b = st[1], c = st[2], d = st[3];
-    uint32_t e = st[4], f = st[5], g = st[6], h = st[7];
+    uint32_t a = st[0], b = st[kHashThreads], c = st[2 * kHashThreads], d = st[3 * kHashThreads];
+    uint32_t e = st[4 * kHashThreads], f = st[5 * kHashThreads], g = st[6 * kHashThreads], h = st[7 * kHashThreads];
 #pragma unroll
     for (int t = 0; t < 64; t++) {
         uint32_t wt;
@@ -94,22 +101,23 @@ __device__ __noinline__ void sha_compress(uint32_t st[8], const uint32_t *w)
         h = g; g = f; f = e; e = d + t1;
         d = c; c = b; b = a; a = t1 + t2;
     }
-    st[0] += a; st[1] += b; st[2] += c; st[3] += d;
-    st[4] += e; st[5] += f; st[6] += g; st[7] += h;
+    st[0] += a; st[kHashThreads] += b; st[2 * kHashThreads] += c; st[3 * kHashThreads] += d;
+    st[4 * kHashThreads] += e; st[5 * kHashThreads] += f; st[6 * kHashThreads] += g; st[7 * kHashThreads] += h;
 }
 
-/* byte stream -> 64-byte message blocks in shared memory */
+/* byte stream -> 64-byte message blocks in shared memory; the counters are
+ * plain registers (nothing here is address-taken) */
 struct Streamer {
-    uint32_t *w;      /* this thread's column: word k at w[k * kHashThreads] */
+    uint32_t *w;      /* this thread's message column: word k at w[k * kHashThreads] */
+    uint32_t *st;     /* this thread's state column */
     uint32_t acc;     /* bytes not yet forming a full word, big-endian */
     int nacc;         /* bytes in acc (0..3) */
     int wpos;         /* words filled in the current block (0..15) */
-    uint32_t st[8];
 
-    __device__ __forceinline__ void word(uint32_t v, bool flush_block = true)
+    __device__ __forceinline__ void word(uint32_t v)
     {
         w[wpos * kHashThreads] = v;
-        if (++wpos == 16 && flush_block) {
+        if (++wpos == 16) {
             sha_compress(st, w);
             wpos = 0;
         }
@@ -164,6 +172,7 @@ struct HashArgs {
 __global__ void __launch_bounds__(kHashThreads) block_hash_kernel(const HashArgs a)
 {
     __shared__ uint32_t sw[16 * kHashThreads];
+    __shared__ uint32_t sst[8 * kHashThreads];
     const uint32_t r = blockIdx.x * kHashThreads + threadIdx.x;
     if (r >= a.num_req)
         return;
@@ -192,6 +201,7 @@ __global__ void __launch_bounds__(kHashThreads) block_hash_kernel(const HashArgs
 
     Streamer s;
     s.w = sw + threadIdx.x;
+    s.st = sst + threadIdx.x;
     for (int i = 0; i < nblk; i++, tok += bs) {
         uint32_t len = fixed;
         for (uint32_t j = 0; j < bs; j++)
@@ -244,15 +254,19 @@ __global__ void __launch_bounds__(kHashThreads) block_hash_kernel(const HashArgs
         s.byte(0x2e);
         s.finish(len);
 
+        uint32_t dg[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            dg[k] = s.st[k * kHashThreads];
         uint4 lo, hi;
-        lo.x = __byte_perm(s.st[0], 0, 0x0123);
-        lo.y = __byte_perm(s.st[1], 0, 0x0123);
-        lo.z = __byte_perm(s.st[2], 0, 0x0123);
-        lo.w = __byte_perm(s.st[3], 0, 0x0123);
-        hi.x = __byte_perm(s.st[4], 0, 0x0123);
-        hi.y = __byte_perm(s.st[5], 0, 0x0123);
-        hi.z = __byte_perm(s.st[6], 0, 0x0123);
-        hi.w = __byte_perm(s.st[7], 0, 0x0123);
+        lo.x = __byte_perm(dg[0], 0, 0x0123);
+        lo.y = __byte_perm(dg[1], 0, 0x0123);
+        lo.z = __byte_perm(dg[2], 0, 0x0123);
+        lo.w = __byte_perm(dg[3], 0, 0x0123);
+        hi.x = __byte_perm(dg[4], 0, 0x0123);
+        hi.y = __byte_perm(dg[5], 0, 0x0123);
+        hi.z = __byte_perm(dg[6], 0, 0x0123);
+        hi.w = __byte_perm(dg[7], 0, 0x0123);
         uint8_t *o = out + (uint64_t)i * 32;
         if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
             reinterpret_cast<uint4 *>(o)[0] = lo;
@@ -263,7 +277,7 @@ __global__ void __launch_bounds__(kHashThreads) block_hash_kernel(const HashArgs
         }
 #pragma unroll
         for (int k = 0; k < 8; k++)
-            parent[k] = s.st[k];
+            parent[k] = dg[k];
     }
 }
 

@@ -770,3 +770,50 @@ adaptor_t *cuda_adaptor_create(void)
 }
 
 void cuda_adaptor_destroy(adaptor_t *adaptor) { delete adaptor; }
+
+/* 72-byte CUDA IPC key of device memory: the cudaIpcMemHandle_t of the
+ * cudaMalloc allocation containing dptr, then the uint64 byte offset of dptr
+ * inside it (the allocation base comes from the driver's
+ * cuMemGetAddressRange, reached through cudaGetDriverEntryPointByVersion so
+ * that no libcuda link is needed). */
+int ipc_export_key(const void *dptr, uint8_t *key_out)
+{
+    typedef int (*get_range_fn)(unsigned long long *, size_t *, unsigned long long);
+    static get_range_fn get_range = nullptr;
+    static std::once_flag once;
+    if (!dptr || !key_out)
+        return -EINVAL;
+    std::call_once(once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult st;
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 12000, cudaEnableDefault, &st) ==
+                cudaSuccess && st == cudaDriverEntryPointSuccess)
+            get_range = reinterpret_cast<get_range_fn>(fn);
+    });
+    if (!get_range)
+        return -ENOSYS;
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, dptr) != cudaSuccess || attr.type != cudaMemoryTypeDevice)
+        return -EINVAL;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(attr.device) != cudaSuccess)
+        return -EIO;
+    unsigned long long base = 0;
+    size_t size = 0;
+    int ret = 0;
+    cudaIpcMemHandle_t h;
+    if (get_range(&base, &size, (unsigned long long)(uintptr_t)dptr) != 0) {
+        ret = -EINVAL;
+    } else if (cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base)) != cudaSuccess) {
+        log_error("ipc_export_key: cudaIpcGetMemHandle failed (memory not from cudaMalloc?)");
+        ret = -EINVAL;
+    } else {
+        uint64_t off = (uint64_t)(uintptr_t)dptr - base;
+        memcpy(key_out, &h, sizeof(h));
+        memcpy(key_out + sizeof(h), &off, 8);
+    }
+    if (prev >= 0)
+        cudaSetDevice(prev);
+    return ret;
+}

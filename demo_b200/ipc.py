@@ -10,8 +10,6 @@ accepts such keys with per_len 72.
 """
 from __future__ import annotations
 
-import struct
-
 import torch
 
 IPC_HANDLE_BYTES = 64
@@ -19,17 +17,21 @@ KEY_BYTES = IPC_HANDLE_BYTES + 8
 
 
 def ipckey_from_tensor(t: torch.Tensor) -> bytes:
+    """72-byte key of the tensor's first element (include/device.h
+    ipc_export_key): handle of the enclosing cudaMalloc block + byte offset."""
+    import ctypes as C
+
+    from ._lib import lib
+
     if not t.is_cuda:
         raise ValueError("tensor must be on a CUDA device")
     if not t.is_contiguous():
         raise ValueError("tensor must be contiguous")
-    st = t.untyped_storage()
-    info = st._share_cuda_()
-    handle, storage_offset_bytes = info[1], info[3]
-    if len(handle) != IPC_HANDLE_BYTES:
-        raise RuntimeError(f"unexpected IPC handle size {len(handle)}")
-    off = storage_offset_bytes + t.storage_offset() * t.element_size()
-    return bytes(handle) + struct.pack("<Q", off)
+    buf = (C.c_uint8 * KEY_BYTES)()
+    ret = lib.ipc_export_key(C.c_void_p(t.data_ptr()), buf)
+    if ret:
+        raise RuntimeError(f"ipc_export_key failed: {ret}")
+    return bytes(buf)
 
 
 def layer_keys(kv_caches) -> tuple[bytes, bytes | None]:

@@ -108,6 +108,15 @@ struct transfer_batch {
 
 int transfer_kvcache_batch(adaptor_t *adaptor, struct transfer_batch *batch);
 
+/* new: CUDA counterpart of CrossCache's ipckey_from_tensor
+ * (python/ipckey_utils.cpp:19-33, aclrtIpcMemGetExportKey, 64 bytes).
+ * Writes the 72-byte key of device address dptr into key_out: the
+ * cudaIpcMemHandle_t of the cudaMalloc allocation that contains dptr,
+ * followed by the uint64 byte offset of dptr inside that allocation -- the
+ * per_len 72 form open_ipc_keys accepts.  0, -EINVAL (not device memory from
+ * cudaMalloc) or -ENOSYS. */
+int ipc_export_key(const void *dptr, uint8_t *key_out);
+
 /* new: number of device kernels this library has launched since load
  * (every backend; the CPU backend never launches any). */
 uint64_t crosscache_kernel_launches(void);

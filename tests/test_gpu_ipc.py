@@ -15,6 +15,15 @@ NB, BS, H, D, L = 64, 16, 8, 128, 3
 
 
 def _worker(q_keys, q_done, q_res):
+    try:
+        _worker_body(q_keys, q_done, q_res)
+    except Exception as e:            # unblock the server and the test at once
+        q_keys.put(("error", repr(e)))
+        q_res.put(("worker-error", repr(e)))
+        raise
+
+
+def _worker_body(q_keys, q_done, q_res):
     import torch
 
     from demo_b200.ipc import layer_keys
@@ -42,6 +51,10 @@ def _server(q_keys, q_done, q_res):
 
     torch.cuda.set_device(0)
     kk, vk = q_keys.get(timeout=120)
+    if kk == "error":
+        q_done.put(None)
+        q_res.put(("server", 0))
+        return
     cc.init(256, 8 * 2 * L * 256 * H * D * 2, None)
     lay = cc.KVLayout(L, NB, BS, H * D, 2, 2)
     w = cc.Worker("ipc-model", lay, [0] * L, [0] * L)
@@ -71,6 +84,7 @@ def test_cross_process_ipc_registration():
     pw.join(timeout=60)
     ps.join(timeout=60)
     assert pw.exitcode == 0 and ps.exitcode == 0
+    assert not any(r[0] == "worker-error" for r in res), res
     by = {r[0] if r[0] == "server" else "worker": r for r in res}
     assert by["server"][1] > 0
     (r1, r2), ok = by["worker"]
