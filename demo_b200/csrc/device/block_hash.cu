@@ -22,14 +22,14 @@
  * (CPython _pickle.c save_bytes/save_tuple/save_long; a 0..255 token is
  * BININT1, 256..65535 BININT2, anything else BININT 4-byte two's complement.)
  *
- * SHA-256 is FIPS 180-4.  One thread follows one request's chain (the chain
- * is serial: block i's first message block holds h_{i-1}); requests run in
- * parallel, one warp per CTA so that chains spread over SMs.  Each thread
- * streams its message bytes into a 64-byte block held in shared memory
- * (word-interleaved across the warp to avoid bank conflicts) and compresses
- * whenever the block fills, so no message buffer of block_size-dependent
- * size is needed; the SHA state also lives in shared memory so that the
- * byte counters stay in registers around the out-of-line compression.
+ * SHA-256 is FIPS 180-4.  One warp follows one request's chain (the chain is
+ * serial: block i's first message block holds h_{i-1}); requests run in
+ * parallel.  The lanes build each block's pickle bytes in parallel into a
+ * shared-memory ring (token bytes placed by a warp prefix scan of their
+ * 2/3/5-byte widths) and the warp compresses every complete 64-byte block,
+ * so the control flow is uniform: with one thread per chain the lanes of a
+ * warp reach their compressions at different byte counts and the warp
+ * serialises them.
  */
 #include "kvhash.h"
 #include "adaptor.h"
@@ -43,7 +43,8 @@
 
 namespace {
 
-constexpr int kHashThreads = 32;   /* one warp per CTA: chains spread over SMs */
+constexpr int kWarpsPerCta = 4;     /* one warp per request chain */
+constexpr uint32_t kRing = 512;     /* message ring per warp, bytes (multiple of 64) */
 
 /* FIPS 180-4 section 4.2.2: first 32 bits of the fractional parts of the cube
  * roots of the first 64 primes */
@@ -57,29 +58,20 @@ __constant__ uint32_t kRound[64] = {
     0x19a4c116, 0x1e376c08, 0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a, 0x5b9cca4f, 0x682e6ff3,
     0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208, 0x90befffa, 0xa4506ceb, 0xbef9a3f7, 0xc67178f2};
 
-/* FIPS 180-4 section 5.3.3: initial hash value (state column stride kHashThreads) */
-__device__ __forceinline__ void sha_init(uint32_t *st)
-{
-    st[0] = 0x6a09e667; st[kHashThreads] = 0xbb67ae85; st[2 * kHashThreads] = 0x3c6ef372;
-    st[3 * kHashThreads] = 0xa54ff53a; st[4 * kHashThreads] = 0x510e527f;
-    st[5 * kHashThreads] = 0x9b05688c; st[6 * kHashThreads] = 0x1f83d9ab;
-    st[7 * kHashThreads] = 0x5be0cd19;
-}
-
 __device__ __forceinline__ uint32_t rotr(uint32_t x, int n) { return __funnelshift_r(x, x, n); }
+__device__ __forceinline__ uint32_t bswap(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
 
-/* one compression: state st[k * kHashThreads] (shared memory), message words
- * w[k * kHashThreads].  Not inlined: the byte streamer calls it from many
- * places, and keeping it out of line keeps the kernel small; all of its
- * operands are in shared memory so the caller's registers stay registers. */
-__device__ __noinline__ void sha_compress(uint32_t *st, const uint32_t *w)
+/* one compression of the 64 message bytes at `blk` (shared memory, message
+ * byte order); every lane of the warp runs it on the same data */
+__device__ __forceinline__ void sha_compress(uint32_t st[8], const uint8_t *blk)
 {
+    const uint32_t *w32 = reinterpret_cast<const uint32_t *>(blk);
     uint32_t m[16];
 #pragma unroll
     for (int k = 0; k < 16; k++)
-        m[k] = w[k * kHashThreads];
-    uint32_t a = st[0], b = st[kHashThreads], c = st[2 * kHashThreads], d = st[3 * kHashThreads];
-    uint32_t e = st[4 * kHashThreads], f = st[5 * kHashThreads], g = st[6 * kHashThreads], h = st[7 * kHashThreads];
+        m[k] = bswap(w32[k]);
+    uint32_t a = st[0], b = st[1], c = st[2], d = st[3];
+    uint32_t e = st[4], f = st[5], g = st[6], h = st[7];
 #pragma unroll
     for (int t = 0; t < 64; t++) {
         uint32_t wt;
@@ -101,60 +93,22 @@ __device__ __noinline__ void sha_compress(uint32_t *st, const uint32_t *w)
         h = g; g = f; f = e; e = d + t1;
         d = c; c = b; b = a; a = t1 + t2;
     }
-    st[0] += a; st[kHashThreads] += b; st[2 * kHashThreads] += c; st[3 * kHashThreads] += d;
-    st[4 * kHashThreads] += e; st[5 * kHashThreads] += f; st[6 * kHashThreads] += g; st[7 * kHashThreads] += h;
+    st[0] += a; st[1] += b; st[2] += c; st[3] += d;
+    st[4] += e; st[5] += f; st[6] += g; st[7] += h;
 }
 
-/* byte stream -> 64-byte message blocks in shared memory; the counters are
- * plain registers (nothing here is address-taken) */
-struct Streamer {
-    uint32_t *w;      /* this thread's message column: word k at w[k * kHashThreads] */
-    uint32_t *st;     /* this thread's state column */
-    uint32_t acc;     /* bytes not yet forming a full word, big-endian */
-    int nacc;         /* bytes in acc (0..3) */
-    int wpos;         /* words filled in the current block (0..15) */
-
-    __device__ __forceinline__ void word(uint32_t v)
-    {
-        w[wpos * kHashThreads] = v;
-        if (++wpos == 16) {
-            sha_compress(st, w);
-            wpos = 0;
-        }
-    }
-    __device__ __forceinline__ void byte(uint32_t b)
-    {
-        acc = (acc << 8) | (b & 0xff);
-        if (++nacc == 4) {
-            word(acc);
-            acc = 0;
-            nacc = 0;
-        }
-    }
-    /* SHA-256 padding for a message of `len` bytes, final compression */
-    __device__ __forceinline__ void finish(uint64_t len)
-    {
-        byte(0x80);
-        if (nacc) {
-            acc <<= 8 * (4 - nacc);
-            nacc = 0;
-            word(acc);
-            acc = 0;
-        }
-        if (wpos > 14) {
-            while (wpos != 0)
-                word(0);
-        }
-        while (wpos < 14)
-            word(0);
-        word((uint32_t)((len * 8) >> 32));
-        word((uint32_t)(len * 8));
-    }
-};
-
+/* pickle encoding width of a token id: BININT1 (2), BININT2 (3), BININT (5) */
 __device__ __forceinline__ uint32_t token_width(int32_t v)
 {
     return (v >= 0 && v <= 0xff) ? 2u : ((v >= 0 && v <= 0xffff) ? 3u : 5u);
+}
+
+/* byte k (0-based) of the pickle opcode + argument encoding token id v */
+__device__ __forceinline__ uint32_t token_byte(int32_t v, uint32_t k)
+{
+    const uint32_t u = (uint32_t)v;
+    const uint32_t op = (v >= 0 && v <= 0xff) ? 0x4bu : ((v >= 0 && v <= 0xffff) ? 0x4du : 0x4au);
+    return k == 0 ? op : (u >> (8 * (k - 1))) & 0xffu;
 }
 
 struct HashArgs {
@@ -169,115 +123,136 @@ struct HashArgs {
     uint32_t none_hash[8];   /* big-endian words */
 };
 
-__global__ void __launch_bounds__(kHashThreads) block_hash_kernel(const HashArgs a)
+/* Warp w of the grid follows the chain of request w.  Per block the lanes
+ * (1) sum the token widths to get the message length, (2) write the pickle
+ * bytes into a shared-memory ring in parallel -- the header and parent, then
+ * 32 tokens at a time at offsets from a warp prefix scan of their widths,
+ * then the trailer and the SHA-256 padding -- and (3) after every write phase
+ * compress each complete 64-byte block.  Control flow is uniform across the
+ * warp, so every compression runs once per warp. */
+__global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const HashArgs a)
 {
-    __shared__ uint32_t sw[16 * kHashThreads];
-    __shared__ uint32_t sst[8 * kHashThreads];
-    const uint32_t r = blockIdx.x * kHashThreads + threadIdx.x;
+    __shared__ __align__(16) uint8_t ring_all[kWarpsPerCta][kRing];
+    __shared__ __align__(16) uint8_t parent_all[kWarpsPerCta][32];
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t wid = threadIdx.x >> 5;
+    const uint32_t r = blockIdx.x * kWarpsPerCta + wid;
     if (r >= a.num_req)
-        return;
+        return;                       /* whole warp exits together */
+    uint8_t *ring = ring_all[wid];
+    uint8_t *par = parent_all[wid];
 
-    uint32_t parent[8];
     if (a.parents) {
-        const uint8_t *pp = a.parents + (uint64_t)r * 32;
-#pragma unroll
-        for (int k = 0; k < 8; k++)
-            parent[k] = ((uint32_t)pp[4 * k] << 24) | ((uint32_t)pp[4 * k + 1] << 16) |
-                        ((uint32_t)pp[4 * k + 2] << 8) | (uint32_t)pp[4 * k + 3];
+        par[lane] = a.parents[(uint64_t)r * 32 + lane];
     } else {
+        /* constant parameter indices only (a dynamic index would copy the
+         * whole parameter block to local memory) */
 #pragma unroll
         for (int k = 0; k < 8; k++)
-            parent[k] = a.none_hash[k];
+            if (lane == (uint32_t)k)
+                reinterpret_cast<uint32_t *>(par)[k] = bswap(a.none_hash[k]);
     }
+    __syncwarp();
 
     const uint32_t bs = a.block_size;
+    const uint32_t hdr_len = bs > 3 ? 47u : 46u;
+    const uint32_t fixed = hdr_len + 6;          /* + tuple op, MEMOIZE NONE TUPLE3 MEMOIZE STOP */
+    const uint32_t tuple_op = bs > 3 ? 0x74u : (0x84u + bs);
     const int32_t *tok = a.tokens + a.tok_offsets[r];
     uint8_t *out = a.out + (uint64_t)a.out_offsets[r] * 32;
     const int nblk = a.num_blocks[r];
-    /* fixed bytes: PROTO 2, FRAME 9, SHORT_BINBYTES 34, MEMOIZE 1, [MARK 1],
-     * tuple opcode 1, MEMOIZE NONE TUPLE3 MEMOIZE STOP 5 */
-    const uint32_t fixed = 2 + 9 + 34 + 1 + (bs > 3 ? 1 : 0) + 1 + 5;
-    const uint32_t tuple_op = bs > 3 ? 0x74u : (0x84u + bs);
 
-    Streamer s;
-    s.w = sw + threadIdx.x;
-    s.st = sst + threadIdx.x;
     for (int i = 0; i < nblk; i++, tok += bs) {
-        uint32_t len = fixed;
-        for (uint32_t j = 0; j < bs; j++)
-            len += token_width(tok[j]);
+        /* (1) message length */
+        uint32_t wsum = 0;
+        for (uint32_t j = lane; j < bs; j += 32)
+            wsum += token_width(tok[j]);
+        const uint32_t len = fixed + __reduce_add_sync(0xffffffffu, wsum);
+        const uint32_t total = (len + 9 + 63) & ~63u;     /* padded length */
         const uint64_t frame = len - 11;
 
-        sha_init(s.st);
-        s.acc = 0;
-        s.nacc = 0;
-        s.wpos = 0;
-        s.byte(0x80);
-        s.byte(0x05);
-        s.byte(0x95);
-        for (int k = 0; k < 8; k++)
-            s.byte((uint32_t)(frame >> (8 * k)));
-        s.byte(0x43);
-        s.byte(0x20);
-        for (int k = 0; k < 8; k++) {
-            s.byte(parent[k] >> 24);
-            s.byte(parent[k] >> 16);
-            s.byte(parent[k] >> 8);
-            s.byte(parent[k]);
-        }
-        s.byte(0x94);
-        if (bs > 3)
-            s.byte(0x28);
-        for (uint32_t j = 0; j < bs; j++) {
-            const int32_t v = tok[j];
-            const uint32_t u = (uint32_t)v;
-            if (v >= 0 && v <= 0xff) {
-                s.byte(0x4b);
-                s.byte(u);
-            } else if (v >= 0 && v <= 0xffff) {
-                s.byte(0x4d);
-                s.byte(u);
-                s.byte(u >> 8);
-            } else {
-                s.byte(0x4a);
-                s.byte(u);
-                s.byte(u >> 8);
-                s.byte(u >> 16);
-                s.byte(u >> 24);
-            }
-        }
-        s.byte(tuple_op);
-        s.byte(0x94);
-        s.byte(0x4e);
-        s.byte(0x87);
-        s.byte(0x94);
-        s.byte(0x2e);
-        s.finish(len);
+        uint32_t st[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a,
+                          0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
+        uint32_t pos = 0, done = 0;
 
-        uint32_t dg[8];
+        /* phase list: 0 = header, 1..G = token groups, G+1 = tail */
+        const uint32_t groups = (bs + 31) / 32;
+        for (uint32_t ph = 0; ph <= groups + 1; ph++) {
+            if (ph == 0) {
+                for (uint32_t p = lane; p < hdr_len; p += 32) {
+                    uint32_t v;
+                    if (p < 3)
+                        v = p == 0 ? 0x80u : (p == 1 ? 0x05u : 0x95u);
+                    else if (p < 11)
+                        v = (uint32_t)(frame >> (8 * (p - 3))) & 0xffu;
+                    else if (p < 13)
+                        v = p == 11 ? 0x43u : 0x20u;
+                    else if (p < 45)
+                        v = par[p - 13];
+                    else
+                        v = p == 45 ? 0x94u : 0x28u;
+                    ring[p % kRing] = (uint8_t)v;
+                }
+                pos = hdr_len;
+            } else if (ph <= groups) {
+                const uint32_t j = (ph - 1) * 32 + lane;
+                const int32_t v = j < bs ? tok[j] : 0;
+                const uint32_t wdt = j < bs ? token_width(v) : 0u;
+                uint32_t incl = wdt;
 #pragma unroll
-        for (int k = 0; k < 8; k++)
-            dg[k] = s.st[k * kHashThreads];
-        uint4 lo, hi;
-        lo.x = __byte_perm(dg[0], 0, 0x0123);
-        lo.y = __byte_perm(dg[1], 0, 0x0123);
-        lo.z = __byte_perm(dg[2], 0, 0x0123);
-        lo.w = __byte_perm(dg[3], 0, 0x0123);
-        hi.x = __byte_perm(dg[4], 0, 0x0123);
-        hi.y = __byte_perm(dg[5], 0, 0x0123);
-        hi.z = __byte_perm(dg[6], 0, 0x0123);
-        hi.w = __byte_perm(dg[7], 0, 0x0123);
-        uint8_t *o = out + (uint64_t)i * 32;
-        if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-            reinterpret_cast<uint4 *>(o)[0] = lo;
-            reinterpret_cast<uint4 *>(o)[1] = hi;
-        } else {
-            memcpy(o, &lo, 16);
-            memcpy(o + 16, &hi, 16);
+                for (int o = 1; o < 32; o <<= 1) {
+                    uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= (uint32_t)o)
+                        incl += n;
+                }
+                const uint32_t off = pos + incl - wdt;
+                for (uint32_t k = 0; k < wdt; k++)
+                    ring[(off + k) % kRing] = (uint8_t)token_byte(v, k);
+                pos += __shfl_sync(0xffffffffu, incl, 31);
+            } else {
+                /* trailer bytes, then 0x80, zeros, 64-bit big-endian bit length */
+                const uint32_t tail0 = pos;
+                const uint64_t bits = (uint64_t)len * 8;
+                for (uint32_t p = tail0 + lane; p < total; p += 32) {
+                    uint32_t v;
+                    if (p < len) {
+                        const uint32_t k = p - (len - 6);
+                        v = k == 0 ? tuple_op : (k == 1 ? 0x94u : (k == 2 ? 0x4eu : (k == 3 ? 0x87u : (k == 4 ? 0x94u : 0x2eu))));
+                    } else if (p == len) {
+                        v = 0x80u;
+                    } else if (p < total - 8) {
+                        v = 0u;
+                    } else {
+                        v = (uint32_t)(bits >> (8 * (total - 1 - p))) & 0xffu;
+                    }
+                    ring[p % kRing] = (uint8_t)v;
+                }
+                pos = total;
+            }
+            __syncwarp();
+            while (pos - done >= 64) {
+                sha_compress(st, ring + (done % kRing));
+                done += 64;
+            }
+            __syncwarp();
         }
+
+        /* digest: lane k < 8 publishes word k as the next parent and output */
+        uint32_t dw = st[0];
 #pragma unroll
-        for (int k = 0; k < 8; k++)
-            parent[k] = dg[k];
+        for (int k = 1; k < 8; k++)
+            if (lane == (uint32_t)k)
+                dw = st[k];
+        if (lane < 8) {
+            const uint32_t be = bswap(dw);
+            reinterpret_cast<uint32_t *>(par)[lane] = be;
+            uint8_t *o = out + (uint64_t)i * 32 + 4 * lane;
+            o[0] = (uint8_t)(dw >> 24);
+            o[1] = (uint8_t)(dw >> 16);
+            o[2] = (uint8_t)(dw >> 8);
+            o[3] = (uint8_t)dw;
+        }
+        __syncwarp();
     }
 }
 
@@ -315,8 +290,8 @@ extern "C" int kv_block_hash_launch(const int32_t *tokens, const int64_t *tok_of
         for (int k = 0; k < 8; k++)
             a.none_hash[k] = ((uint32_t)none_hash[4 * k] << 24) | ((uint32_t)none_hash[4 * k + 1] << 16) |
                              ((uint32_t)none_hash[4 * k + 2] << 8) | (uint32_t)none_hash[4 * k + 3];
-    unsigned grid = (num_req + kHashThreads - 1) / kHashThreads;
-    block_hash_kernel<<<grid, kHashThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    unsigned grid = (num_req + kWarpsPerCta - 1) / kWarpsPerCta;
+    block_hash_kernel<<<grid, kWarpsPerCta * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
     g_cc_kernel_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
 }
