@@ -168,7 +168,7 @@ def _load() -> C.CDLL:
         raise ImportError(
             f"{LIB_PATH} is not built; run `python -m demo_b200.build` (nvcc for sm_100a). "
             "There is no fallback implementation.")
-    lib = C.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | C.RTLD_GLOBAL)
+    lib = C.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | os.RTLD_LOCAL)
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.restype = res

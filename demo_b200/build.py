@@ -94,8 +94,10 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
         objs.append(obj)
     if force or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
+        # --exclude-libs: keep the statically linked CUDA runtime's symbols
+        # private, so they never interpose another runtime in the process
         _run([NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs),
-              "-Xlinker", "-soname,libcrosscache.so", "-lpthread"], verbose)
+              "-Xlinker", "-soname,libcrosscache.so", "-Xlinker", "--exclude-libs,ALL", "-lpthread"], verbose)
         os.replace(tmp, LIB)
     return LIB
 

@@ -32,8 +32,18 @@
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kUnroll = 8;
+/* launch shape; overridable at compile time for tuning sweeps */
+#ifndef KVCOPY_THREADS
+#define KVCOPY_THREADS 256
+#endif
+#ifndef KVCOPY_UNROLL
+#define KVCOPY_UNROLL 8
+#endif
+#ifndef KVCOPY_MIN_BLOCKS
+#define KVCOPY_MIN_BLOCKS 1
+#endif
+constexpr int kThreads = KVCOPY_THREADS;
+constexpr int kUnroll = KVCOPY_UNROLL;
 constexpr uint32_t kTileVectors = kThreads * kUnroll;   /* 2048 vectors */
 
 /* unsigned 32-bit division by a run-time constant: q = (umulhi(n, m) + n) >> s
@@ -126,7 +136,7 @@ __device__ void copy_tile_bytes(const Params &p, uint32_t r, uint8_t *layer, uin
 }
 
 template <int VEC, bool TO_RECORD>
-__global__ void __launch_bounds__(kThreads) kv_copy_kernel(const Params p)
+__global__ void __launch_bounds__(kThreads, KVCOPY_MIN_BLOCKS) kv_copy_kernel(const Params p)
 {
     using T = typename VecOf<VEC>::T;
 
