@@ -245,6 +245,258 @@ def run_reference_arm(args) -> None:
 
 
 # ---------------------------------------------------------------------------
+# prefix-reuse and MLA-eviction workloads (1 GPU, through the C API)
+
+def _sha_none(seed: str = "0") -> bytes:
+    import hashlib
+    import pickle
+    return hashlib.sha256(pickle.dumps(seed, protocol=5)).digest()
+
+
+def _device_hashes(tokens: np.ndarray, lens: np.ndarray, bs: int, dev: int) -> np.ndarray:
+    from demo_b200._lib import lib
+    nblk = int((lens // bs).sum())
+    out = np.zeros((nblk, 32), dtype=np.uint8)
+    flat = np.ascontiguousarray(tokens.astype(np.int32))
+    n = lib.kv_block_hash_host(dev, flat.ctypes.data, np.ascontiguousarray(lens).ctypes.data, len(lens), bs,
+                               _sha_none(), out.ctypes.data)
+    assert n == nblk, n
+    return out
+
+
+def run_cache_workload(args) -> None:
+    import torch
+
+    from demo_b200 import cache as cc
+    from demo_b200._lib import lib
+    from oracle.cache_model import LRUPool     # host-side LRU model: the checker only
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1:
+        raise SystemExit("this workload runs on 1 GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if args.workload == "prefix-reuse":
+        res = _prefix_reuse(args, dev, cc, lib)
+    else:
+        res = _mla_evict(args, dev, cc, lib, LRUPool)
+    print(json.dumps(res), flush=True)
+
+
+def _prefix_reuse(args, dev, cc, lib) -> dict:
+    """256 requests = one shared 1024-token prefix + a unique 512-token suffix
+    (token ids U[0,128256), seed 1); Llama-3-8B KV shapes (32 layers x 8 KV
+    heads x 128 bf16, block 16, 16384 blocks/layer, N(0,1) seed 0).  Per step:
+    clear, hash all 256 requests on the device, store the first 128 (block
+    table: seeded permutation, seed 2), look up the other 128, load only their
+    hit records into a fresh block table (seed 3), one cache_load per request."""
+    import torch
+    nreq, pre, suf = 256, 1024, 512
+    ntok = pre + suf
+    g = torch.Generator(device=dev).manual_seed(0)
+    layers = [torch.randn(2, NUM_BLOCKS, BS, KV_HEADS, HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+              for _ in range(L)]
+    layout, kp, vp = cc.layout_from_kv_tensors(layers)
+    rb = layout.per_token_size * CHUNK
+    gt = torch.Generator().manual_seed(1)
+    prefix = torch.randint(0, VOCAB, (pre,), generator=gt)
+    toks = torch.cat([prefix.repeat(nreq, 1), torch.randint(0, VOCAB, (nreq, suf), generator=gt)], 1).numpy()
+    lens = np.full(nreq, ntok, dtype=np.int64)
+    bpc = CHUNK // BS
+    kpr = ntok // CHUNK                      # 6 chunk keys per request
+    bpr = ntok // BS                         # 96 blocks per request
+    save_bt = torch.randperm(NUM_BLOCKS, generator=torch.Generator().manual_seed(2))[: 128 * bpr].numpy().astype(np.uint64)
+    load_bt = torch.randperm(NUM_BLOCKS, generator=torch.Generator().manual_seed(3)).numpy().astype(np.uint64)
+    uniq = pre // CHUNK + 128 * (kpr - pre // CHUNK)
+    cc.init(CHUNK, (uniq + 8) * rb, None)
+    w = cc.Worker("llama-3-8b", layout, kp, vp)
+    w.register()
+    key_nums = np.full(128, kpr, dtype=np.uint32)
+    hits = np.zeros(128, dtype=np.uint32)
+
+    def step(lat, check=False):
+        t0 = time.perf_counter()
+        w.clear()
+        hashes = _device_hashes(toks.reshape(-1), lens, BS, 0)
+        keys = np.ascontiguousarray(hashes[bpc - 1::bpc])           # 256 x 6 chunk keys
+        kb = keys.tobytes()
+        t1 = time.perf_counter()
+        assert lib.cache_store(C.byref(w.ctx), kb[: 128 * kpr * 32], 32, save_bt.ctypes.data, 128 * bpr) == 0
+        t2 = time.perf_counter()
+        kl = kb[128 * kpr * 32:]
+        assert lib.cache_lookup_batch(C.byref(w.ctx), kl, key_nums.ctypes.data, 128, 32, hits.ctypes.data) == 0
+        off = 0
+        for r in range(128):
+            h = int(hits[r])
+            bt = np.ascontiguousarray(load_bt[off: off + h * bpc])
+            ts = time.perf_counter()
+            assert lib.cache_load(C.byref(w.ctx), kl[r * kpr * 32: (r * kpr + h) * 32], 32, bt.ctypes.data, h * bpc) == 0
+            if lat is not None:
+                lat.append(time.perf_counter() - ts)
+            off += h * bpc
+        t3 = time.perf_counter()
+        ok = None
+        if check:
+            torch.cuda.synchronize()
+            src = torch.from_numpy(save_bt[: pre // BS].astype(np.int64)).to(dev)   # request 0's prefix blocks
+            ok = True
+            for r in range(128):
+                dst = torch.from_numpy(load_bt[r * (pre // BS): (r + 1) * (pre // BS)].astype(np.int64)).to(dev)
+                ok &= all(torch.equal(t[:, src].view(torch.int16), t[:, dst].view(torch.int16)) for t in layers)
+        return t1 - t0, t2 - t1, t3 - t2, int(hits.sum()), ok
+
+    _, _, _, _, ok = step(None, check=True)          # pristine first pass: verified
+    for _ in range(max(0, args.warmup - 1)):
+        step(None)
+    lat, parts = [], []
+    ta = time.perf_counter()
+    for _ in range(args.steps):
+        parts.append(step(lat))
+    te = time.perf_counter() - ta
+    st = w.stats()
+    w.unregister()
+    cc.exit()
+    hit_chunks = parts[-1][3]
+    stored_b = uniq * rb
+    loaded_b = hit_chunks * rb
+    save_s = statistics.median(p[1] for p in parts)
+    load_s = statistics.median(p[2] for p in parts)
+    return {"metric": METRIC, "value": round((stored_b + loaded_b) * args.steps / te / GB, 3), "unit": "GB/s",
+            "workload": "prefix-reuse: Llama-3-8B KV, 256 requests = shared 1024-token prefix + unique "
+                        "512-token suffix; save 128, look up + load the other 128",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(te / args.steps * 1e3, 3), "higher_is_better": True,
+            "data": "synthetic", "dtype": "u8",
+            "hit_blocks_per_request": hit_chunks * bpc // 128, "hit_rate_chunks": round(hit_chunks / (128 * kpr), 4),
+            "records_stored_per_step": uniq, "store_keys_deduplicated_per_step": 128 * kpr - uniq,
+            "save_gbs": round(stored_b / save_s / GB, 3), "load_gbs": round(loaded_b / load_s / GB, 3),
+            "p50_load_latency_ms": round(statistics.median(lat) * 1e3, 3),
+            "hash_store_lookup_load_s": [round(statistics.median(p[i] for p in parts), 4) for i in range(3)],
+            "verified_bytes": bool(ok), "stats": st}
+
+
+def _mla_evict(args, dev, cc, lib, LRUPool) -> dict:
+    """DeepSeek-V2-Lite MLA latent cache: 27 layers, K-only width 576 bf16,
+    block 64.  512 requests x 4096 tokens = a 2048-token base prefix (one of 64
+    seeded bases, chosen Zipf(1.1), seed 4) + a unique 2048-token suffix
+    (seed 5).  Host pool = 25 % of the 60.75 GiB working set, so LRU eviction
+    runs continuously.  Per request, in order: look up its 16 chunk keys, load
+    the hit prefix records into its blocks, write the KV of the missed chunks
+    (a pattern derived from each chunk key, standing in for the model), store
+    all 16 keys.  Every loaded block is checked against its key's pattern, and
+    the hit and eviction counts against the host LRU model."""
+    import torch
+    nl, width, bs, nreq, ntok, nbase = 27, 576, 64, 512, 4096, 64
+    nb = 4096                                         # 64 requests' worth of blocks
+    kv = torch.zeros(nl, nb, bs, width, dtype=torch.bfloat16, device=dev)
+    layers = [kv[l] for l in range(nl)]
+    layout, kp, vp = cc.layout_from_kv_tensors(layers)
+    assert layout.kv == 1 and layout.unit == width * 2
+    rb = layout.per_token_size * CHUNK                # 7.59 MiB
+    bpc = CHUNK // bs                                 # 4 blocks per record
+    kpr = ntok // CHUNK                               # 16 chunk keys per request
+    total_records = nreq * kpr
+    pool_records = total_records // 4                 # 25 % of the working set
+    gt = torch.Generator().manual_seed(4)
+    bases = torch.randint(0, VOCAB, (nbase, ntok // 2), generator=torch.Generator().manual_seed(6))
+    ranks = np.arange(1, nbase + 1, dtype=np.float64)
+    pz = ranks ** -1.1
+    pz /= pz.sum()
+    choice = np.random.default_rng(4).choice(nbase, size=nreq, p=pz)
+    suffix = torch.randint(0, VOCAB, (nreq, ntok // 2), generator=torch.Generator().manual_seed(5))
+    toks = torch.cat([bases[torch.from_numpy(choice)], suffix], 1).numpy()
+    lens = np.full(nreq, ntok, dtype=np.int64)
+    hashes = _device_hashes(toks.reshape(-1), lens, bs, 0)
+    keys = np.ascontiguousarray(hashes[bpc - 1::bpc]).reshape(nreq, kpr, 32)
+    key8 = torch.from_numpy(keys[:, :, :8].copy().view(np.int64).reshape(nreq, kpr)).to(dev)
+    lidx = torch.arange(nl, dtype=torch.int64, device=dev).view(nl, 1, 1) << 56
+    jidx = (torch.arange(bpc, dtype=torch.int64, device=dev) << 48).view(1, 1, bpc)
+    kv64 = kv.view(nl, nb, -1).view(torch.int64)      # [27, nb, 64*576*2/8]
+    perm = np.random.default_rng(7).permutation(nb)
+
+    # expected hits / evictions from the host LRU model
+    model = LRUPool(pool_records)
+    exp_hits = []
+    for r in range(nreq):
+        kr = [bytes(k) for k in keys[r]]
+        h = model.lookup(kr)
+        exp_hits.append(h)
+        model.store(kr)
+    cc.init(CHUNK, pool_records * rb, None)
+    w = cc.Worker("deepseek-v2-lite", layout, kp, None)
+    w.register()
+
+    def patterns(r, chunks):
+        """int64 fill values [27, len(chunks) * 4, 1] of the given chunks of request r"""
+        k = key8[r, chunks].view(1, len(chunks), 1)             # [1, c, 1]
+        vals = (k ^ lidx) ^ jidx                                # [27, c, 4]
+        return vals.reshape(nl, len(chunks) * bpc, 1)
+
+    def one_pass(check: bool):
+        w.clear()
+        hit_tot, mism, store_s, load_s, lat = 0, 0, 0.0, 0.0, []
+        moved_in = moved_out = 0
+        for r in range(nreq):
+            base = (r % (nb // (kpr * bpc))) * kpr * bpc
+            bt = perm[base: base + kpr * bpc].astype(np.uint64)
+            kb = keys[r].tobytes()
+            h = lib.cache_lookup(C.byref(w.ctx), kb, kpr, 32) // 32
+            hit_tot += h
+            if h:
+                ts = time.perf_counter()
+                assert lib.cache_load(C.byref(w.ctx), kb[: h * 32], 32, np.ascontiguousarray(bt[: h * bpc]).ctypes.data,
+                                      h * bpc) == 0
+                dt = time.perf_counter() - ts
+                load_s += dt
+                lat.append(dt)
+                moved_in += h * rb
+                if check:
+                    got = kv64[:, torch.from_numpy(bt[: h * bpc].astype(np.int64)).to(dev)]
+                    mism += int((got != patterns(r, list(range(h)))).sum())     # every word of every block
+            miss = list(range(h, kpr))
+            if miss:
+                idx = torch.from_numpy(bt[h * bpc:].astype(np.int64)).to(dev)
+                kv64[:, idx] = patterns(r, miss).expand(nl, len(miss) * bpc, kv64.shape[2])
+            torch.cuda.synchronize()
+            before = w.stats()["stored"]
+            ts = time.perf_counter()
+            assert lib.cache_store(C.byref(w.ctx), kb, 32, np.ascontiguousarray(bt).ctypes.data, kpr * bpc) == 0
+            store_s += time.perf_counter() - ts
+            moved_out += (w.stats()["stored"] - before) * rb
+        return hit_tot, mism, store_s, load_s, lat, moved_in, moved_out
+
+    ev0 = w.stats()["evictions"]
+    hit_tot, mism, *_ = one_pass(True)
+    ev1 = w.stats()["evictions"]
+    for _ in range(max(0, args.warmup - 1)):
+        one_pass(False)
+    res = []
+    ta = time.perf_counter()
+    for _ in range(args.steps):
+        e0 = w.stats()["evictions"]
+        res.append(one_pass(False) + (w.stats()["evictions"] - e0,))
+    te = time.perf_counter() - ta
+    w.unregister()
+    cc.exit()
+    moved = sum(r[5] + r[6] for r in res)
+    lat = [x for r in res for x in r[4]]
+    return {"metric": METRIC, "value": round(moved / te / GB, 3), "unit": "GB/s",
+            "workload": "mla-evict: DeepSeek-V2-Lite MLA latent (27 layers, 576 bf16, block 64), 512 requests x "
+                        "4096 tokens, Zipf(1.1) reuse of 64 base prefixes, host pool 25 % of the working set",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(te / args.steps * 1e3, 3), "higher_is_better": True,
+            "data": "synthetic", "dtype": "u8",
+            "pool_records": pool_records, "working_set_records": total_records,
+            "hit_rate_chunks": round(hit_tot / total_records, 4),
+            "evictions_per_pass": ev1 - ev0, "hits_per_pass": hit_tot,
+            "lru_model_hits": int(sum(exp_hits)), "lru_model_evictions": model.evictions,
+            "hits_match_model": hit_tot == int(sum(exp_hits)), "evictions_match_model": (ev1 - ev0) == model.evictions,
+            "save_gbs": round(sum(r[6] for r in res) / sum(r[2] for r in res) / GB, 3),
+            "load_gbs": round(sum(r[5] for r in res) / max(1e-9, sum(r[3] for r in res)) / GB, 3),
+            "p50_load_latency_ms": round(statistics.median(lat) * 1e3, 3) if lat else None,
+            "loaded_block_mismatches": mism, "verified_bytes": mism == 0}
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 
 def main() -> None:
@@ -258,9 +510,16 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=L, help="smaller cases for ncu captures only")
     ap.add_argument("--requests", type=int, default=REQS)
     ap.add_argument("--blocks-per-layer", type=int, default=NUM_BLOCKS)
+    ap.add_argument("--workload", default="llama3-8b",
+                    choices=["llama3-8b", "prefix-reuse", "mla-evict"],
+                    help="llama3-8b: the headline save/load config; prefix-reuse and mla-evict: "
+                         "the prefix-reuse and MLA-eviction configs (1 GPU)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
+        return
+    if args.workload != "llama3-8b":
+        run_cache_workload(args)
         return
 
     import torch
