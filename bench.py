@@ -48,15 +48,29 @@ REQS, TOKENS, CHUNK, VOCAB = 64, 2048, 256, 128256
 GB = 1e9
 
 
-def workload_config(tp: int) -> dict:
+PRESETS = {
+    # the headline config: Llama-3-8B GQA, 64 requests x 2048 tokens
+    "llama3-8b": dict(layers=32, requests=64, tokens=2048, blocks=16384,
+                      name="llama3-8b-gqa-kv-offload: 32 layers x 8 KV heads x 128 bf16, block 16, "
+                           "16384 blocks/layer; 64 requests x 2048 tokens; 256-token records"),
+    # the TP config: Llama-3-70B, 80 layers, heads re-split per world size
+    "tp70b": dict(layers=80, requests=32, tokens=8192, blocks=16384,
+                  name="llama3-70b-tp-kv-offload: 80 layers x 8 KV heads x 128 bf16 split over TP ranks, "
+                       "block 16, 16384 blocks/layer; 32 requests x 8192 tokens; 256-token records"),
+}
+
+
+def workload_config(tp: int, preset: str = "llama3-8b", **over) -> dict:
+    pr = dict(PRESETS[preset], **over)
+    paged = 2 * pr["blocks"] * BS * KV_HEADS * HEAD_DIM * ELT * pr["layers"] / tp / 2**30
+    recs = 2 * pr["requests"] * pr["tokens"] * KV_HEADS * HEAD_DIM * ELT * pr["layers"] / tp / 2**30
     return {
-        "workload": "llama3-8b-gqa-kv-offload: 32 layers x 8 KV heads x 128 bf16, block 16, "
-                    "16384 blocks/layer; 64 requests x 2048 tokens; 256-token records",
-        "layers": L, "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "kv_dtype": "bf16",
-        "block_size": BS, "blocks_per_layer": NUM_BLOCKS, "requests": REQS,
-        "tokens_per_request": TOKENS, "chunk_tokens": CHUNK, "tp": tp,
+        "workload": pr["name"],
+        "layers": pr["layers"], "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "kv_dtype": "bf16",
+        "block_size": BS, "blocks_per_layer": pr["blocks"], "requests": pr["requests"],
+        "tokens_per_request": pr["tokens"], "chunk_tokens": CHUNK, "tp": tp,
         "kv_heads_per_rank": KV_HEADS // tp,
-        "l2": "inputs larger than L2: 32 GiB/tp paged cache, 16 GiB/tp of records per step",
+        "l2": f"inputs larger than L2: {paged:g} GiB paged cache and {recs:g} GiB of records per rank per step",
     }
 
 
@@ -313,6 +327,9 @@ def _prefix_reuse(args, dev, cc, lib) -> dict:
     key_nums = np.full(128, kpr, dtype=np.uint32)
     hits = np.zeros(128, dtype=np.uint32)
 
+    src = torch.from_numpy(save_bt[: pre // BS].astype(np.int64)).to(dev)      # request 0's prefix blocks
+    snap = [t[:, src].clone() for t in layers]      # what the stored prefix records must hold
+
     def step(lat, check=False):
         t0 = time.perf_counter()
         w.clear()
@@ -336,12 +353,13 @@ def _prefix_reuse(args, dev, cc, lib) -> dict:
         t3 = time.perf_counter()
         ok = None
         if check:
+            # the load table may overlap the save table (both are drawn from all
+            # blocks), so compare every loaded prefix with the pre-step snapshot
             torch.cuda.synchronize()
-            src = torch.from_numpy(save_bt[: pre // BS].astype(np.int64)).to(dev)   # request 0's prefix blocks
             ok = True
             for r in range(128):
                 dst = torch.from_numpy(load_bt[r * (pre // BS): (r + 1) * (pre // BS)].astype(np.int64)).to(dev)
-                ok &= all(torch.equal(t[:, src].view(torch.int16), t[:, dst].view(torch.int16)) for t in layers)
+                ok &= all(torch.equal(sn.view(torch.int16), t[:, dst].view(torch.int16)) for sn, t in zip(snap, layers))
         return t1 - t0, t2 - t1, t3 - t2, int(hits.sum()), ok
 
     _, _, _, _, ok = step(None, check=True)          # pristine first pass: verified
@@ -510,15 +528,21 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=L, help="smaller cases for ncu captures only")
     ap.add_argument("--requests", type=int, default=REQS)
     ap.add_argument("--blocks-per-layer", type=int, default=NUM_BLOCKS)
+    ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--workload", default="llama3-8b",
-                    choices=["llama3-8b", "prefix-reuse", "mla-evict"],
-                    help="llama3-8b: the headline save/load config; prefix-reuse and mla-evict: "
-                         "the prefix-reuse and MLA-eviction configs (1 GPU)")
+                    choices=["llama3-8b", "tp70b", "prefix-reuse", "mla-evict"],
+                    help="llama3-8b: the headline save/load config; tp70b: the Llama-3-70B TP "
+                         "config; prefix-reuse and mla-evict: the prefix-reuse and MLA-eviction "
+                         "configs (1 GPU)")
     args = ap.parse_args()
+    if args.workload == "tp70b":
+        pr = PRESETS["tp70b"]
+        args.layers, args.requests, args.tokens, args.blocks_per_layer = (
+            pr["layers"], pr["requests"], pr["tokens"], pr["blocks"])
     if args.impl == "reference":
         run_reference_arm(args)
         return
-    if args.workload != "llama3-8b":
+    if args.workload in ("prefix-reuse", "mla-evict"):
         run_cache_workload(args)
         return
 
@@ -559,12 +583,13 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
-    n_layers, n_req, n_blocks = args.layers, args.requests, args.blocks_per_layer
+    n_layers, n_req, n_blocks, n_tok = args.layers, args.requests, args.blocks_per_layer, args.tokens
+    preset = "tp70b" if args.workload == "tp70b" else "llama3-8b"
     heads = KV_HEADS // world
     hidden = heads * HEAD_DIM
     unit = hidden * ELT
     bpc = CHUNK // BS
-    nblk = n_req * TOKENS // BS                # 8192 blocks
+    nblk = n_req * n_tok // BS                 # 8192 blocks
     nrec = nblk // bpc                         # 512 records
     rec_bytes = 2 * n_layers * CHUNK * unit
     payload = nrec * rec_bytes                 # one direction, this rank
@@ -579,53 +604,84 @@ def main() -> None:
         del full
     torch.cuda.empty_cache()
     layout, kp, vp = cc.layout_from_kv_tensors(layers)
-    # block tables: a seeded permutation of free block ids for the save (seed 2);
-    # the reload goes to a fresh seeded permutation (seed 3) of the blocks the
-    # save did not use, so repeated steps never overwrite a block a later
-    # gather reads and the final bytes can be compared exactly
-    if 2 * nblk > n_blocks:
-        raise SystemExit("blocks per layer must hold the save and the reload tables")
+    # block tables: a seeded permutation of free block ids for the save (seed 2).
+    # The reload goes to a fresh seeded permutation (seed 3): of the blocks the
+    # save did not use when the cache holds both tables (then repeated steps
+    # never overwrite a block a later gather reads and the final bytes are
+    # compared exactly), else of all blocks ("the cache was cleared").  Either
+    # way the first step is checked against per-block checksums taken before it.
+    if nblk > n_blocks:
+        raise SystemExit("blocks per layer must hold the saved blocks")
     perm = torch.randperm(n_blocks, generator=torch.Generator().manual_seed(2))
     bt_save = perm[:nblk].numpy().astype(np.uint64)
-    free = perm[nblk:]
+    disjoint = 2 * nblk <= n_blocks
+    free = perm[nblk:] if disjoint else perm
     bt_load = free[torch.randperm(free.numel(), generator=torch.Generator().manual_seed(3))][:nblk].numpy().astype(np.uint64)
-    tokens = torch.randint(0, VOCAB, (n_req, TOKENS), generator=torch.Generator().manual_seed(1),
+    tokens = torch.randint(0, VOCAB, (n_req, n_tok), generator=torch.Generator().manual_seed(1),
                            dtype=torch.int64).to(torch.int32).numpy()
+
+    def block_sums(idx: "torch.Tensor") -> list:
+        """per (layer, K/V, block) position-weighted int64 checksums of the given blocks"""
+        out = []
+        for t in layers:
+            per = []
+            for kv in range(2):
+                x = t[kv, idx].view(torch.int16).reshape(idx.numel(), -1).to(torch.int64)
+                wgt = (torch.arange(x.shape[1], device=dev, dtype=torch.int64) % 251) + 1
+                per.append(torch.stack([x.sum(1), (x * wgt).sum(1)]))
+                del x
+            out.append(torch.stack(per))
+        return out
+
+    def sums_equal(a: list, b: list) -> bool:
+        return all(torch.equal(x, y) for x, y in zip(a, b))
 
     # ---------------- value: device-resident records, kernel path ----------
     kp_d = torch.tensor(kp, dtype=torch.int64, device=dev)
     vp_d = torch.tensor(vp, dtype=torch.int64, device=dev)
-    records = torch.empty(nrec * rec_bytes, dtype=torch.uint8, device=dev)
-    rec_ptrs = torch.arange(nrec, dtype=torch.int64, device=dev) * rec_bytes + records.data_ptr()
+    # records in HBM: all of them when they fit next to the paged cache, else
+    # in batches that reuse one buffer (each batch = one gather + one scatter)
+    free_b, _ = torch.cuda.mem_get_info(dev)
+    batch = int(max(1, min(nrec, (free_b - (12 << 30)) // rec_bytes)))
+    nbatch = (nrec + batch - 1) // batch
+    records = torch.empty(batch * rec_bytes, dtype=torch.uint8, device=dev)
+    rec_ptrs = torch.arange(batch, dtype=torch.int64, device=dev) * rec_bytes + records.data_ptr()
     b_save = torch.from_numpy(bt_save.astype(np.int64)).to(dev)
     b_load = torch.from_numpy(bt_load.astype(np.int64)).to(dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
 
-    def desc(bids, direction):
+    def desc(bids, first, n, direction):
         return KvCopyDesc(layer_k=kp_d.data_ptr(), layer_v=vp_d.data_ptr(), records=rec_ptrs.data_ptr(),
-                          slots=None, block_ids=bids.data_ptr(), error=err.data_ptr(),
+                          slots=None, block_ids=bids.data_ptr() + first * bpc * 8, error=err.data_ptr(),
                           page_buffer_size=n_blocks * BS, unit_bytes=unit, num_tokens=CHUNK,
-                          block_size=BS, num_layers=n_layers, num_records=nrec, direction=direction)
+                          block_size=BS, num_layers=n_layers, num_records=n, direction=direction)
 
-    d_gather, d_scatter = desc(b_save, 1), desc(b_load, 0)
-    assert lib.kv_copy_payload_bytes(C.byref(d_gather)) == payload
+    batches = [(i * batch, min(batch, nrec - i * batch)) for i in range(nbatch)]
+    d_pairs = [(desc(b_save, f, n, 1), desc(b_load, f, n, 0)) for f, n in batches]
+    assert sum(lib.kv_copy_payload_bytes(C.byref(g)) for g, _ in d_pairs) == payload
     stream = torch.cuda.Stream(dev)
     sptr = C.c_void_p(stream.cuda_stream)
 
     def kernel_step(ev=None):
-        if ev:
-            ev[0].record(stream)
-        assert lib.kv_copy_launch(C.byref(d_gather), sptr) == 0
-        if ev:
-            ev[1].record(stream)
-        assert lib.kv_copy_launch(C.byref(d_scatter), sptr) == 0
-        if ev:
-            ev[2].record(stream)
+        for bi, (dg, ds) in enumerate(d_pairs):
+            if ev:
+                ev[bi][0].record(stream)
+            assert lib.kv_copy_launch(C.byref(dg), sptr) == 0
+            if ev:
+                ev[bi][1].record(stream)
+            assert lib.kv_copy_launch(C.byref(ds), sptr) == 0
+            if ev:
+                ev[bi][2].record(stream)
 
-    for _ in range(args.warmup):
+    sums0 = block_sums(b_save)
+    kernel_step()                      # first step from the pristine cache: checked
+    torch.cuda.synchronize()
+    ok_first = sums_equal(block_sums(b_load), sums0)
+    for _ in range(args.warmup - 1):
         kernel_step()
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(nbatch)]
+           for _ in range(args.steps)]
     l0 = lib.crosscache_kernel_launches()
     barrier()
     torch.cuda.synchronize()
@@ -641,15 +697,18 @@ def main() -> None:
     barrier()
     launches = lib.crosscache_kernel_launches() - l0
     dt = max_over_ranks(t0.elapsed_time(t1) / 1e3)
-    gather_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
-    scatter_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    # per-step sums over the record batches (one launch each when all records fit)
+    gather_ms = statistics.mean(sum(b[0].elapsed_time(b[1]) for b in e) for e in evs)
+    scatter_ms = statistics.mean(sum(b[1].elapsed_time(b[2]) for b in e) for e in evs)
     assert int(err.item()) == 0, "kv copy reported an error"
-    # verify: block bt_load[i] of the destination == block bt_save[i] of the source
-    ok_value = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers)
+    # verify: the first step against the pre-step checksums; with disjoint
+    # tables also every byte after the timed steps
+    ok_value = ok_first and (not disjoint or all(
+        torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers))
     total_payload = sum_over_ranks(2 * payload)
     value = total_payload * args.steps / dt / GB
     hbm_peak, peak_kind = peaks()
-    achieved = 2 * payload / (gather_ms / 1e3) / GB       # read + write bytes per gather launch
+    achieved = 2 * payload / (gather_ms / 1e3) / GB       # read + write bytes of the gathers of a step
     del records
     torch.cuda.empty_cache()
 
@@ -657,9 +716,9 @@ def main() -> None:
     from demo_b200.hashing import block_hashes_device
     none_hash_h = __import__("hashlib").sha256(__import__("pickle").dumps("0", protocol=5)).digest()
     tok_d = torch.from_numpy(tokens.reshape(-1).copy()).to(dev)
-    toff_d = torch.arange(n_req, dtype=torch.int64, device=dev) * TOKENS
-    ooff_d = torch.arange(n_req, dtype=torch.int64, device=dev) * (TOKENS // BS)
-    nb_d = torch.full((n_req,), TOKENS // BS, dtype=torch.int32, device=dev)
+    toff_d = torch.arange(n_req, dtype=torch.int64, device=dev) * n_tok
+    ooff_d = torch.arange(n_req, dtype=torch.int64, device=dev) * (n_tok // BS)
+    nb_d = torch.full((n_req,), n_tok // BS, dtype=torch.int32, device=dev)
     hout = torch.empty(nblk, 32, dtype=torch.uint8, device=dev)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -674,7 +733,7 @@ def main() -> None:
     hash_info = {"kernel_ms": round(hash_ms, 4), "blocks": nblk, "chains": n_req,
                  "blocks_per_s": round(nblk / (hash_ms / 1e3), 1),
                  "sha256_compressions_per_s": round(3 * nblk / (hash_ms / 1e3), 1),
-                 "us_per_block_along_a_chain": round(hash_ms * 1e3 / (TOKENS // BS), 3),
+                 "us_per_block_along_a_chain": round(hash_ms * 1e3 / (n_tok // BS), 3),
                  "bound": "integer latency along each chain (3 SHA-256 compressions per 16-token block)"}
 
     # ---------------- e2e: public C API, pinned host pool -------------------
@@ -706,13 +765,13 @@ def main() -> None:
         from demo_b200._lib import lib as L_
         from demo_b200.tp import agree_min_hits
         flat_tok = np.ascontiguousarray(tokens.reshape(-1))
-        tok_lens = np.full(n_req, TOKENS, dtype=np.int64)
+        tok_lens = np.full(n_req, n_tok, dtype=np.int64)
         none_hash = __import__("hashlib").sha256(__import__("pickle").dumps("0", protocol=5)).digest()
         hashes = np.zeros((nblk, 32), dtype=np.uint8)
-        key_nums = np.full(n_req, TOKENS // CHUNK, dtype=np.uint32)
+        key_nums = np.full(n_req, n_tok // CHUNK, dtype=np.uint32)
         hits = np.zeros(n_req, dtype=np.uint32)
         bt_save_c = np.ascontiguousarray(bt_save)
-        per_req_blocks = TOKENS // BS
+        per_req_blocks = n_tok // BS
         load_bids = [np.ascontiguousarray(bt_load[r * per_req_blocks:(r + 1) * per_req_blocks]) for r in range(n_req)]
 
         def e2e_step(lat: list | None):
@@ -730,7 +789,7 @@ def main() -> None:
             ret = L_.cache_lookup_batch(C.byref(w.ctx), kb, key_nums.ctypes.data, n_req, 32, hits.ctypes.data)
             assert ret == 0
             hit = agree_min_hits(hits, device=dev)       # NCCL all-reduce(min) under TP
-            per_req_keys = TOKENS // CHUNK
+            per_req_keys = n_tok // CHUNK
             for r in range(n_req):
                 h = int(hit[r])
                 ts = time.perf_counter()
@@ -742,9 +801,15 @@ def main() -> None:
             t_d = time.perf_counter()
             return t_b - t_a, t_c - t_b, t_d - t_c, int(hit.sum())
 
-        for t in layers:   # verification needs the destination blocks to start empty
-            t[:, b_load] = 0
-        for _ in range(args.warmup):
+        if disjoint:
+            for t in layers:   # the exact final check needs the destination blocks empty
+                t[:, b_load] = 0
+        sums1 = block_sums(b_save)
+        e2e_step(None)         # checked first step
+        torch.cuda.synchronize()
+        ok_e2e_first = sums_equal(block_sums(b_load), sums1)
+        del sums1
+        for _ in range(args.warmup - 1):
             e2e_step(None)
         lat: list[float] = []
         parts = []
@@ -758,7 +823,8 @@ def main() -> None:
         te = max_over_ranks(time.perf_counter() - ts0)
         barrier()
         e2e_launches = lib.crosscache_kernel_launches() - l1
-        ok_e2e = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers)
+        ok_e2e = ok_e2e_first and (not disjoint or all(
+            torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers))
         st = w.stats()
         w.unregister()
         cc.exit()
@@ -795,10 +861,12 @@ def main() -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic (seeded N(0,1) bf16 KV, uniform token ids, random block tables)",
-            "config": workload_config(world) if (n_layers, n_req, n_blocks) == (L, REQS, NUM_BLOCKS) else
-            {**workload_config(world), "workload": f"reduced case for profiling: {n_layers} layers, {n_req} requests, "
-                                                    f"{n_blocks} blocks/layer", "layers": n_layers,
-             "requests": n_req, "blocks_per_layer": n_blocks},
+            "config": workload_config(world, preset) if (n_layers, n_req, n_blocks, n_tok) == tuple(
+                PRESETS[preset][k] for k in ("layers", "requests", "blocks", "tokens")) else
+            {**workload_config(world, preset, layers=n_layers, requests=n_req, blocks=n_blocks, tokens=n_tok),
+             "workload": f"reduced case for profiling: {n_layers} layers, {n_req} requests x {n_tok} tokens, "
+                         f"{n_blocks} blocks/layer"},
+            "record_batches_per_step": nbatch,
             "roofline": {"bound": "hbm", "kernel": "kv_copy gather (save)", "achieved": round(achieved, 1),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "peak_kind": peak_kind, "traffic": ncu_traffic(),
