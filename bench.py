@@ -789,6 +789,7 @@ def main() -> None:
             ret = L_.cache_lookup_batch(C.byref(w.ctx), kb, key_nums.ctypes.data, n_req, 32, hits.ctypes.data)
             assert ret == 0
             hit = agree_min_hits(hits, device=dev)       # NCCL all-reduce(min) under TP
+            t_d = time.perf_counter()
             per_req_keys = n_tok // CHUNK
             for r in range(n_req):
                 h = int(hit[r])
@@ -798,8 +799,8 @@ def main() -> None:
                 assert ret == 0, ret
                 if lat is not None:
                     lat.append(time.perf_counter() - ts)
-            t_d = time.perf_counter()
-            return t_b - t_a, t_c - t_b, t_d - t_c, int(hit.sum())
+            t_e = time.perf_counter()
+            return t_b - t_a, t_c - t_b, t_e - t_d, int(hit.sum()), t_d - t_c
 
         if disjoint:
             for t in layers:   # the exact final check needs the destination blocks empty
@@ -825,6 +826,68 @@ def main() -> None:
         e2e_launches = lib.crosscache_kernel_launches() - l1
         ok_e2e = ok_e2e_first and (not disjoint or all(
             torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers))
+
+        # duplex: request r's load (H2D) overlaps request r+1's save (D2H), the
+        # two running on separate adaptor lanes from two host threads -- the
+        # cache serving stores and loads at once, as the reference's separate
+        # store and load thread pools do.  Needs disjoint block tables.
+        duplex = None
+        if world == 1 and disjoint:
+            import threading
+            per_req_keys = n_tok // CHUNK
+            save_bids = [np.ascontiguousarray(bt_save[r * per_req_blocks:(r + 1) * per_req_blocks])
+                         for r in range(n_req)]
+
+            def duplex_step(dlat):
+                w.clear()
+                n = L_.kv_block_hash_host(local, flat_tok.ctypes.data, tok_lens.ctypes.data, n_req, BS,
+                                          none_hash, hashes.ctypes.data)
+                assert n == nblk
+                kb = np.ascontiguousarray(hashes[bpc - 1::bpc]).tobytes()
+                ready = [threading.Event() for _ in range(n_req)]
+                errs = []
+
+                def saver():
+                    for r in range(n_req):
+                        kr = kb[r * per_req_keys * 32:(r + 1) * per_req_keys * 32]
+                        ret = L_.cache_store(C.byref(w.ctx), kr, 32, save_bids[r].ctypes.data, per_req_blocks)
+                        if ret:
+                            errs.append(ret)
+                        ready[r].set()
+                th = threading.Thread(target=saver)
+                th.start()
+                for r in range(n_req):
+                    ready[r].wait()
+                    kr = kb[r * per_req_keys * 32:(r + 1) * per_req_keys * 32]
+                    h = L_.cache_lookup(C.byref(w.ctx), kr, per_req_keys, 32) // 32
+                    ts = time.perf_counter()
+                    ret = L_.cache_load(C.byref(w.ctx), kr[: h * 32], 32, load_bids[r].ctypes.data, h * bpc)
+                    if ret:
+                        errs.append(ret)
+                    if dlat is not None:
+                        dlat.append(time.perf_counter() - ts)
+                th.join()
+                assert not errs, errs
+
+            for t in layers:
+                t[:, b_load] = 0
+            duplex_step(None)
+            torch.cuda.synchronize()
+            ok_dup = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16))
+                         for t in layers)
+            for _ in range(args.warmup - 1):
+                duplex_step(None)
+            dlat: list[float] = []
+            td0 = time.perf_counter()
+            for _ in range(args.steps):
+                duplex_step(dlat)
+            td = time.perf_counter() - td0
+            duplex = {"value": round(2 * payload * args.steps / td / GB, 3), "unit": "GB/s",
+                      "ms_per_step": round(td / args.steps * 1e3, 3),
+                      "p50_load_latency_ms": round(statistics.median(dlat) * 1e3, 3),
+                      "verified_bytes": bool(ok_dup),
+                      "note": "same steps as e2e (hash, store every request, look up and load every "
+                              "request) with the load of request r overlapping the save of request r+1"}
         st = w.stats()
         w.unregister()
         cc.exit()
@@ -832,6 +895,7 @@ def main() -> None:
         save_s = max_over_ranks(statistics.median(p[1] for p in parts))
         load_s = max_over_ranks(statistics.median(p[2] for p in parts))
         hash_s = max_over_ranks(statistics.median(p[0] for p in parts))
+        agree_s = max_over_ranks(statistics.median(p[4] for p in parts))
         p50 = max_over_ranks(statistics.median(lat)) * 1e3
         e2e_value = total_payload * args.steps / te / GB
         h2d = payload + flat_tok.nbytes + tok_lens.nbytes + nblk * 8
@@ -840,10 +904,11 @@ def main() -> None:
                "d2h_bytes_per_step": int(d2h), "ms_per_step": round(te / args.steps * 1e3, 3),
                "save_gbs_per_gpu": round(payload / save_s / GB, 3),
                "load_gbs_per_gpu": round(payload / load_s / GB, 3),
-               "hash_ms": round(hash_s * 1e3, 3), "p50_load_latency_ms": round(p50, 3),
+               "hash_ms": round(hash_s * 1e3, 3), "lookup_agree_ms": round(agree_s * 1e3, 3),
+               "p50_load_latency_ms": round(p50, 3),
                "p90_load_latency_ms": round(float(np.percentile(lat, 90)) * 1e3, 3),
                "hit_blocks_per_request": hit_blocks // n_req, "gpu_launches": int(e2e_launches),
-               "verified_bytes": bool(ok_e2e), "evictions": st["evictions"]}
+               "verified_bytes": bool(ok_e2e), "evictions": st["evictions"], "duplex": duplex}
         link = {"d2h_peak_gbs": round(link_peak["d2h"], 2), "h2d_peak_gbs": round(link_peak["h2d"], 2),
                 "save_frac": round(payload / save_s / GB / link_peak["d2h"], 4),
                 "load_frac": round(payload / load_s / GB / link_peak["h2d"], 4),
