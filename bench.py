@@ -741,7 +741,9 @@ def main() -> None:
     link = None
     p50 = None
     if not args.skip_e2e:
-        # host-link peaks measured in this run (pinned 256 MiB copies)
+        # host-link peaks measured in this run: pinned 256 MiB cudaMemcpyAsync,
+        # 16 per direction (4 GiB), every rank at once after a barrier -- the
+        # per-GPU link as the e2e steps see it when all ranks copy together
         hbuf = torch.empty(256 << 20, dtype=torch.uint8, pin_memory=True)
         dbuf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         link_peak = {}
@@ -750,13 +752,14 @@ def main() -> None:
             for _ in range(2):
                 fn()
             torch.cuda.synchronize()
+            barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            for _ in range(8):
+            for _ in range(16):
                 fn()
             b.record()
             torch.cuda.synchronize()
-            link_peak[name] = 8 * (256 << 20) / (a.elapsed_time(b) / 1e3) / GB
+            link_peak[name] = 16 * (256 << 20) / (a.elapsed_time(b) / 1e3) / GB
         del hbuf, dbuf
 
         cc.init(CHUNK, (nrec + 1) * rec_bytes, None)
@@ -912,7 +915,7 @@ def main() -> None:
         link = {"d2h_peak_gbs": round(link_peak["d2h"], 2), "h2d_peak_gbs": round(link_peak["h2d"], 2),
                 "save_frac": round(payload / save_s / GB / link_peak["d2h"], 4),
                 "load_frac": round(payload / load_s / GB / link_peak["h2d"], 4),
-                "note": "per GPU; pinned 256 MiB cudaMemcpyAsync measured in this run"}
+                "note": "per GPU; pinned cudaMemcpyAsync, 4 GiB per direction, all ranks at once, this run"}
 
     clocks.__exit__(None, None, None)
     cpu = None
