@@ -16,6 +16,8 @@ from dataclasses import dataclass
 from itertools import islice
 from typing import Iterable
 
+import logging
+
 import numpy as np
 import torch
 
@@ -23,6 +25,7 @@ from . import cache as cc
 from .tp import agree_min_hits
 
 CHUNK_SIZE = 256          # tokens per record (python/adaptor.py:74,133)
+logger = logging.getLogger(__name__)
 
 _service_lock = threading.Lock()
 _service_refs = 0
@@ -126,6 +129,7 @@ class WorkerAdapter:
         self.load_futures: dict[str, tuple[Future, list[str]]] = {}
         self.finished_stores: set[str] = set()
         self.previously_finished: set[str] = set()
+        self.results: dict[str, int] = {}      # return code of each finished store/load, by request
 
     def _block_hashes_to_keys(self, block_hashes: list[bytes]) -> list[bytes]:
         return list(striding_block_hashes(block_hashes, self.blocks_in_chunk))
@@ -184,14 +188,19 @@ class WorkerAdapter:
     def get_finished(self, finished_req_ids: set[str]) -> tuple[set[str] | None, set[str] | None]:
         finished_stores: set[str] = set()
         finished_loads: set[str] = set()
-        for rid, (fut, others) in list(self.store_futures.items()):
-            if fut.done():
-                finished_stores.add(rid)
-                finished_stores.update(others)
-        for rid, (fut, others) in list(self.load_futures.items()):
-            if fut.done():
-                finished_loads.add(rid)
-                finished_loads.update(others)
+        for done, futs, what in ((finished_stores, self.store_futures, "store"),
+                                 (finished_loads, self.load_futures, "retrieve")):
+            for rid, (fut, others) in list(futs.items()):
+                if not fut.done():
+                    continue
+                done.add(rid)
+                done.update(others)
+                ret = fut.result() if fut.exception() is None else -1
+                for r in [rid, *others]:
+                    self.results[r] = ret
+                if ret != 0:   # reported but still finished, as the reference does (adaptor.py:243-265)
+                    logger.error("Something went wrong when processing the %s request for request_id=%s, "
+                                 "result=%s", what, rid, ret)
         for rid in finished_stores:
             self.store_futures.pop(rid, None)
         for rid in finished_loads:

@@ -1,0 +1,131 @@
+"""Scheduler side of the vLLM connector (CrossCacheConnector) against an
+in-process cache on the explicit CPU backend: lookup -> matched tokens,
+tracker states, and the chunk-granular STORE / RETRIEVE metadata of
+CrossCache's python/crosscache_connector.py:205-294, 490-661."""
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+
+vllm_base = pytest.importorskip("vllm.distributed.kv_transfer.kv_connector.v1.base")
+
+from demo_b200 import cache as cc  # noqa: E402
+from demo_b200._lib import CACHE_BACKEND_MEM  # noqa: E402
+from demo_b200.connector import (CacheConnectorMetadata, CacheRequestState,  # noqa: E402
+                                 CrossCacheConnector)
+from oracle import blockhash as bh  # noqa: E402
+
+BS = 16
+
+
+class _KVT:
+    def __init__(self):
+        self.kv_connector_extra_config = {}
+
+    def get_from_extra_config(self, key, default):
+        return self.kv_connector_extra_config.get(key, default)
+
+
+def _cfg():
+    return SimpleNamespace(kv_transfer_config=_KVT(), model_config=SimpleNamespace(model="m"),
+                           parallel_config=SimpleNamespace(world_size=1, rank=0),
+                           cache_config=SimpleNamespace(block_size=BS))
+
+
+def _request(rid, ntok, seed):
+    toks = np.random.default_rng(seed).integers(0, 128256, ntok).tolist()
+    return SimpleNamespace(request_id=rid, all_token_ids=toks,
+                           block_hashes=bh.block_hashes(toks, BS, bh.none_hash("0")))
+
+
+class _Blocks:
+    def __init__(self, ids):
+        self.ids = list(ids)
+
+    def get_block_ids(self):
+        return (self.ids,)
+
+
+def _sched_out(new=(), cached=None):
+    cached = cached or SimpleNamespace(req_ids=[], new_block_ids=[], num_computed_tokens=[])
+    return SimpleNamespace(scheduled_new_reqs=[SimpleNamespace(req_id=r) for r, _ in new],
+                           num_scheduled_tokens={r: n for r, n in new}, scheduled_cached_reqs=cached)
+
+
+@pytest.fixture
+def sched():
+    # a MEM-backend worker of model "m" holding the stored chunks
+    nb, unit = 256, 64
+    layers = [np.zeros(nb * BS * unit, np.uint8) for _ in range(2)]
+    cc.init(256, 8 * 2 * 1 * 256 * unit, None, CACHE_BACKEND_MEM)
+    lay = cc.KVLayout(1, nb, BS, 32, 2, 2)
+    w = cc.Worker("m", lay, [layers[0].ctypes.data], [layers[1].ctypes.data])
+    w.register()
+    conn = CrossCacheConnector(_cfg(), vllm_base.KVConnectorRole.SCHEDULER)
+    conn.scheduler_adapter.bind_worker(w)
+    yield conn, w
+    w.unregister()
+    cc.exit()
+
+
+def test_lookup_alloc_and_retrieve_store_metadata(sched):
+    conn, w = sched
+    req = _request("A", 1024, 1)                     # 64 blocks = 4 chunks
+    keys = bh.chunk_keys(req.block_hashes, 256 // BS)
+    assert w.store(keys[:2], np.arange(32)) == 0    # first 2 chunks cached
+    n, load_async = conn.get_num_new_matched_tokens(req, 0)
+    assert (n, load_async) == (512, True)
+    conn.update_state_after_alloc(req, _Blocks(range(100, 164)), 512)
+    t = conn.request_trackers["A"]
+    assert t.state == CacheRequestState.WAITING_FOR_LOAD
+    assert (t.num_vllm_hit_blocks, t.num_cache_hit_blocks, t.num_stored_blocks) == (0, 32, 32)
+    meta = conn.build_connector_meta(_sched_out(new=[("A", 1024)]))
+    assert isinstance(meta, CacheConnectorMetadata)
+    kinds = [(m.direction, len(m.op)) for m in meta.requests]
+    assert kinds == [("RETRIEVE", 32), ("STORE", 32)]
+    ret, store = meta.requests
+    assert ret.op.block_ids == list(range(100, 132))
+    assert ret.op.block_hashes == req.block_hashes[:32]
+    assert store.op.block_ids == list(range(132, 164))
+    assert store.op.block_hashes == req.block_hashes[32:64]
+    assert t.state == CacheRequestState.READY
+    assert conn.request_finished(req, []) == (True, None)
+    assert "A" not in conn.request_trackers
+
+
+def test_partial_vllm_hit_retrieves_from_chunk_boundary(sched):
+    conn, w = sched
+    req = _request("B", 1024, 2)
+    keys = bh.chunk_keys(req.block_hashes, 256 // BS)
+    assert w.store(keys[:3], np.arange(48)) == 0     # 3 chunks cached = 48 blocks
+    # vLLM already holds 20 blocks (320 tokens): load from chunk 1 (block 16)
+    n, load_async = conn.get_num_new_matched_tokens(req, 320)
+    assert (n, load_async) == (768 - 320, True)
+    conn.update_state_after_alloc(req, _Blocks(range(64)), 448)
+    meta = conn.build_connector_meta(_sched_out())
+    (ret,) = meta.requests
+    assert ret.direction == "RETRIEVE"
+    assert ret.op.block_ids == list(range(16, 48))
+    assert ret.op.block_hashes == req.block_hashes[16:48]
+
+
+def test_miss_goes_ready_and_stores_whole_chunks_only(sched):
+    conn, _ = sched
+    req = _request("C", 700, 3)                      # 43 full blocks
+    assert conn.get_num_new_matched_tokens(req, 0) == (0, False)
+    conn.update_state_after_alloc(req, _Blocks(range(10, 54)), 0)
+    assert conn.request_trackers["C"].state == CacheRequestState.READY
+    # 600 tokens scheduled -> 37 full blocks -> 2 whole chunks (32 blocks) stored
+    meta = conn.build_connector_meta(_sched_out(new=[("C", 600)]))
+    (st,) = meta.requests
+    assert st.direction == "STORE" and st.op.block_ids == list(range(10, 42))
+    # next step: a cached-request update adds tokens; no new whole chunk yet
+    cached = SimpleNamespace(req_ids=["C"], new_block_ids=[None], num_computed_tokens=[100])
+    meta2 = conn.build_connector_meta(_sched_out(cached=cached))
+    assert len(meta2) == 0
+
+
+def test_unbound_scheduler_reports_no_hits():
+    conn = CrossCacheConnector(_cfg(), vllm_base.KVConnectorRole.SCHEDULER)
+    req = _request("D", 512, 4)
+    assert conn.get_num_new_matched_tokens(req, 0) == (0, False)
