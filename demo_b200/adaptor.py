@@ -10,13 +10,12 @@ get_finished reports completion, exactly as the reference's futures do.
 """
 from __future__ import annotations
 
+import logging
 import threading
 from concurrent.futures import Future, ThreadPoolExecutor
 from dataclasses import dataclass
 from itertools import islice
 from typing import Iterable
-
-import logging
 
 import numpy as np
 import torch
