@@ -550,7 +550,7 @@ def main() -> None:
     import torch.distributed as dist
 
     from demo_b200 import cache as cc
-    from demo_b200._lib import KvCopyDesc, lib
+    from demo_b200._lib import KVCOPY_FLAG_BULK, KvCopyDesc, lib
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -654,7 +654,8 @@ def main() -> None:
         return KvCopyDesc(layer_k=kp_d.data_ptr(), layer_v=vp_d.data_ptr(), records=rec_ptrs.data_ptr(),
                           slots=None, block_ids=bids.data_ptr() + first * bpc * 8, error=err.data_ptr(),
                           page_buffer_size=n_blocks * BS, unit_bytes=unit, num_tokens=CHUNK,
-                          block_size=BS, num_layers=n_layers, num_records=n, direction=direction)
+                          block_size=BS, num_layers=n_layers, num_records=n, direction=direction,
+                          flags=KVCOPY_FLAG_BULK)
 
     batches = [(i * batch, min(batch, nrec - i * batch)) for i in range(nbatch)]
     d_pairs = [(desc(b_save, f, n, 1), desc(b_load, f, n, 0)) for f, n in batches]

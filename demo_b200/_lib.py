@@ -16,6 +16,9 @@ CACHE_BACKEND_MEM = 1
 
 KVCOPY_ERR_SLOT_RANGE = 0x1
 KVCOPY_ERR_NULL_LAYER = 0x2
+KVCOPY_ERR_TIMEOUT = 0x4
+KVCOPY_ERR_ALIGN = 0x8
+KVCOPY_FLAG_BULK = 0x1
 KVHASH_MAX_BLOCK_SIZE = 8192
 
 
@@ -104,6 +107,7 @@ class KvCopyDesc(C.Structure):
         ("num_layers", C.c_uint32),
         ("num_records", C.c_uint32),
         ("direction", C.c_int32),
+        ("flags", C.c_uint32),
     ]
 
 

@@ -521,6 +521,21 @@ private:
         set.opened.clear();
     }
 
+    /* true when every layer base registered under this device array is 16-byte aligned */
+    bool layers_aligned(const void *dptrs)
+    {
+        if (!dptrs)
+            return true;
+        std::lock_guard<std::mutex> g(reg_mu_);
+        auto it = ipc_.find(const_cast<void *>(dptrs));
+        if (it == ipc_.end())
+            return false;
+        for (uint64_t p : it->second.host_ptrs)
+            if (p % 16)
+                return false;
+        return true;
+    }
+
     int run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch *b);
     int finish(Lane *l, cudaStream_t last, int ret);
 
@@ -603,6 +618,15 @@ int CudaAdaptor::run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch 
     d.block_size = b->block_size;
     d.num_layers = b->num_layers;
     d.direction = save ? 1 : 0;
+    /* TMA bulk copies need HBM records (staging or device records) and
+     * 16-byte aligned bases; mapped host records keep the register path */
+    bool recs_aligned = true;
+    if (device_recs)
+        for (uint32_t r = 0; r < R; r++)
+            recs_aligned = recs_aligned && ((uintptr_t)b->records[r] % 16 == 0);
+    if ((device_recs || !direct) && recs_aligned && layers_aligned(b->keys_ptrs) &&
+        layers_aligned(b->value_ptrs))
+        d.flags = KVCOPY_FLAG_BULK;
 
     if (direct) {
         d.block_ids = l->d_meta;

@@ -28,6 +28,8 @@
 
 #include <cerrno>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace {
@@ -249,6 +251,253 @@ int launch_dir(const Params &p, int vec, cudaStream_t s)
     return launch_vec<TO_RECORD, WideShape>(p, vec, s);
 }
 
+/* ------------------------------------------------------------------------
+ * TMA bulk-copy path (KVCOPY_FLAG_BULK, block-id mode).
+ *
+ * A tile is up to 32 KiB of one (record, K/V, layer): whole paged blocks,
+ * each one contiguous run of block_size * unit bytes on the paged side and
+ * consecutive on the record side.  One thread per CTA drives a ring of
+ * kBulkStages shared-memory stages: cp.async.bulk global->shared for every
+ * run of a tile (completion counted in bytes on the stage's mbarrier), then
+ * one cp.async.bulk shared->global of the stage (scatter: the reverse), with
+ * up to kBulkStages-1 tiles loading while the previous one stores.  The data
+ * never passes through registers.  Every mbarrier wait is bounded: after
+ * kBulkSpinLimit polls the kernel sets KVCOPY_ERR_TIMEOUT, waits (bounded) for
+ * its other loads in flight and for its stores, and returns.
+ * ---------------------------------------------------------------------- */
+constexpr uint32_t kBulkTileBytes = 32768;
+constexpr int kBulkStages = 4;
+constexpr uint32_t kBulkSpinLimit = 1u << 24;   /* polls of ~128 ns back-off: ~2 s */
+
+struct BulkParams {
+    const uint64_t *layer_k;
+    const uint64_t *layer_v;
+    const uint64_t *records;
+    const uint64_t *block_ids;
+    int32_t *error;
+    uint64_t num_blocks;        /* paged blocks per layer */
+    uint64_t run_bytes;         /* block_size * unit */
+    uint64_t layer_rec_bytes;   /* num_tokens * unit: one layer of one record part */
+    uint32_t bpr;               /* blocks per record */
+    uint32_t gpt;               /* blocks per tile */
+    uint32_t num_layers;
+    uint32_t num_kv;
+    uint32_t num_tiles;
+    FastDiv div_tpl, div_layers, div_kv;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+__device__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity)
+{
+    for (uint32_t i = 0; i < kBulkSpinLimit; i++) {
+        if (mbar_try_wait(bar, parity))
+            return true;
+        if (i > 32)
+            __nanosleep(128);
+    }
+    return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void *sdst, const void *gsrc, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(sdst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void bulk_s2g(void *gdst, const void *ssrc, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(gdst), "r"(smem_u32(ssrc)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+struct BulkTile {
+    uint8_t *layer;
+    uint8_t *rec;
+    const uint64_t *bids;
+    uint32_t nb;
+};
+
+__device__ __forceinline__ BulkTile bulk_decode(const BulkParams &p, uint32_t w)
+{
+    const uint32_t tpl = p.div_tpl.d;
+    uint32_t w1 = fdiv(w, p.div_tpl);
+    uint32_t g = w - w1 * tpl;
+    uint32_t w2 = fdiv(w1, p.div_layers);
+    uint32_t l = w1 - w2 * p.num_layers;
+    uint32_t r = fdiv(w2, p.div_kv);
+    uint32_t kv = w2 - r * p.num_kv;
+    BulkTile t;
+    uint32_t b0 = g * p.gpt;
+    t.nb = min(p.gpt, p.bpr - b0);
+    t.layer = reinterpret_cast<uint8_t *>((kv ? p.layer_v : p.layer_k)[l]);
+    t.rec = reinterpret_cast<uint8_t *>(p.records[r]) + ((uint64_t)kv * p.num_layers + l) * p.layer_rec_bytes +
+            (uint64_t)b0 * p.run_bytes;
+    t.bids = p.block_ids + (uint64_t)r * p.bpr + b0;
+    return t;
+}
+
+template <bool TO_RECORD>
+__global__ void __launch_bounds__(32, 1) kv_copy_bulk_kernel(const BulkParams p)
+{
+    extern __shared__ __align__(128) uint8_t bulk_smem[];
+    __shared__ __align__(8) uint64_t bars[kBulkStages];
+    if (threadIdx.x != 0)
+        return;
+    for (int s = 0; s < kBulkStages; s++)
+        mbar_init(&bars[s], 1);
+    mbar_fence_init();
+
+    const uint32_t n_my = p.num_tiles > blockIdx.x ? (p.num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    const uint32_t run = (uint32_t)p.run_bytes;
+
+    /* start the loads of my k-th tile into stage s; false when a base is unusable */
+    auto issue_load = [&](uint32_t k, int s) {
+        BulkTile t = bulk_decode(p, blockIdx.x + k * gridDim.x);
+        uint8_t *stage = bulk_smem + (uint32_t)s * kBulkTileBytes;
+        bool bad_base = !t.layer || ((reinterpret_cast<uintptr_t>(t.layer) | reinterpret_cast<uintptr_t>(t.rec)) & 15);
+        if (bad_base) {
+            if (p.error)
+                atomicOr(p.error, t.layer ? KVCOPY_ERR_ALIGN : KVCOPY_ERR_NULL_LAYER);
+            mbar_expect_tx(&bars[s], 0);
+            return;
+        }
+        if (TO_RECORD) {
+            uint32_t bytes = 0;
+            for (uint32_t j = 0; j < t.nb; j++)
+                if (t.bids[j] < p.num_blocks)
+                    bytes += run;
+            mbar_expect_tx(&bars[s], bytes);
+            for (uint32_t j = 0; j < t.nb; j++) {
+                uint64_t bid = t.bids[j];
+                if (bid < p.num_blocks)
+                    bulk_g2s(stage + j * run, t.layer + bid * p.run_bytes, run, &bars[s]);
+                else if (p.error)
+                    atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
+            }
+        } else {
+            mbar_expect_tx(&bars[s], t.nb * run);
+            bulk_g2s(stage, t.rec, t.nb * run, &bars[s]);
+        }
+    };
+    /* store my k-th tile from stage s (one bulk group) */
+    auto issue_store = [&](uint32_t k, int s) {
+        BulkTile t = bulk_decode(p, blockIdx.x + k * gridDim.x);
+        uint8_t *stage = bulk_smem + (uint32_t)s * kBulkTileBytes;
+        bool bad_base = !t.layer || ((reinterpret_cast<uintptr_t>(t.layer) | reinterpret_cast<uintptr_t>(t.rec)) & 15);
+        if (!bad_base) {
+            if (TO_RECORD) {
+                bulk_s2g(t.rec, stage, t.nb * run);
+            } else {
+                for (uint32_t j = 0; j < t.nb; j++) {
+                    uint64_t bid = t.bids[j];
+                    if (bid < p.num_blocks)
+                        bulk_s2g(t.layer + bid * p.run_bytes, stage + j * run, run);
+                    else if (p.error)
+                        atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
+                }
+            }
+        }
+        bulk_commit();
+    };
+
+    uint32_t issued = 0;
+    for (; issued < n_my && issued < (uint32_t)kBulkStages; issued++)
+        issue_load(issued, (int)issued);
+    for (uint32_t k = 0; k < n_my; k++) {
+        const int s = (int)(k % kBulkStages);
+        if (!mbar_wait_bounded(&bars[s], (k / kBulkStages) & 1)) {
+            if (p.error)
+                atomicOr(p.error, KVCOPY_ERR_TIMEOUT);
+            for (uint32_t j = k + 1; j < issued; j++)       /* loads still in flight */
+                mbar_wait_bounded(&bars[j % kBulkStages], (j / kBulkStages) & 1);
+            break;
+        }
+        issue_store(k, s);
+        /* refill the stage of tile k-1 once its store has read the stage */
+        if (k >= 1 && issued < n_my) {
+            bulk_wait_read1();
+            issue_load(issued, (int)((k - 1) % kBulkStages));
+            issued++;
+        }
+    }
+    bulk_wait_all();
+}
+
+int launch_bulk(const BulkParams &bp, bool to_record, cudaStream_t stream)
+{
+    static int sm_count[64];
+    static std::once_flag once[64];
+    static cudaError_t attr_err[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return -EIO;
+    const int smem = kBulkStages * (int)kBulkTileBytes;
+    std::call_once(once[dev], [&] {
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        sm_count[dev] = sms > 0 ? sms : 1;
+        attr_err[dev] = cudaFuncSetAttribute(kv_copy_bulk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (attr_err[dev] == cudaSuccess)
+            attr_err[dev] = cudaFuncSetAttribute(kv_copy_bulk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
+    if (attr_err[dev] != cudaSuccess)
+        return -EIO;
+    uint32_t grid = (uint32_t)sm_count[dev];
+    if (grid > bp.num_tiles)
+        grid = bp.num_tiles;
+    if (to_record)
+        kv_copy_bulk_kernel<true><<<grid, 32, smem, stream>>>(bp);
+    else
+        kv_copy_bulk_kernel<false><<<grid, 32, smem, stream>>>(bp);
+    g_cc_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
+}
+
+/* CROSSCACHE_KVCOPY=lsu forces the register path even when the bulk path is allowed */
+bool bulk_allowed_by_env()
+{
+    static int v = -1;
+    if (v < 0) {
+        const char *s = getenv("CROSSCACHE_KVCOPY");
+        v = (s && !strcmp(s, "lsu")) ? 0 : 1;
+    }
+    return v == 1;
+}
+
 }  // namespace
 
 extern "C" uint64_t kv_copy_payload_bytes(const struct kv_copy_desc *d)
@@ -268,6 +517,35 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
         return 0;
     if (!d->slots && (!d->block_ids || d->num_tokens % d->block_size))
         return -EINVAL;
+
+    const uint64_t run_bytes = (uint64_t)d->block_size * d->unit_bytes;
+    if ((d->flags & KVCOPY_FLAG_BULK) && !d->slots && d->unit_bytes % 16 == 0 &&
+        run_bytes <= kBulkTileBytes && d->page_buffer_size % d->block_size == 0 && bulk_allowed_by_env()) {
+        BulkParams bp{};
+        bp.layer_k = d->layer_k;
+        bp.layer_v = d->layer_v;
+        bp.records = d->records;
+        bp.block_ids = d->block_ids;
+        bp.error = d->error;
+        bp.num_blocks = d->page_buffer_size / d->block_size;
+        bp.run_bytes = run_bytes;
+        bp.layer_rec_bytes = (uint64_t)d->num_tokens * d->unit_bytes;
+        bp.bpr = d->num_tokens / d->block_size;
+        bp.gpt = (uint32_t)(kBulkTileBytes / run_bytes);
+        if (bp.gpt > bp.bpr)
+            bp.gpt = bp.bpr;
+        bp.num_layers = d->num_layers;
+        bp.num_kv = d->layer_v ? 2 : 1;
+        const uint32_t tpl = (bp.bpr + bp.gpt - 1) / bp.gpt;
+        const uint64_t tiles = (uint64_t)d->num_records * bp.num_kv * bp.num_layers * tpl;
+        if (tiles >= (1ull << 31))
+            return -EINVAL;
+        bp.num_tiles = (uint32_t)tiles;
+        bp.div_tpl = make_fastdiv(tpl);
+        bp.div_layers = make_fastdiv(bp.num_layers);
+        bp.div_kv = make_fastdiv(bp.num_kv);
+        return launch_bulk(bp, d->direction != 0, static_cast<cudaStream_t>(stream));
+    }
 
     Params p{};
     p.layer_k = d->layer_k;

@@ -32,6 +32,18 @@ extern "C" {
 /* error bits the kernels OR into *error */
 #define KVCOPY_ERR_SLOT_RANGE   0x1   /* slot < 0 or slot >= page_buffer_size */
 #define KVCOPY_ERR_NULL_LAYER   0x2   /* a layer base pointer is 0            */
+#define KVCOPY_ERR_TIMEOUT      0x4   /* a bulk copy did not complete in time */
+#define KVCOPY_ERR_ALIGN        0x8   /* bulk path given a misaligned base    */
+
+/* kv_copy_desc.flags */
+#define KVCOPY_FLAG_BULK        0x1   /* the caller guarantees that records and
+                                       * layers are device memory (HBM) and that
+                                       * every layer base and record address is
+                                       * 16-byte aligned: block-id transfers
+                                       * whose block run (block_size * unit) is a
+                                       * multiple of 16 bytes and at most 32 KiB
+                                       * then use TMA bulk copies
+                                       * (cp.async.bulk) staged in shared memory */
 
 struct kv_copy_desc {
     const uint64_t *layer_k;     /* [num_layers] K layer base addresses      */
@@ -47,6 +59,7 @@ struct kv_copy_desc {
     uint32_t num_layers;
     uint32_t num_records;
     int32_t direction;           /* 1: paged -> record, 0: record -> paged   */
+    uint32_t flags;              /* KVCOPY_FLAG_*                            */
 };
 
 /* Launch the gather/scatter on `stream` (a cudaStream_t, NULL = legacy

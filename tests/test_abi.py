@@ -62,7 +62,7 @@ int main(void) {
   F(transfer_params, num_layers); F(transfer_params, hidden_dim_size); F(transfer_params, direction);
   S(transfer_batch); F(transfer_batch, records); F(transfer_batch, num_records);
   F(transfer_batch, num_layers); F(transfer_batch, direction);
-  S(kv_copy_desc); F(kv_copy_desc, page_buffer_size); F(kv_copy_desc, direction);
+  S(kv_copy_desc); F(kv_copy_desc, page_buffer_size); F(kv_copy_desc, direction); F(kv_copy_desc, flags);
   S(cache_stats);
   return 0;
 }

@@ -8,7 +8,8 @@ import numpy as np
 import pytest
 import torch
 
-from demo_b200._lib import KVCOPY_ERR_SLOT_RANGE, KvCopyDesc, TransferBatch, TransferParams, lib
+from demo_b200._lib import (KVCOPY_ERR_SLOT_RANGE, KVCOPY_FLAG_BULK, KvCopyDesc, TransferBatch,
+                            TransferParams, lib)
 from oracle import kvcopy as ok
 from tests.golden import gen
 from tests.gpu_util import DeviceKV, dsha, ptr_array, to_dev
@@ -16,7 +17,7 @@ from tests.gpu_util import DeviceKV, dsha, ptr_array, to_dev
 pytestmark = pytest.mark.gpu
 
 
-def launch(kv: DeviceKV, records, bids=None, slots=None, direction=1, err=None, num_records=None):
+def launch(kv: DeviceKV, records, bids=None, slots=None, direction=1, err=None, num_records=None, flags=0):
     case = kv.case
     recp = ptr_array(records)
     d = KvCopyDesc(layer_k=kv.kp.data_ptr(), layer_v=kv.vp.data_ptr() if kv.vp is not None else None,
@@ -28,19 +29,20 @@ def launch(kv: DeviceKV, records, bids=None, slots=None, direction=1, err=None, 
                    unit_bytes=gen.unit_of(case), num_tokens=case["chunk_size"],
                    block_size=case["block_size"], num_layers=case["num_layers"],
                    num_records=len(records) if num_records is None else num_records,
-                   direction=direction)
+                   direction=direction, flags=flags)
     ret = lib.kv_copy_launch(C.byref(d), C.c_void_p(torch.cuda.current_stream().cuda_stream))
     torch.cuda.synchronize()
     return ret
 
 
+@pytest.mark.parametrize("flags", [0, KVCOPY_FLAG_BULK], ids=["lsu", "bulk"])
 @pytest.mark.parametrize("case", gen.KV_CASES, ids=lambda c: c["name"])
-def test_gather_block_mode_matches_reference_golden(case, golden_records):
+def test_gather_block_mode_matches_reference_golden(case, flags, golden_records):
     kv = DeviceKV(case)
     bids = gen.block_ids(case)
     recs = [torch.zeros(gen.record_bytes(case), dtype=torch.uint8, device="cuda") for _ in range(case["chunks"])]
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    assert launch(kv, recs, bids=to_dev(bids.astype(np.int64)), err=err) == 0
+    assert launch(kv, recs, bids=to_dev(bids.astype(np.int64)), err=err, flags=flags) == 0
     assert int(err.item()) == 0
     assert [dsha(r) for r in recs] == golden_records[case["name"]]["record_sha256"]
 
@@ -58,12 +60,13 @@ def test_gather_slot_mode_matches_oracle(case):
         assert np.array_equal(r.cpu().numpy(), e)
 
 
+@pytest.mark.parametrize("flags", [0, KVCOPY_FLAG_BULK], ids=["lsu", "bulk"])
 @pytest.mark.parametrize("case", gen.KV_CASES, ids=lambda c: c["name"])
-def test_scatter_matches_reference_golden(case, golden_records):
+def test_scatter_matches_reference_golden(case, flags, golden_records):
     kv = DeviceKV(case, zero=True)
     bids2 = gen.block_ids(case, seed_offset=1)
     recs = [to_dev(r) for r in gen.records_for_scatter(case)]
-    assert launch(kv, recs, bids=to_dev(bids2.astype(np.int64)), direction=0) == 0
+    assert launch(kv, recs, bids=to_dev(bids2.astype(np.int64)), direction=0, flags=flags) == 0
     g = golden_records[case["name"]]
     assert [dsha(t) for t in kv.k] == g["scatter_k_sha256"]
     if kv.v is not None:
@@ -98,7 +101,8 @@ def test_random_slots_and_unaligned_bases_match_oracle():
             assert np.array_equal(recs[i].cpu().numpy(), e), (trial, i)
 
 
-def test_out_of_range_block_sets_error_and_copies_the_rest():
+@pytest.mark.parametrize("flags", [0, KVCOPY_FLAG_BULK], ids=["lsu", "bulk"])
+def test_out_of_range_block_sets_error_and_copies_the_rest(flags):
     case = gen.KV_CASES[1]
     kv = DeviceKV(case)
     bids = gen.block_ids(case).astype(np.int64)
@@ -106,7 +110,7 @@ def test_out_of_range_block_sets_error_and_copies_the_rest():
     bad[3] = case["num_blocks"]              # one block id past the end
     recs = [torch.zeros(gen.record_bytes(case), dtype=torch.uint8, device="cuda") for _ in range(case["chunks"])]
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    assert launch(kv, recs, bids=to_dev(bad), err=err) == 0
+    assert launch(kv, recs, bids=to_dev(bad), err=err, flags=flags) == 0
     assert int(err.item()) & KVCOPY_ERR_SLOT_RANGE
     k, v = gen.paged_layers(case)
     exp = ok.gather(k, v, bids, case["chunk_size"], case["block_size"], gen.unit_of(case))
@@ -298,6 +302,48 @@ def test_staging_ring_many_records_larger_than_ring(cuda_adaptor):
     assert all(np.array_equal(a, b) for a, b in zip(kh, ek))
     assert all(np.array_equal(a, b) for a, b in zip(vh, ev))
     lib.free_pinned_ptr(cuda_adaptor, host, size)
+
+
+def test_bulk_scatter_skips_bad_block_and_writes_the_rest():
+    case = gen.KV_CASES[4]                  # 256-byte units: 8 blocks per bulk tile
+    kv = DeviceKV(case, zero=True)
+    bids = gen.block_ids(case).astype(np.int64)
+    bad = bids.copy()
+    bad[5] = case["num_blocks"] + 1
+    recs = [to_dev(r) for r in gen.records_for_scatter(case)]
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert launch(kv, recs, bids=to_dev(bad), err=err, direction=0, flags=KVCOPY_FLAG_BULK) == 0
+    assert int(err.item()) & KVCOPY_ERR_SLOT_RANGE
+    # every other block holds exactly what the oracle writes with the good table;
+    # the block the bad id replaced is never written
+    ek, ev = gen.paged_layers(case, zero=True)
+    ok.scatter(gen.records_for_scatter(case), ek, ev, bids.astype(np.uint64), case["chunk_size"],
+               case["block_size"], gen.unit_of(case))
+    kh, vh = kv.host()
+    blk = case["block_size"] * gen.unit_of(case)
+    keep = [int(b) for i, b in enumerate(bids) if i != 5]
+    for a, e in zip(kh + vh, ek + ev):
+        assert np.array_equal(a.reshape(-1, blk)[keep], e.reshape(-1, blk)[keep])
+        assert not a.reshape(-1, blk)[int(bids[5])].any()
+
+
+def test_bulk_path_matches_lsu_on_large_random_tables():
+    """many tiles per CTA (pipeline wrap-around of the 4-stage ring)"""
+    case = dict(num_blocks=4096, block_size=16, chunk_size=256, num_layers=8, hidden=1024, elt=2,
+                kv=2, chunks=96, seed=77)
+    kv = DeviceKV(case)
+    bids = to_dev(gen.block_ids(case).astype(np.int64))
+    rb = gen.record_bytes(case)
+    a = [torch.zeros(rb, dtype=torch.uint8, device="cuda") for _ in range(case["chunks"])]
+    b = [torch.zeros(rb, dtype=torch.uint8, device="cuda") for _ in range(case["chunks"])]
+    assert launch(kv, a, bids=bids) == 0
+    assert launch(kv, b, bids=bids, flags=KVCOPY_FLAG_BULK) == 0
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    dst1, dst2 = DeviceKV(case, zero=True), DeviceKV(case, zero=True)
+    bids2 = to_dev(gen.block_ids(case, seed_offset=1).astype(np.int64))
+    assert launch(dst1, a, bids=bids2, direction=0) == 0
+    assert launch(dst2, a, bids=bids2, direction=0, flags=KVCOPY_FLAG_BULK) == 0
+    assert all(torch.equal(x, y) for x, y in zip(dst1.k + dst1.v, dst2.k + dst2.v))
 
 
 def test_kernel_launch_counter_advances(cuda_adaptor):
