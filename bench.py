@@ -84,9 +84,14 @@ def peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+def kvcopy_path() -> str:
+    """which gather/scatter kernel the value path runs (CROSSCACHE_KVCOPY=lsu forces registers)"""
+    return "lsu" if os.environ.get("CROSSCACHE_KVCOPY") == "lsu" else "bulk"
+
+
 def ncu_traffic() -> float | None:
-    """DRAM bytes per gather launch from the committed ncu summary, if any."""
-    f = ROOT / "profiles" / "kv_copy_gather.md"
+    """DRAM bytes per gather launch from the committed ncu summary of that kernel, if any."""
+    f = ROOT / "profiles" / ("kv_copy_gather.md" if kvcopy_path() == "lsu" else "kv_copy_bulk.md")
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
@@ -936,7 +941,10 @@ def main() -> None:
              "workload": f"reduced case for profiling: {n_layers} layers, {n_req} requests x {n_tok} tokens, "
                          f"{n_blocks} blocks/layer"},
             "record_batches_per_step": nbatch,
-            "roofline": {"bound": "hbm", "kernel": "kv_copy gather (save)", "achieved": round(achieved, 1),
+            "roofline": {"bound": "hbm",
+                         "kernel": ("kv_copy_kernel gather (16-byte register copies)" if kvcopy_path() == "lsu"
+                                    else "kv_copy_bulk_kernel gather (TMA cp.async.bulk via shared memory)"),
+                         "achieved": round(achieved, 1),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "peak_kind": peak_kind, "traffic": ncu_traffic(),
                          "algorithmic_bytes_per_launch": 2 * payload,
