@@ -257,7 +257,8 @@ def test_load_of_missing_key_fails_but_loads_the_hits(mem_cache):
 def test_pool_exhaustion_and_partial_chunks(mem_cache):
     case = gen.KV_CASES[0]
     mem_cache(2, case)
-    w = HostKV(case).worker()
+    kv = HostKV(case)          # owns the paged layers for the life of the worker
+    w = kv.worker()
     w.register()
     bpc = case["chunk_size"] // case["block_size"]
     keys = keys_for(3, seed=44)
@@ -307,7 +308,8 @@ def test_errors(mem_cache):
 def test_clear_and_stats(mem_cache):
     case = gen.KV_CASES[0]
     mem_cache(4, case)
-    w = HostKV(case).worker()
+    kv = HostKV(case)          # owns the paged layers for the life of the worker
+    w = kv.worker()
     w.register()
     bpc = case["chunk_size"] // case["block_size"]
     keys = keys_for(3, seed=55)
@@ -349,3 +351,28 @@ def test_per_chunk_transfer_abi_mem_adaptor(case):
             lib.close_ipc_keys(ad, dv)
     finally:
         lib.mem_adaptor_destroy(ad)
+
+
+def test_key_stride_wider_than_32_bytes_and_empty_calls(mem_cache):
+    """keys are compared on their first 32 bytes at a key_len stride
+    (reference cache.c:139-145,538-546); empty calls are no-ops"""
+    case = gen.KV_CASES[0]
+    mem_cache(8, case)
+    kv = HostKV(case)          # owns the paged layers for the life of the worker
+    w = kv.worker()
+    w.register()
+    bpc = case["chunk_size"] // case["block_size"]
+    k = keys_for(3, seed=90)
+    stride = 48
+    buf = b"".join(x + bytes([7]) * (stride - 32) for x in k)
+    bids = np.arange(3 * bpc, dtype=np.uint64)
+    assert cc.lib.cache_store(C.byref(w.ctx), buf, stride, bids.ctypes.data, len(bids)) == 0
+    assert cc.lib.cache_lookup(C.byref(w.ctx), buf, 3, stride) == 3 * stride
+    # the padding bytes are not part of the key
+    buf2 = b"".join(x + bytes([9]) * (stride - 32) for x in k)
+    assert cc.lib.cache_lookup(C.byref(w.ctx), buf2, 3, stride) == 3 * stride
+    assert w.lookup(k) == 3 * 32
+    assert cc.lib.cache_store(C.byref(w.ctx), buf, stride, bids.ctypes.data, 0) == 0
+    assert cc.lib.cache_load(C.byref(w.ctx), buf, stride, bids.ctypes.data, 0) == 0
+    assert cc.lib.cache_lookup(C.byref(w.ctx), buf, 0, stride) == 0
+    w.unregister()
