@@ -41,7 +41,7 @@ extern "C" {
                                        * every layer base and record address is
                                        * 16-byte aligned: block-id transfers
                                        * whose block run (block_size * unit) is a
-                                       * multiple of 16 bytes and at most 32 KiB
+                                       * multiple of 16 bytes from 8 to 32 KiB
                                        * then use TMA bulk copies
                                        * (cp.async.bulk) staged in shared memory */
 

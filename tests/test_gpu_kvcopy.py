@@ -305,7 +305,9 @@ def test_staging_ring_many_records_larger_than_ring(cuda_adaptor):
 
 
 def test_bulk_scatter_skips_bad_block_and_writes_the_rest():
-    case = gen.KV_CASES[4]                  # 256-byte units: 8 blocks per bulk tile
+    # 1 KiB units x 16 tokens = 16 KiB runs: 2 blocks per 32 KiB bulk tile
+    case = dict(num_blocks=128, block_size=16, chunk_size=256, num_layers=3, hidden=512, elt=2,
+                kv=2, chunks=4, seed=16)
     kv = DeviceKV(case, zero=True)
     bids = gen.block_ids(case).astype(np.int64)
     bad = bids.copy()
