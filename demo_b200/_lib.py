@@ -20,6 +20,7 @@ KVCOPY_ERR_TIMEOUT = 0x4
 KVCOPY_ERR_ALIGN = 0x8
 KVCOPY_FLAG_BULK = 0x1
 KVHASH_MAX_BLOCK_SIZE = 8192
+KVHASH_ALGOS = {"sha256": 0, "sha256_cbor": 1}
 
 
 class ModelInfo(C.Structure):
@@ -164,6 +165,11 @@ SIGNATURES: dict[str, tuple] = {
                                        C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p]),
     "kv_block_hash_host": (C.c_int64, [C.c_int, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
                                        C.c_void_p, C.c_void_p]),
+    "kv_block_hash_launch_algo": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                            C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_int,
+                                            C.c_void_p]),
+    "kv_block_hash_host_algo": (C.c_int64, [C.c_int, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
+                                            C.c_void_p, C.c_void_p, C.c_int]),
 }
 
 

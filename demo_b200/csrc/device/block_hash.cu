@@ -97,19 +97,80 @@ __device__ __forceinline__ void sha_compress(uint32_t st[8], const uint8_t *blk)
     st[4] += e; st[5] += f; st[6] += g; st[7] += h;
 }
 
-/* pickle encoding width of a token id: BININT1 (2), BININT2 (3), BININT (5) */
-__device__ __forceinline__ uint32_t token_width(int32_t v)
-{
-    return (v >= 0 && v <= 0xff) ? 2u : ((v >= 0 && v <= 0xffff) ? 3u : 5u);
-}
+/* The two serialisations of the (parent, tuple(tokens), None) triple that
+ * vLLM hashes with SHA-256: pickle protocol 5 (vllm/utils/hashing.py:26-41)
+ * and canonical CBOR (vllm/utils/hashing.py:43-57).  Each gives the header
+ * length, the header bytes (which carry the 32 parent bytes), the encoding of
+ * one int32 token, and the trailer. */
+struct PickleFmt {
+    static __device__ __forceinline__ uint32_t hdr_len(uint32_t bs) { return bs > 3 ? 47u : 46u; }
+    static constexpr uint32_t kTrailer = 6;   /* tuple op, MEMOIZE NONE TUPLE3 MEMOIZE STOP */
+    static __device__ __forceinline__ uint32_t header_byte(uint32_t p, uint32_t bs, uint64_t frame,
+                                                           const uint8_t *par)
+    {
+        if (p < 3)
+            return p == 0 ? 0x80u : (p == 1 ? 0x05u : 0x95u);     /* PROTO 5, FRAME */
+        if (p < 11)
+            return (uint32_t)(frame >> (8 * (p - 3))) & 0xffu;      /* frame length, LE */
+        if (p < 13)
+            return p == 11 ? 0x43u : 0x20u;                         /* SHORT_BINBYTES 32 */
+        if (p < 45)
+            return par[p - 13];
+        return p == 45 ? 0x94u : 0x28u;                             /* MEMOIZE, MARK */
+    }
+    /* BININT1 (2 bytes), BININT2 (3), BININT (5) */
+    static __device__ __forceinline__ uint32_t token_width(int32_t v)
+    {
+        return (v >= 0 && v <= 0xff) ? 2u : ((v >= 0 && v <= 0xffff) ? 3u : 5u);
+    }
+    static __device__ __forceinline__ uint32_t token_byte(int32_t v, uint32_t k)
+    {
+        const uint32_t u = (uint32_t)v;
+        const uint32_t op = (v >= 0 && v <= 0xff) ? 0x4bu : ((v >= 0 && v <= 0xffff) ? 0x4du : 0x4au);
+        return k == 0 ? op : (u >> (8 * (k - 1))) & 0xffu;
+    }
+    static __device__ __forceinline__ uint32_t trailer_byte(uint32_t k, uint32_t bs)
+    {
+        const uint32_t tuple_op = bs > 3 ? 0x74u : (0x84u + bs);    /* TUPLE or TUPLE1..3 */
+        return k == 0 ? tuple_op : (k == 1 ? 0x94u : (k == 2 ? 0x4eu : (k == 3 ? 0x87u : (k == 4 ? 0x94u : 0x2eu))));
+    }
+};
 
-/* byte k (0-based) of the pickle opcode + argument encoding token id v */
-__device__ __forceinline__ uint32_t token_byte(int32_t v, uint32_t k)
-{
-    const uint32_t u = (uint32_t)v;
-    const uint32_t op = (v >= 0 && v <= 0xff) ? 0x4bu : ((v >= 0 && v <= 0xffff) ? 0x4du : 0x4au);
-    return k == 0 ? op : (u >> (8 * (k - 1))) & 0xffu;
-}
+struct CborFmt {
+    /* array(3), bytes(32) head, parent, array(bs) head of 1, 2 or 3 bytes */
+    static __device__ __forceinline__ uint32_t arr_head(uint32_t bs) { return bs < 24 ? 1u : (bs < 256 ? 2u : 3u); }
+    static __device__ __forceinline__ uint32_t hdr_len(uint32_t bs) { return 35u + arr_head(bs); }
+    static constexpr uint32_t kTrailer = 1;   /* null */
+    static __device__ __forceinline__ uint32_t header_byte(uint32_t p, uint32_t bs, uint64_t, const uint8_t *par)
+    {
+        if (p < 3)
+            return p == 0 ? 0x83u : (p == 1 ? 0x58u : 0x20u);
+        if (p < 35)
+            return par[p - 3];
+        const uint32_t k = p - 35, h = arr_head(bs);
+        if (h == 1)
+            return 0x80u | bs;
+        if (h == 2)
+            return k == 0 ? 0x98u : bs;
+        return k == 0 ? 0x99u : (k == 1 ? (bs >> 8) & 0xffu : bs & 0xffu);
+    }
+    /* major type 0 (v >= 0) or 1 (argument -1 - v), shortest head */
+    static __device__ __forceinline__ uint32_t token_width(int32_t v)
+    {
+        const uint32_t n = v >= 0 ? (uint32_t)v : ~(uint32_t)v;
+        return n < 24 ? 1u : (n < 0x100 ? 2u : (n < 0x10000 ? 3u : 5u));
+    }
+    static __device__ __forceinline__ uint32_t token_byte(int32_t v, uint32_t k)
+    {
+        const uint32_t n = v >= 0 ? (uint32_t)v : ~(uint32_t)v;
+        const uint32_t major = v >= 0 ? 0x00u : 0x20u;
+        const uint32_t w = token_width(v);
+        if (k == 0)
+            return w == 1 ? (major | n) : (major | (w == 2 ? 24u : (w == 3 ? 25u : 26u)));
+        return (n >> (8 * (w - 1 - k))) & 0xffu;
+    }
+    static __device__ __forceinline__ uint32_t trailer_byte(uint32_t, uint32_t) { return 0xf6u; }
+};
 
 struct HashArgs {
     const int32_t *tokens;
@@ -130,6 +191,7 @@ struct HashArgs {
  * then the trailer and the SHA-256 padding -- and (3) after every write phase
  * compress each complete 64-byte block.  Control flow is uniform across the
  * warp, so every compression runs once per warp. */
+template <typename F>
 __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const HashArgs a)
 {
     __shared__ __align__(16) uint8_t ring_all[kWarpsPerCta][kRing];
@@ -155,9 +217,8 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
     __syncwarp();
 
     const uint32_t bs = a.block_size;
-    const uint32_t hdr_len = bs > 3 ? 47u : 46u;
-    const uint32_t fixed = hdr_len + 6;          /* + tuple op, MEMOIZE NONE TUPLE3 MEMOIZE STOP */
-    const uint32_t tuple_op = bs > 3 ? 0x74u : (0x84u + bs);
+    const uint32_t hdr_len = F::hdr_len(bs);
+    const uint32_t fixed = hdr_len + F::kTrailer;
     const int32_t *tok = a.tokens + a.tok_offsets[r];
     uint8_t *out = a.out + (uint64_t)a.out_offsets[r] * 32;
     const int nblk = a.num_blocks[r];
@@ -166,7 +227,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
         /* (1) message length */
         uint32_t wsum = 0;
         for (uint32_t j = lane; j < bs; j += 32)
-            wsum += token_width(tok[j]);
+            wsum += F::token_width(tok[j]);
         const uint32_t len = fixed + __reduce_add_sync(0xffffffffu, wsum);
         const uint32_t total = (len + 9 + 63) & ~63u;     /* padded length */
         const uint64_t frame = len - 11;
@@ -179,25 +240,13 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
         const uint32_t groups = (bs + 31) / 32;
         for (uint32_t ph = 0; ph <= groups + 1; ph++) {
             if (ph == 0) {
-                for (uint32_t p = lane; p < hdr_len; p += 32) {
-                    uint32_t v;
-                    if (p < 3)
-                        v = p == 0 ? 0x80u : (p == 1 ? 0x05u : 0x95u);
-                    else if (p < 11)
-                        v = (uint32_t)(frame >> (8 * (p - 3))) & 0xffu;
-                    else if (p < 13)
-                        v = p == 11 ? 0x43u : 0x20u;
-                    else if (p < 45)
-                        v = par[p - 13];
-                    else
-                        v = p == 45 ? 0x94u : 0x28u;
-                    ring[p % kRing] = (uint8_t)v;
-                }
+                for (uint32_t p = lane; p < hdr_len; p += 32)
+                    ring[p % kRing] = (uint8_t)F::header_byte(p, bs, frame, par);
                 pos = hdr_len;
             } else if (ph <= groups) {
                 const uint32_t j = (ph - 1) * 32 + lane;
                 const int32_t v = j < bs ? tok[j] : 0;
-                const uint32_t wdt = j < bs ? token_width(v) : 0u;
+                const uint32_t wdt = j < bs ? F::token_width(v) : 0u;
                 uint32_t incl = wdt;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
@@ -207,7 +256,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
                 }
                 const uint32_t off = pos + incl - wdt;
                 for (uint32_t k = 0; k < wdt; k++)
-                    ring[(off + k) % kRing] = (uint8_t)token_byte(v, k);
+                    ring[(off + k) % kRing] = (uint8_t)F::token_byte(v, k);
                 pos += __shfl_sync(0xffffffffu, incl, 31);
             } else {
                 /* trailer bytes, then 0x80, zeros, 64-bit big-endian bit length */
@@ -216,8 +265,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
                 for (uint32_t p = tail0 + lane; p < total; p += 32) {
                     uint32_t v;
                     if (p < len) {
-                        const uint32_t k = p - (len - 6);
-                        v = k == 0 ? tuple_op : (k == 1 ? 0x94u : (k == 2 ? 0x4eu : (k == 3 ? 0x87u : (k == 4 ? 0x94u : 0x2eu))));
+                        v = F::trailer_byte(p - (len - F::kTrailer), bs);
                     } else if (p == len) {
                         v = 0x80u;
                     } else if (p < total - 8) {
@@ -266,12 +314,14 @@ HostWorkspace g_ws[64];
 
 }  // namespace
 
-extern "C" int kv_block_hash_launch(const int32_t *tokens, const int64_t *tok_offsets,
-                                    const int32_t *num_blocks, const int64_t *out_offsets,
-                                    const uint8_t *parents, uint32_t num_req,
-                                    uint32_t block_size, const uint8_t *none_hash,
-                                    uint8_t *out, void *stream)
+extern "C" int kv_block_hash_launch_algo(const int32_t *tokens, const int64_t *tok_offsets,
+                                         const int32_t *num_blocks, const int64_t *out_offsets,
+                                         const uint8_t *parents, uint32_t num_req,
+                                         uint32_t block_size, const uint8_t *none_hash,
+                                         uint8_t *out, int algo, void *stream)
 {
+    if (algo != KVHASH_SHA256_PICKLE && algo != KVHASH_SHA256_CBOR)
+        return -EINVAL;
     if (!num_req)
         return 0;
     if (!tokens || !tok_offsets || !num_blocks || !out_offsets || !out || !block_size ||
@@ -291,15 +341,30 @@ extern "C" int kv_block_hash_launch(const int32_t *tokens, const int64_t *tok_of
             a.none_hash[k] = ((uint32_t)none_hash[4 * k] << 24) | ((uint32_t)none_hash[4 * k + 1] << 16) |
                              ((uint32_t)none_hash[4 * k + 2] << 8) | (uint32_t)none_hash[4 * k + 3];
     unsigned grid = (num_req + kWarpsPerCta - 1) / kWarpsPerCta;
-    block_hash_kernel<<<grid, kWarpsPerCta * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    if (algo == KVHASH_SHA256_CBOR)
+        block_hash_kernel<CborFmt><<<grid, kWarpsPerCta * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    else
+        block_hash_kernel<PickleFmt><<<grid, kWarpsPerCta * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
     g_cc_kernel_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
 }
 
-extern "C" int64_t kv_block_hash_host(int devid, const int32_t *tokens, const int64_t *tok_lens,
-                                      uint32_t num_req, uint32_t block_size,
-                                      const uint8_t *none_hash, uint8_t *out_hashes)
+extern "C" int kv_block_hash_launch(const int32_t *tokens, const int64_t *tok_offsets,
+                                    const int32_t *num_blocks, const int64_t *out_offsets,
+                                    const uint8_t *parents, uint32_t num_req,
+                                    uint32_t block_size, const uint8_t *none_hash,
+                                    uint8_t *out, void *stream)
 {
+    return kv_block_hash_launch_algo(tokens, tok_offsets, num_blocks, out_offsets, parents, num_req,
+                                     block_size, none_hash, out, KVHASH_SHA256_PICKLE, stream);
+}
+
+extern "C" int64_t kv_block_hash_host_algo(int devid, const int32_t *tokens, const int64_t *tok_lens,
+                                           uint32_t num_req, uint32_t block_size,
+                                           const uint8_t *none_hash, uint8_t *out_hashes, int algo)
+{
+    if (algo != KVHASH_SHA256_PICKLE && algo != KVHASH_SHA256_CBOR)
+        return -EINVAL;
     if (devid < 0 || devid >= 64 || !tok_lens || !none_hash || !out_hashes || !block_size ||
         block_size > KVHASH_MAX_BLOCK_SIZE)
         return -EINVAL;
@@ -353,11 +418,11 @@ extern "C" int64_t kv_block_hash_host(int devid, const int32_t *tokens, const in
         cudaMemcpyAsync(b + o_ooff, ooff.data(), num_req * 8, cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(b + o_nblk, nblk.data(), num_req * 4, cudaMemcpyHostToDevice, s) != cudaSuccess)
         ret = -EIO;
-    if (ret > 0 && kv_block_hash_launch(reinterpret_cast<int32_t *>(b + o_tok),
-                                        reinterpret_cast<int64_t *>(b + o_toff),
-                                        reinterpret_cast<int32_t *>(b + o_nblk),
-                                        reinterpret_cast<int64_t *>(b + o_ooff), nullptr, num_req,
-                                        block_size, none_hash, b + o_out, s))
+    if (ret > 0 && kv_block_hash_launch_algo(reinterpret_cast<int32_t *>(b + o_tok),
+                                             reinterpret_cast<int64_t *>(b + o_toff),
+                                             reinterpret_cast<int32_t *>(b + o_nblk),
+                                             reinterpret_cast<int64_t *>(b + o_ooff), nullptr, num_req,
+                                             block_size, none_hash, b + o_out, algo, s))
         ret = -EIO;
     if (ret > 0 && cudaMemcpyAsync(out_hashes, b + o_out, (size_t)nout * 32, cudaMemcpyDeviceToHost, s) != cudaSuccess)
         ret = -EIO;
@@ -365,4 +430,12 @@ extern "C" int64_t kv_block_hash_host(int devid, const int32_t *tokens, const in
         ret = -EIO;
     cudaStreamDestroy(s);
     return ret;
+}
+
+extern "C" int64_t kv_block_hash_host(int devid, const int32_t *tokens, const int64_t *tok_lens,
+                                      uint32_t num_req, uint32_t block_size,
+                                      const uint8_t *none_hash, uint8_t *out_hashes)
+{
+    return kv_block_hash_host_algo(devid, tokens, tok_lens, num_req, block_size, none_hash, out_hashes,
+                                   KVHASH_SHA256_PICKLE);
 }

@@ -1,8 +1,8 @@
 """Device block hashing (include/kvhash.h) for torch token tensors.
 
 block_hashes() returns the same bytes as vLLM's hash_block_tokens with the
-sha256 hash function (vllm/v1/core/kv_cache_utils.py:541-570) for every full
-block of every request; chunk_keys() strides them the way CrossCache's
+sha256 or sha256_cbor hash function (vllm/v1/core/kv_cache_utils.py:541-570,
+vllm/utils/hashing.py:26-57) for every full block of every request; chunk_keys() strides them the way CrossCache's
 adaptor does (python/adaptor.py:32-40).
 """
 from __future__ import annotations
@@ -14,25 +14,29 @@ from typing import Sequence
 
 import torch
 
-from ._lib import lib
+from ._lib import KVHASH_ALGOS, lib
 
 
-def none_hash_for_seed(seed: str | None = None) -> bytes:
+def none_hash_for_seed(seed: str | None = None, algo: str = "sha256") -> bytes:
     """NONE_HASH as vLLM's init_none_hash derives it from PYTHONHASHSEED
-    (kv_cache_utils.py:97-112): sha256 of the pickled seed string; random
-    when no seed is set."""
+    (kv_cache_utils.py:97-112): the hash function applied to the seed string
+    (pickled for "sha256", canonical CBOR for "sha256_cbor"); random when no
+    seed is set."""
     import pickle
 
     seed = os.getenv("PYTHONHASHSEED") if seed is None else seed
     if seed is None:
         return os.urandom(32)
+    if algo == "sha256_cbor":
+        import cbor2
+        return hashlib.sha256(cbor2.dumps(seed, canonical=True)).digest()
     return hashlib.sha256(pickle.dumps(seed, protocol=pickle.HIGHEST_PROTOCOL)).digest()
 
 
 def block_hashes_device(tokens: torch.Tensor, tok_offsets: torch.Tensor, num_blocks: torch.Tensor,
                         out_offsets: torch.Tensor, block_size: int, none_hash: bytes,
                         out: torch.Tensor, parents: torch.Tensor | None = None,
-                        stream: torch.cuda.Stream | None = None) -> None:
+                        stream: torch.cuda.Stream | None = None, algo: str = "sha256") -> None:
     """Launch the hash kernel on device tensors (int32 tokens, int64 offsets,
     int32 block counts, uint8 [total, 32] output).  Asynchronous."""
     for t, dt in ((tokens, torch.int32), (tok_offsets, torch.int64), (num_blocks, torch.int32),
@@ -42,17 +46,17 @@ def block_hashes_device(tokens: torch.Tensor, tok_offsets: torch.Tensor, num_blo
     if len(none_hash) != 32:
         raise ValueError("none_hash must be 32 bytes")
     s = stream if stream is not None else torch.cuda.current_stream(tokens.device)
-    ret = lib.kv_block_hash_launch(tokens.data_ptr(), tok_offsets.data_ptr(), num_blocks.data_ptr(),
-                                   out_offsets.data_ptr(),
-                                   parents.data_ptr() if parents is not None else None,
-                                   tok_offsets.numel(), block_size, none_hash, out.data_ptr(),
-                                   C.c_void_p(s.cuda_stream))
+    ret = lib.kv_block_hash_launch_algo(tokens.data_ptr(), tok_offsets.data_ptr(), num_blocks.data_ptr(),
+                                        out_offsets.data_ptr(),
+                                        parents.data_ptr() if parents is not None else None,
+                                        tok_offsets.numel(), block_size, none_hash, out.data_ptr(),
+                                        KVHASH_ALGOS[algo], C.c_void_p(s.cuda_stream))
     if ret:
         raise RuntimeError(f"kv_block_hash_launch failed: {ret}")
 
 
 def block_hashes(token_lists: Sequence[Sequence[int]], block_size: int, none_hash: bytes,
-                 device: int = 0) -> list[list[bytes]]:
+                 device: int = 0, algo: str = "sha256") -> list[list[bytes]]:
     """Chained block hashes of each request (host lists in, host bytes out),
     computed on `device` through kv_block_hash_host."""
     import numpy as np
@@ -65,8 +69,8 @@ def block_hashes(token_lists: Sequence[Sequence[int]], block_size: int, none_has
     flat = flat.astype(np.int32)
     nblk = lens // block_size
     out = np.zeros((int(nblk.sum()), 32), dtype=np.uint8)
-    ret = lib.kv_block_hash_host(device, flat.ctypes.data, lens.ctypes.data, len(lens), block_size,
-                                 none_hash, out.ctypes.data)
+    ret = lib.kv_block_hash_host_algo(device, flat.ctypes.data, lens.ctypes.data, len(lens), block_size,
+                                      none_hash, out.ctypes.data, KVHASH_ALGOS[algo])
     if ret < 0:
         raise RuntimeError(f"kv_block_hash_host failed: {ret}")
     res, off = [], 0

@@ -13,6 +13,9 @@
  *
  * The kernel serialises each block's pickle byte stream on the device and
  * runs SHA-256 (FIPS 180-4), one chain per request, requests in parallel.
+ * vLLM's other SHA-256 variant, sha256_cbor (vllm/utils/hashing.py:43-57,
+ * canonical CBOR of the same triple), is available through the *_algo entry
+ * points.
  * The chunk keys CrossCache sends to the server are every
  * (chunk_size / block_size)-th hash (python/adaptor.py:32-40).
  *
@@ -29,6 +32,12 @@ extern "C" {
 #endif
 
 #define KVHASH_MAX_BLOCK_SIZE 8192
+
+/* hash functions (vLLM's prefix_caching_hash_algo) */
+#define KVHASH_SHA256_PICKLE 0   /* "sha256": SHA-256 of pickle protocol 5 (default) */
+#define KVHASH_SHA256_CBOR   1   /* "sha256_cbor": SHA-256 of canonical CBOR
+                                  * (vllm/utils/hashing.py:43-57); NONE_HASH is
+                                  * then SHA-256 of the CBOR text string seed */
 
 /* Device-pointer form, asynchronous on `stream` (a cudaStream_t).
  *   tokens       int32 token ids, requests packed back to back
@@ -55,6 +64,19 @@ int64_t kv_block_hash_host(int devid, const int32_t *tokens,
                            const int64_t *tok_lens, uint32_t num_req,
                            uint32_t block_size, const uint8_t *none_hash,
                            uint8_t *out_hashes);
+
+/* The same two entry points with an explicit hash function (KVHASH_*); the
+ * forms above are KVHASH_SHA256_PICKLE.  -EINVAL for an unknown algo. */
+int kv_block_hash_launch_algo(const int32_t *tokens, const int64_t *tok_offsets,
+                              const int32_t *num_blocks, const int64_t *out_offsets,
+                              const uint8_t *parents, uint32_t num_req,
+                              uint32_t block_size, const uint8_t *none_hash,
+                              uint8_t *out, int algo, void *stream);
+
+int64_t kv_block_hash_host_algo(int devid, const int32_t *tokens,
+                                const int64_t *tok_lens, uint32_t num_req,
+                                uint32_t block_size, const uint8_t *none_hash,
+                                uint8_t *out_hashes, int algo);
 
 #ifdef __cplusplus
 }

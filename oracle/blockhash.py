@@ -8,6 +8,9 @@ block hash, the key CrossCache stores records under:
       NONE_HASH = hash_fn(PYTHONHASHSEED string)
   CrossCache python/adaptor.py:32-40  striding_block_hashes: chunk keys are
       the hashes of blocks bpc-1, 2*bpc-1, ...
+  vllm/utils/hashing.py:43-57  sha256_cbor: SHA-256 of cbor2.dumps(obj,
+      canonical=True) -- the same triple as a CBOR array (RFC 8949: shortest
+      heads, definite lengths)
 
 The pickle byte stream is written out here opcode by opcode (CPython
 _pickle.c: PROTO, FRAME, SHORT_BINBYTES, MEMOIZE, MARK, BININT1/BININT2/
@@ -52,9 +55,39 @@ def pickle_block(parent: bytes, tokens: Sequence[int]) -> bytes:
     return bytes([PROTO, 5, FRAME]) + struct.pack("<Q", len(body)) + bytes(body)
 
 
-def none_hash(seed: str) -> bytes:
-    """NONE_HASH for PYTHONHASHSEED=seed: sha256(pickle.dumps(seed, 5))."""
+def _cbor_head(major: int, n: int) -> bytes:
+    """RFC 8949 shortest head for major type `major` and argument n"""
+    if n < 24:
+        return bytes([major << 5 | n])
+    if n < 0x100:
+        return bytes([major << 5 | 24, n])
+    if n < 0x10000:
+        return bytes([major << 5 | 25]) + struct.pack(">H", n)
+    if n < 0x100000000:
+        return bytes([major << 5 | 26]) + struct.pack(">I", n)
+    return bytes([major << 5 | 27]) + struct.pack(">Q", n)
+
+
+def cbor_block(parent: bytes, tokens: Sequence[int]) -> bytes:
+    """cbor2.dumps((parent, tuple(tokens), None), canonical=True) for int32 tokens"""
+    if len(parent) != 32:
+        raise ValueError("parent must be 32 bytes")
+    out = bytearray(_cbor_head(4, 3)) + _cbor_head(2, 32) + parent + _cbor_head(4, len(tokens))
+    for v in tokens:
+        v = int(v)
+        if not -0x80000000 <= v <= 0x7FFFFFFF:
+            raise ValueError("token id outside int32")
+        out += _cbor_head(0, v) if v >= 0 else _cbor_head(1, -1 - v)
+    out.append(0xF6)                      # simple value null
+    return bytes(out)
+
+
+def none_hash(seed: str, algo: str = "sha256") -> bytes:
+    """NONE_HASH for PYTHONHASHSEED=seed: hash_fn(seed) -- sha256 of
+    pickle.dumps(seed, 5), or sha256 of the canonical CBOR text string."""
     b = seed.encode()
+    if algo == "sha256_cbor":
+        return hashlib.sha256(_cbor_head(3, len(b)) + b).digest()
     if len(b) >= 256:
         raise ValueError("seed too long for this restatement")
     # PROTO 5, FRAME, SHORT_BINUNICODE len data, MEMOIZE, STOP
@@ -63,12 +96,13 @@ def none_hash(seed: str) -> bytes:
     return hashlib.sha256(msg).digest()
 
 
-def block_hashes(tokens: Sequence[int], block_size: int, parent: bytes) -> list[bytes]:
+def block_hashes(tokens: Sequence[int], block_size: int, parent: bytes, algo: str = "sha256") -> list[bytes]:
     """Chained hashes of the full blocks of `tokens` starting from `parent`."""
+    ser = cbor_block if algo == "sha256_cbor" else pickle_block
     out = []
     h = parent
     for i in range(len(tokens) // block_size):
-        h = hashlib.sha256(pickle_block(h, tokens[i * block_size:(i + 1) * block_size])).digest()
+        h = hashlib.sha256(ser(h, tokens[i * block_size:(i + 1) * block_size])).digest()
         out.append(h)
     return out
 
@@ -78,5 +112,6 @@ def chunk_keys(hashes: Sequence[bytes], blocks_in_chunk: int) -> list[bytes]:
     return list(hashes[blocks_in_chunk - 1::blocks_in_chunk])
 
 
-def batch_block_hashes(requests: Iterable[Sequence[int]], block_size: int, parent: bytes) -> list[list[bytes]]:
-    return [block_hashes(t, block_size, parent) for t in requests]
+def batch_block_hashes(requests: Iterable[Sequence[int]], block_size: int, parent: bytes,
+                       algo: str = "sha256") -> list[list[bytes]]:
+    return [block_hashes(t, block_size, parent, algo) for t in requests]

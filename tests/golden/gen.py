@@ -80,13 +80,29 @@ HASH_CASES = [
     ("bs16_int32_extremes", 16, "42", "extremes"),
     ("bs128_mixed", 128, "3", (0, 300000, 3 * 128)),
 ]
+# the same token specs hashed with vLLM's sha256_cbor (appended after the
+# pickle cases so their generator seeds are unchanged)
+HASH_CASES_CBOR = [
+    ("cbor_bs16_llama3_vocab", 16, "0", (0, 128256, 8 * 16 + 3)),
+    ("cbor_bs16_small_ids", 16, "0", (0, 24, 4 * 16)),
+    ("cbor_bs16_boundaries", 16, "1234", "boundaries"),
+    ("cbor_bs16_int32_extremes", 16, "42", "extremes"),
+    ("cbor_bs1", 1, "0", (0, 300, 9)),
+    ("cbor_bs3", 3, "7", (0, 70000, 12)),
+    ("cbor_bs23", 23, "7", (0, 70000, 46)),
+    ("cbor_bs24", 24, "7", (0, 70000, 48)),
+    ("cbor_bs64_llama3_vocab", 64, "0", (0, 128256, 4 * 64)),
+    ("cbor_bs256", 256, "5", (0, 128256, 2 * 256)),
+    ("cbor_bs300", 300, "5", (-1000, 128256, 2 * 300)),
+]
 
 
 def hash_tokens(spec, case_index: int) -> list[int]:
     rng = np.random.default_rng(5000 + case_index)
     if spec == "boundaries":
-        base = [0, 1, 254, 255, 256, 257, 65534, 65535, 65536, 65537, 128255, 127, 128, 300, 70000, 5]
-        return base * 4
+        base = [0, 1, 254, 255, 256, 257, 65534, 65535, 65536, 65537, 128255, 127, 128, 300, 70000, 5,
+                23, 24, 25, 22]
+        return base[:16] * 3 + base[4:]
     if spec == "extremes":
         return [-2**31, -1, 2**31 - 1, 0, -256, 256, -65536, 65536,
                 -2, 2, 2**31 - 2, -(2**31) + 1, 255, -255, 65535, -65535] * 2

@@ -4,9 +4,10 @@
 
 block_hashes.json  chained block hashes computed by the INSTALLED vLLM
                    (vllm.v1.core.kv_cache_utils.hash_block_tokens with
-                   vllm.utils.hashing.sha256, NONE_HASH from init_none_hash
-                   under PYTHONHASHSEED=<seed>) -- the function CrossCache's
-                   keys come from (python/crosscache_connector.py:133).
+                   vllm.utils.hashing.sha256 and sha256_cbor, NONE_HASH from
+                   init_none_hash under PYTHONHASHSEED=<seed>) -- the function
+                   CrossCache's keys come from
+                   (python/crosscache_connector.py:133).
 kv_records.json    SHA-256 digests of records gathered, and of paged layers
                    after a scatter, by CrossCache's own MemAdaptor::
                    TransferKVCache (src/device/mem/mem.cpp:114-173) compiled
@@ -30,20 +31,22 @@ from tests.golden import gen  # noqa: E402
 
 
 def make_hashes() -> list[dict]:
-    from vllm.utils.hashing import sha256
+    from vllm.utils.hashing import sha256, sha256_cbor
     from vllm.v1.core import kv_cache_utils as kcu
 
     out = []
-    for i, (name, bs, seed, spec) in enumerate(gen.HASH_CASES):
+    cases = [(i, c, "sha256", sha256) for i, c in enumerate(gen.HASH_CASES)]
+    cases += [(100 + i, c, "sha256_cbor", sha256_cbor) for i, c in enumerate(gen.HASH_CASES_CBOR)]
+    for i, (name, bs, seed, spec), algo, fn in cases:
         os.environ["PYTHONHASHSEED"] = seed
-        kcu.init_none_hash(sha256)
+        kcu.init_none_hash(fn)
         tokens = gen.hash_tokens(spec, i)
         hashes = []
         parent = None
         for b in range(len(tokens) // bs):
-            parent = kcu.hash_block_tokens(sha256, parent, tokens[b * bs:(b + 1) * bs], None)
+            parent = kcu.hash_block_tokens(fn, parent, tokens[b * bs:(b + 1) * bs], None)
             hashes.append(bytes(parent).hex())
-        out.append(dict(name=name, block_size=bs, pythonhashseed=seed,
+        out.append(dict(name=name, algo=algo, block_size=bs, pythonhashseed=seed,
                         none_hash=bytes(kcu.NONE_HASH).hex(), tokens=tokens, hashes=hashes))
     return out
 

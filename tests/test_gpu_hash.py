@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 def test_golden_vectors_host_entry(golden_hashes):
     for case in golden_hashes:
         nh = bytes.fromhex(case["none_hash"])
-        got = hashing.block_hashes([case["tokens"]], case["block_size"], nh)[0]
+        got = hashing.block_hashes([case["tokens"]], case["block_size"], nh, algo=case["algo"])[0]
         assert [h.hex() for h in got] == case["hashes"], case["name"]
 
 
@@ -22,8 +22,8 @@ def test_golden_vectors_batched_device_entry(golden_hashes):
     chains of later cases continued from explicit parents"""
     by_bs = {}
     for c in golden_hashes:
-        by_bs.setdefault((c["block_size"], c["none_hash"]), []).append(c)
-    for (bs, nh_hex), cases in by_bs.items():
+        by_bs.setdefault((c["block_size"], c["none_hash"], c["algo"]), []).append(c)
+    for (bs, nh_hex, algo), cases in by_bs.items():
         toks = [c["tokens"] for c in cases]
         lens = [len(t) for t in toks]
         nblk = [n // bs for n in lens]
@@ -32,7 +32,7 @@ def test_golden_vectors_batched_device_entry(golden_hashes):
         ooff = torch.tensor(np.cumsum([0] + nblk[:-1]), dtype=torch.int64, device="cuda")
         nb = torch.tensor(nblk, dtype=torch.int32, device="cuda")
         out = torch.zeros(sum(nblk), 32, dtype=torch.uint8, device="cuda")
-        hashing.block_hashes_device(flat, toff, nb, ooff, bs, bytes.fromhex(nh_hex), out)
+        hashing.block_hashes_device(flat, toff, nb, ooff, bs, bytes.fromhex(nh_hex), out, algo=algo)
         torch.cuda.synchronize()
         got = [bytes(r) for r in out.cpu().numpy()]
         exp = [bytes.fromhex(h) for c in cases for h in c["hashes"]]
@@ -42,21 +42,23 @@ def test_golden_vectors_batched_device_entry(golden_hashes):
         toff2 = toff + bs
         nb2 = nb - 1
         out2 = torch.zeros_like(out)
-        hashing.block_hashes_device(flat, toff2, nb2, ooff, bs, bytes.fromhex(nh_hex), out2, parents=parents)
+        hashing.block_hashes_device(flat, toff2, nb2, ooff, bs, bytes.fromhex(nh_hex), out2, parents=parents,
+                                    algo=algo)
         torch.cuda.synchronize()
         for c, o, n in zip(cases, ooff.tolist(), nblk):
             assert [bytes(r).hex() for r in out2[o:o + n - 1].cpu().numpy()] == c["hashes"][1:]
 
 
+@pytest.mark.parametrize("algo", ["sha256", "sha256_cbor"])
 @pytest.mark.parametrize("bs", [16, 64])
-def test_random_batch_matches_oracle(bs):
+def test_random_batch_matches_oracle(bs, algo):
     rng = np.random.default_rng(bs)
-    reqs = [rng.integers(0, 128256, int(rng.integers(0, 40 * bs))).tolist() for _ in range(100)]
+    reqs = [rng.integers(-100, 128256, int(rng.integers(0, 40 * bs))).tolist() for _ in range(100)]
     reqs[3] = []                                       # empty request
     reqs[4] = reqs[4][: bs - 1]                        # no full block
-    nh = bh.none_hash("0")
-    got = hashing.block_hashes(reqs, bs, nh)
-    exp = bh.batch_block_hashes(reqs, bs, nh)
+    nh = bh.none_hash("0", algo)
+    got = hashing.block_hashes(reqs, bs, nh, algo=algo)
+    exp = bh.batch_block_hashes(reqs, bs, nh, algo)
     assert got == exp
 
 

@@ -13,12 +13,23 @@ from tests.golden import gen
 
 
 def test_hash_restatement_matches_vllm_golden(golden_hashes):
-    assert len(golden_hashes) == len(gen.HASH_CASES)
+    assert len(golden_hashes) == len(gen.HASH_CASES) + len(gen.HASH_CASES_CBOR)
+    assert {c["algo"] for c in golden_hashes} == {"sha256", "sha256_cbor"}
     for case in golden_hashes:
         nh = bytes.fromhex(case["none_hash"])
-        assert nh == bh.none_hash(case["pythonhashseed"]), case["name"]
-        got = bh.block_hashes(case["tokens"], case["block_size"], nh)
+        assert nh == bh.none_hash(case["pythonhashseed"], case["algo"]), case["name"]
+        got = bh.block_hashes(case["tokens"], case["block_size"], nh, case["algo"])
         assert [h.hex() for h in got] == case["hashes"], case["name"]
+
+
+@pytest.mark.parametrize("bs", [1, 3, 16, 23, 24, 255, 256, 300])
+def test_cbor_block_bytes_equal_cbor2(bs):
+    cbor2 = pytest.importorskip("cbor2")
+    rnd = random.Random(1000 + bs)
+    for lo, hi in [(0, 24), (0, 256), (0, 65536), (0, 128256), (-2**31, 2**31)]:
+        toks = [rnd.randrange(lo, hi) for _ in range(bs)]
+        parent = bytes(rnd.randrange(256) for _ in range(32))
+        assert bh.cbor_block(parent, toks) == cbor2.dumps((parent, tuple(toks), None), canonical=True)
 
 
 def test_golden_tokens_cover_pickle_int_widths(golden_hashes):
