@@ -117,7 +117,9 @@ class CacheStats(C.Structure):
 
     _fields_ = [(n, C.c_uint64) for n in (
         "records_total", "records_used", "lookups", "lookup_hits", "stored",
-        "store_dedup", "loaded", "load_misses", "evictions", "bytes_saved", "bytes_loaded")]
+        "store_dedup", "loaded", "load_misses", "evictions", "bytes_saved", "bytes_loaded",
+        "disk_writes", "disk_write_skips", "disk_write_errors", "disk_reads", "disk_read_errors",
+        "disk_lookup_hits", "bytes_written_disk", "bytes_read_disk")]
 
     def as_dict(self) -> dict:
         return {n: int(getattr(self, n)) for n, _ in self._fields_}
@@ -138,6 +140,7 @@ SIGNATURES: dict[str, tuple] = {
                                      C.c_uint32, C.c_void_p]),
     "cache_get_stats": (C.c_int, [C.POINTER(WorkerContext), C.POINTER(CacheStats)]),
     "cache_clear": (C.c_int, [C.POINTER(WorkerContext)]),
+    "cache_flush": (C.c_int, [C.POINTER(WorkerContext)]),
     # include/device.h
     "cuda_adaptor_create": (C.c_void_p, []),
     "cuda_adaptor_destroy": (None, [C.c_void_p]),

@@ -11,6 +11,7 @@ get_finished reports completion, exactly as the reference's futures do.
 from __future__ import annotations
 
 import logging
+import os
 import threading
 from concurrent.futures import Future, ThreadPoolExecutor
 from dataclasses import dataclass
@@ -30,13 +31,15 @@ _service_lock = threading.Lock()
 _service_refs = 0
 
 
-def ensure_cache(pool_size: int, chunk_size: int = CHUNK_SIZE) -> None:
+def ensure_cache(pool_size: int, chunk_size: int = CHUNK_SIZE, cache_dir: str | None = None) -> None:
     """Process-wide cache_init on first use (the reference's server does
-    cache_init once at start-up, src/main.c:388-413)."""
+    cache_init once at start-up, src/main.c:388-413).  The disk tier's
+    directory is `cache_dir`, else $CROSSCACHE_CACHEDIR (the reference
+    server's --cachedir, main.c:436-448); neither means memory only."""
     global _service_refs
     with _service_lock:
         if _service_refs == 0:
-            cc.init(chunk_size, pool_size, None)
+            cc.init(chunk_size, pool_size, cache_dir or os.getenv("CROSSCACHE_CACHEDIR") or None)
         _service_refs += 1
 
 

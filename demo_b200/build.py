@@ -29,6 +29,7 @@ C_SOURCES = [
     "infra/kvmap.c",
     "infra/threadpool.c",
     "cache/cache.c",
+    "cache/disk.c",
 ]
 CXX_SOURCES = [
     "device/device.cpp",

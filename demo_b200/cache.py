@@ -149,6 +149,12 @@ class Worker:
         if ret:
             raise CacheError("cache_clear", ret)
 
+    def flush(self) -> None:
+        """cache_flush: wait for the disk writes of every stored record."""
+        ret = lib.cache_flush(C.byref(self.ctx))
+        if ret:
+            raise CacheError("cache_flush", ret)
+
 
 def layout_from_kv_tensors(kv_caches, tp_heads: int | None = None) -> tuple[KVLayout, list[int], list[int] | None]:
     """Layout and per-layer K/V plane pointers of vLLM paged caches.

@@ -18,21 +18,38 @@
  *     (transfer_kvcache_batch) instead of one pipeline task per record;
  *   - eviction is deterministic LRU over unpinned records and fails with
  *     -ENOMEM instead of spinning when everything is in flight (:319-343);
- *   - records being loaded are pinned so eviction cannot recycle them;
- *   - the disk tier (:222-278) is not part of this build: a load of a key
- *     that is not in memory fails with -ENOENT.
+ *   - records being loaded are pinned so eviction cannot recycle them.
+ *
+ * Disk tier (enabled when cache_init gets a directory; cache.c:222-278,
+ * 471-504, 739-742, 759-787):
+ *   - every stored record is also written to a file (write-through, as the
+ *     reference's pipeline_io does), but behind the call: the store returns
+ *     once the record is in host memory and a pool of IO threads writes it
+ *     out, the record pinned until its file is complete.  cache_flush waits
+ *     for those writes;
+ *   - a lookup that misses in memory asks the disk (stat) and keeps walking
+ *     on a hit (reference lookup_file);
+ *   - a load reads the records missing from memory from their files in
+ *     parallel into pool records, then moves them in the same batched
+ *     host-to-device transfer as the memory hits; the read records stay
+ *     cached in memory (reference pipeline_io PIPELINE_START branch).
+ *   File naming and layout are in disk.h.
  */
 #include "cache.h"
 #include "device.h"
+#include "disk.h"
 
 #include "../infra/kvmap.h"
 #include "../infra/log.h"
 #include "../infra/mempool.h"
+#include "../infra/threadpool.h"
 
 #include <errno.h>
 #include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
+#include <unistd.h>
 
 #define KV_H_TO_D false
 #define KV_D_TO_H true
@@ -58,6 +75,11 @@ struct rt_entry {
     kvmap_t *map;
     struct cache_stats stats;
     pthread_mutex_t mu;
+    pthread_cond_t cv;         /* signalled when a disk write completes */
+
+    int dfd;                   /* namespace directory, -1 without disk tier */
+    uint32_t disk_pending;     /* write-behind jobs not yet finished */
+    int disk_err;              /* first write error since the last flush */
 
     struct rt_entry *next;
 };
@@ -68,12 +90,27 @@ struct cache_manager {
     uint64_t pool_size;
     int backend;
     char *local_dir;
+    int dirfd;                 /* root of the disk tier, -1 when disabled */
+    threadpool_t *io_write;    /* write-behind of stored records */
+    threadpool_t *io_read;     /* record reads of loads */
     adaptor_t *adaptor;
     pthread_mutex_t mu;        /* guards the entry list */
     struct rt_entry *entries;
 };
 
-static struct cache_manager g_mgr = {.mu = PTHREAD_MUTEX_INITIALIZER};
+static struct cache_manager g_mgr = {.mu = PTHREAD_MUTEX_INITIALIZER,
+                                     .dirfd = -1};
+
+/* a store waits at most this long for write-behind to release pool records */
+#define DISK_WAIT_SEC 30
+
+struct disk_job {
+    struct rt_entry *e;
+    int64_t idx;
+    uint8_t key[KVMAP_KEY_LEN];
+    int ret;
+    cc_latch_t *latch;         /* reads: the load's completion latch */
+};
 
 static struct rt_entry *find_entry_locked(const char *tag, uint8_t tp_size,
                                           uint8_t tp_id)
@@ -98,15 +135,41 @@ static struct rt_entry *get_entry(struct worker_context *wctx)
     return e;
 }
 
+/* wait until every write-behind job of e finished; returns and clears the
+ * first write error since the previous call */
+static int drain_writes(struct rt_entry *e)
+{
+    int ret;
+
+    pthread_mutex_lock(&e->mu);
+    while (e->disk_pending)
+        pthread_cond_wait(&e->cv, &e->mu);
+    ret = e->disk_err;
+    e->disk_err = 0;
+    pthread_mutex_unlock(&e->mu);
+    return ret;
+}
+
 static void destroy_entry(struct rt_entry *e)
 {
+    drain_writes(e);
     kvmap_destroy(e->map);
     mempool_destroy(e->pool);
     if (e->host_base)
         free_pinned_ptr(g_mgr.adaptor, e->host_base, e->pool_bytes);
+    if (e->dfd >= 0)
+        close(e->dfd);
+    pthread_cond_destroy(&e->cv);
     pthread_mutex_destroy(&e->mu);
     free(e->model_tag);
     free(e);
+}
+
+static int io_threads(void)
+{
+    const char *s = getenv("CROSSCACHE_IO_THREADS");
+    int n = s ? atoi(s) : 4;     /* reference: threadpool_create("CaIO", 4) */
+    return n < 1 ? 1 : (n > 64 ? 64 : n);
 }
 
 /* ------------------------------------------------------------------ */
@@ -115,6 +178,7 @@ int cache_init_backend(uint32_t chunk_size, uint64_t pool_size,
                        const char *root_dir, int backend)
 {
     adaptor_t *ad;
+    int ret = 0;
 
     /* transfer_params.num_tokens is 16-bit (reference device.h:25) */
     if (!chunk_size || chunk_size > UINT16_MAX)
@@ -135,17 +199,52 @@ int cache_init_backend(uint32_t chunk_size, uint64_t pool_size,
         log_error("cache_init: no adaptor for backend %d", backend);
         return -ENODEV;
     }
+    g_mgr.dirfd = -1;
+    g_mgr.io_write = g_mgr.io_read = NULL;
+    g_mgr.local_dir = NULL;
+    if (root_dir && *root_dir) {
+        ret = disk_open_root(root_dir);
+        if (ret < 0) {
+            log_error("cache_init: cache dir %s: %d", root_dir, ret);
+            goto fail;
+        }
+        g_mgr.dirfd = ret;
+        ret = 0;
+        g_mgr.local_dir = strdup(root_dir);
+        g_mgr.io_write = threadpool_create("CaIOw", io_threads());
+        g_mgr.io_read = threadpool_create("CaIOr", io_threads());
+        if (!g_mgr.local_dir || !g_mgr.io_write || !g_mgr.io_read) {
+            ret = -ENOMEM;
+            goto fail;
+        }
+    }
     g_mgr.adaptor = ad;
     g_mgr.backend = backend;
     g_mgr.chunk_size = chunk_size;
     g_mgr.pool_size = pool_size;
-    g_mgr.local_dir = root_dir ? strdup(root_dir) : NULL;
     g_mgr.entries = NULL;
     g_mgr.initialised = 1;
     pthread_mutex_unlock(&g_mgr.mu);
-    log_info("cache_init chunk_size:%u pool_size:%lu backend:%d", chunk_size,
-             (unsigned long)pool_size, backend);
+    log_info("cache_init chunk_size:%u pool_size:%lu backend:%d dir:%s",
+             chunk_size, (unsigned long)pool_size, backend,
+             g_mgr.local_dir ? g_mgr.local_dir : "(none)");
     return 0;
+
+fail:
+    threadpool_destroy(g_mgr.io_write);
+    threadpool_destroy(g_mgr.io_read);
+    g_mgr.io_write = g_mgr.io_read = NULL;
+    if (g_mgr.dirfd >= 0)
+        close(g_mgr.dirfd);
+    g_mgr.dirfd = -1;
+    free(g_mgr.local_dir);
+    g_mgr.local_dir = NULL;
+    if (backend == CACHE_BACKEND_CUDA)
+        cuda_adaptor_destroy(ad);
+    else
+        mem_adaptor_destroy(ad);
+    pthread_mutex_unlock(&g_mgr.mu);
+    return ret;
 }
 
 int cache_init(uint32_t chunk_size, uint64_t pool_size, const char *root_dir)
@@ -163,6 +262,10 @@ void cache_exit()
         pthread_mutex_unlock(&g_mgr.mu);
         return;
     }
+    /* finishes every queued write before the pools go away */
+    threadpool_destroy(g_mgr.io_write);
+    threadpool_destroy(g_mgr.io_read);
+    g_mgr.io_write = g_mgr.io_read = NULL;
     for (e = g_mgr.entries; e; e = n) {
         n = e->next;
         destroy_entry(e);
@@ -173,6 +276,9 @@ void cache_exit()
     else
         mem_adaptor_destroy(g_mgr.adaptor);
     g_mgr.adaptor = NULL;
+    if (g_mgr.dirfd >= 0)
+        close(g_mgr.dirfd);
+    g_mgr.dirfd = -1;
     free(g_mgr.local_dir);
     g_mgr.local_dir = NULL;
     g_mgr.initialised = 0;
@@ -249,6 +355,8 @@ int cache_register(struct worker_context *wctx)
         goto unpin_v;
     }
     pthread_mutex_init(&e->mu, NULL);
+    pthread_cond_init(&e->cv, NULL);
+    e->dfd = -1;
     e->model_tag = strdup(wctx->model.model_name);
     e->tp_size = wctx->world_size;
     e->tp_id = wctx->rank_id;
@@ -278,6 +386,18 @@ int cache_register(struct worker_context *wctx)
         destroy_entry(e);
         pthread_mutex_unlock(&g_mgr.mu);
         goto unpin_v;
+    }
+    if (g_mgr.dirfd >= 0) {
+        e->dfd = disk_open_ns(g_mgr.dirfd, e->model_tag, e->tp_size, e->tp_id);
+        if (e->dfd < 0) {
+            log_error("register: disk namespace of %s: %d", e->model_tag,
+                      e->dfd);
+            ret = e->dfd;
+            e->dfd = -1;
+            destroy_entry(e);
+            pthread_mutex_unlock(&g_mgr.mu);
+            goto unpin_v;
+        }
     }
     e->stats.records_total = m_count;
     e->next = g_mgr.entries;
@@ -368,98 +488,377 @@ static int run_transfer(struct rt_entry *e, struct worker_context *wctx,
     return ret;
 }
 
+/* ---- disk jobs ------------------------------------------------------ */
+
+static void write_job(void *p)
+{
+    struct disk_job *j = p;
+    struct rt_entry *e = j->e;
+    int ret = disk_write(e->dfd, j->key, mempool_addr(e->pool, j->idx),
+                         e->objsize);
+
+    pthread_mutex_lock(&e->mu);
+    kvmap_unpin(e->map, j->idx);
+    if (ret == 0) {
+        e->stats.disk_writes++;
+        e->stats.bytes_written_disk += e->objsize;
+    } else if (ret == 1) {
+        e->stats.disk_write_skips++;
+    } else {
+        e->stats.disk_write_errors++;
+        if (!e->disk_err)
+            e->disk_err = ret;
+    }
+    e->disk_pending--;
+    pthread_cond_broadcast(&e->cv);
+    pthread_mutex_unlock(&e->mu);
+    free(j);
+}
+
+static void read_job(void *p)
+{
+    struct disk_job *j = p;
+    struct rt_entry *e = j->e;
+
+    j->ret = disk_read(e->dfd, j->key, mempool_addr(e->pool, j->idx),
+                       e->objsize);
+    cc_latch_done(j->latch, 0);
+}
+
+/* queue the write-behind of records idx[0..n) (already pinned and counted
+ * in disk_pending by the caller) */
+static void submit_writes(struct rt_entry *e, const int64_t *idx,
+                          const uint8_t *const *keys, uint32_t n)
+{
+    uint32_t i;
+
+    for (i = 0; i < n; i++) {
+        struct disk_job *j = calloc(1, sizeof(*j));
+        if (j) {
+            j->e = e;
+            j->idx = idx[i];
+            memcpy(j->key, keys[i], KVMAP_KEY_LEN);
+            if (threadpool_submit(g_mgr.io_write, j, write_job) == 0)
+                continue;
+            write_job(j);          /* no queue slot: write inline */
+            continue;
+        }
+        pthread_mutex_lock(&e->mu);
+        kvmap_unpin(e->map, idx[i]);
+        e->stats.disk_write_errors++;
+        if (!e->disk_err)
+            e->disk_err = -ENOMEM;
+        e->disk_pending--;
+        pthread_cond_broadcast(&e->cv);
+        pthread_mutex_unlock(&e->mu);
+    }
+}
+
+/* a free or evicted record index; with write-behind in flight, waits for
+ * writes to release records.  Called and returns with e->mu held; may drop
+ * it while waiting (then *waited is set and the caller re-checks its key). */
+static int64_t alloc_record_locked(struct rt_entry *e, int *waited)
+{
+    struct timespec ts;
+    int64_t r;
+
+    *waited = 0;
+    r = mempool_alloc_index(e->pool);
+    if (r >= 0)
+        return r;
+    r = kvmap_evict_lru(e->map);
+    if (r >= 0) {
+        e->stats.evictions++;
+        return r;
+    }
+    if (!e->disk_pending)
+        return -1;
+    clock_gettime(CLOCK_REALTIME, &ts);
+    ts.tv_sec += DISK_WAIT_SEC;
+    if (pthread_cond_timedwait(&e->cv, &e->mu, &ts))
+        return -1;
+    *waited = 1;
+    return -1;
+}
+
+/* ---- store / load --------------------------------------------------- */
+
+struct op_args {
+    struct rt_entry *e;
+    struct worker_context *wctx;
+    const uint8_t *keys;
+    uint32_t key_len;
+    const uint64_t *bids;
+    uint32_t key_num;
+    uint32_t bpc;
+    int64_t *idx;              /* [key_num] record per transferred key */
+    uint64_t *tbids;           /* [key_num * bpc] their block ids */
+    uint32_t *kpos;            /* [key_num] key index of each transfer */
+    uint8_t *from_disk;        /* [key_num] load: record read from a file */
+};
+
+static void add_transfer(struct op_args *a, uint32_t *n, uint32_t i,
+                         int64_t r, int from_disk)
+{
+    a->idx[*n] = r;
+    a->kpos[*n] = i;
+    a->from_disk[*n] = (uint8_t)from_disk;
+    memcpy(a->tbids + (uint64_t)*n * a->bpc, a->bids + (uint64_t)i * a->bpc,
+           a->bpc * sizeof(uint64_t));
+    (*n)++;
+}
+
+static int do_store(struct op_args *a)
+{
+    struct rt_entry *e = a->e;
+    const uint8_t **wkeys = NULL;
+    uint32_t i, n = 0;
+    int ret = 0, xret, waited;
+
+    pthread_mutex_lock(&e->mu);
+    for (i = 0; i < a->key_num; i++) {
+        const uint8_t *key = a->keys + (uint64_t)i * a->key_len;
+        int64_t r;
+    again:
+        r = kvmap_find(e->map, key);
+        if (r >= 0) {                   /* cached or in flight: keep it */
+            e->stats.store_dedup++;
+            continue;
+        }
+        r = alloc_record_locked(e, &waited);
+        if (waited)
+            goto again;
+        if (r < 0) {
+            log_warn("store: pool exhausted (all records pinned/in flight)");
+            ret = -ENOMEM;
+            break;
+        }
+        kvmap_insert(e->map, r, key, KVMAP_PENDING);
+        add_transfer(a, &n, i, r, 0);
+    }
+    pthread_mutex_unlock(&e->mu);
+
+    xret = n ? run_transfer(e, a->wctx, KV_D_TO_H, a->idx, a->tbids, n) : 0;
+    if (xret < 0 && ret == 0)
+        ret = xret;
+
+    if (xret == 0 && n && e->dfd >= 0)
+        wkeys = malloc(n * sizeof(*wkeys));
+    pthread_mutex_lock(&e->mu);
+    for (i = 0; i < n; i++) {
+        if (xret == 0) {
+            kvmap_publish(e->map, a->idx[i]);
+            e->stats.stored++;
+            e->stats.bytes_saved += e->objsize;
+            if (wkeys) {
+                kvmap_pin(e->map, a->idx[i]);   /* until its file is written */
+                e->disk_pending++;
+                wkeys[i] = a->keys + (uint64_t)a->kpos[i] * a->key_len;
+            }
+        } else {
+            kvmap_remove(e->map, a->idx[i]);
+            mempool_free_index(e->pool, a->idx[i]);
+        }
+    }
+    if (xret == 0 && n && e->dfd >= 0 && !wkeys) {
+        e->stats.disk_write_errors += n;
+        if (!e->disk_err)
+            e->disk_err = -ENOMEM;
+    }
+    pthread_mutex_unlock(&e->mu);
+    if (wkeys) {
+        submit_writes(e, a->idx, wkeys, n);
+        free(wkeys);
+    }
+    return ret;
+}
+
+static int do_load(struct op_args *a)
+{
+    struct rt_entry *e = a->e;
+    uint32_t i, n = 0, nc = 0, nd = 0, ok;
+    uint32_t *cand = NULL;
+    struct disk_job *jobs = NULL;
+    cc_latch_t latch;
+    int ret = 0, xret, waited;
+
+    if (e->dfd >= 0) {
+        cand = malloc(a->key_num * sizeof(*cand));
+        if (!cand)
+            return -ENOMEM;
+    }
+    /* 1. memory hits are pinned; absent keys become disk candidates */
+    pthread_mutex_lock(&e->mu);
+    for (i = 0; i < a->key_num; i++) {
+        const uint8_t *key = a->keys + (uint64_t)i * a->key_len;
+        int64_t r = kvmap_find(e->map, key);
+        if (r >= 0 && kvmap_state(e->map, r) == KVMAP_READY) {
+            kvmap_touch(e->map, r);
+            kvmap_pin(e->map, r);
+            add_transfer(a, &n, i, r, 0);
+        } else if (r < 0 && cand) {
+            cand[nc++] = i;
+        } else {
+            e->stats.load_misses++;
+            ret = -ENOENT;
+        }
+    }
+    pthread_mutex_unlock(&e->mu);
+
+    /* 2. which candidates have a file (no lock held) */
+    for (i = 0; i < nc; i++)
+        if (disk_stat(e->dfd, a->keys + (uint64_t)cand[i] * a->key_len,
+                      e->objsize) == 0)
+            cand[nd++] = cand[i];
+
+    /* 3. a PENDING record per file; a key another thread cached meanwhile
+     *    is a memory hit after all */
+    pthread_mutex_lock(&e->mu);
+    if (nd < nc) {
+        e->stats.load_misses += nc - nd;
+        ret = -ENOENT;
+    }
+    for (i = 0; i < nd; i++) {
+        const uint8_t *key = a->keys + (uint64_t)cand[i] * a->key_len;
+        int64_t r;
+    again:
+        r = kvmap_find(e->map, key);
+        if (r >= 0) {
+            if (kvmap_state(e->map, r) == KVMAP_READY) {
+                kvmap_touch(e->map, r);
+                kvmap_pin(e->map, r);
+                add_transfer(a, &n, cand[i], r, 0);
+            } else {
+                e->stats.load_misses++;
+                ret = -ENOENT;
+            }
+            continue;
+        }
+        r = alloc_record_locked(e, &waited);
+        if (waited)
+            goto again;
+        if (r < 0) {
+            log_warn("load: no pool record free for a disk read");
+            e->stats.load_misses++;
+            ret = -ENOMEM;
+            continue;
+        }
+        kvmap_insert(e->map, r, key, KVMAP_PENDING);
+        add_transfer(a, &n, cand[i], r, 1);
+    }
+    pthread_mutex_unlock(&e->mu);
+    free(cand);
+
+    /* 4. read the files in parallel */
+    for (i = 0, nd = 0; i < n; i++)
+        nd += a->from_disk[i];
+    if (nd) {
+        jobs = calloc(n, sizeof(*jobs));
+        if (jobs) {
+            cc_latch_init(&latch, nd);
+            for (i = 0; i < n; i++) {
+                struct disk_job *j = &jobs[i];
+                if (!a->from_disk[i])
+                    continue;
+                j->e = e;
+                j->idx = a->idx[i];
+                memcpy(j->key, a->keys + (uint64_t)a->kpos[i] * a->key_len,
+                       KVMAP_KEY_LEN);
+                j->latch = &latch;
+                if (threadpool_submit(g_mgr.io_read, j, read_job))
+                    read_job(j);
+            }
+            cc_latch_wait(&latch);
+            cc_latch_fini(&latch);
+        }
+    }
+    /* drop failed reads from the transfer list */
+    for (i = 0, ok = 0; i < n; i++) {
+        int rr = !a->from_disk[i] ? 0 : (jobs ? jobs[i].ret : -ENOMEM);
+        if (rr == 0) {
+            if (ok != i) {
+                a->idx[ok] = a->idx[i];
+                a->kpos[ok] = a->kpos[i];
+                a->from_disk[ok] = a->from_disk[i];
+                memcpy(a->tbids + (uint64_t)ok * a->bpc,
+                       a->tbids + (uint64_t)i * a->bpc,
+                       a->bpc * sizeof(uint64_t));
+            }
+            ok++;
+            continue;
+        }
+        pthread_mutex_lock(&e->mu);
+        kvmap_remove(e->map, a->idx[i]);
+        mempool_free_index(e->pool, a->idx[i]);
+        e->stats.disk_read_errors++;
+        e->stats.load_misses++;
+        pthread_mutex_unlock(&e->mu);
+        if (ret == 0)
+            ret = rr == -ENOENT ? -ENOENT : -EIO;
+    }
+    free(jobs);
+    n = ok;
+
+    /* 5. one batched host-to-device transfer for memory and disk records */
+    xret = n ? run_transfer(e, a->wctx, KV_H_TO_D, a->idx, a->tbids, n) : 0;
+    if (xret < 0 && ret == 0)
+        ret = xret;
+
+    /* 6. records read from disk join the memory tier (their host copy is
+     *    valid even when the device transfer failed) */
+    pthread_mutex_lock(&e->mu);
+    for (i = 0; i < n; i++) {
+        if (a->from_disk[i]) {
+            kvmap_publish(e->map, a->idx[i]);
+            e->stats.disk_reads++;
+            e->stats.bytes_read_disk += e->objsize;
+        } else {
+            kvmap_unpin(e->map, a->idx[i]);
+        }
+        if (xret == 0) {
+            e->stats.loaded++;
+            e->stats.bytes_loaded += e->objsize;
+        }
+    }
+    pthread_mutex_unlock(&e->mu);
+    return ret;
+}
+
 static int cache_op(struct worker_context *wctx, uint8_t *keys,
                     uint32_t key_len, uint64_t *bids, uint32_t bnum,
                     bool store)
 {
-    struct rt_entry *e;
-    uint32_t bpc, key_num, i, n = 0;
-    int64_t *idx = NULL;
-    uint64_t *tbids = NULL;
-    int ret = 0, xret;
+    struct op_args a;
+    int ret;
 
-    e = get_entry(wctx);
-    if (!e)
+    memset(&a, 0, sizeof(a));
+    a.e = get_entry(wctx);
+    if (!a.e)
         return -ENOENT;
     if (!keys || key_len < KVMAP_KEY_LEN || (bnum && !bids))
         return -EINVAL;
     if (!wctx->k_ptrs)
         return -EINVAL;
-    bpc = g_mgr.chunk_size / wctx->block_size;
-    key_num = bnum / bpc;
-    if (!key_num)
+    a.wctx = wctx;
+    a.keys = keys;
+    a.key_len = key_len;
+    a.bids = bids;
+    a.bpc = g_mgr.chunk_size / wctx->block_size;
+    a.key_num = bnum / a.bpc;
+    if (!a.key_num)
         return 0;
-    idx = malloc(key_num * sizeof(int64_t));
-    tbids = malloc((uint64_t)key_num * bpc * sizeof(uint64_t));
-    if (!idx || !tbids) {
-        free(idx);
-        free(tbids);
-        return -ENOMEM;
-    }
-
-    pthread_mutex_lock(&e->mu);
-    for (i = 0; i < key_num; i++) {
-        const uint8_t *key = keys + (uint64_t)i * key_len;
-        int64_t r = kvmap_find(e->map, key);
-        if (store) {
-            if (r >= 0) {               /* cached or in flight: keep it */
-                e->stats.store_dedup++;
-                continue;
-            }
-            r = mempool_alloc_index(e->pool);
-            if (r < 0) {
-                r = kvmap_evict_lru(e->map);
-                if (r >= 0)
-                    e->stats.evictions++;
-            }
-            if (r < 0) {
-                log_warn("store: pool exhausted (all records pinned/in flight)");
-                ret = -ENOMEM;
-                break;
-            }
-            kvmap_insert(e->map, r, key, KVMAP_PENDING);
-        } else {
-            if (r < 0 || kvmap_state(e->map, r) != KVMAP_READY) {
-                e->stats.load_misses++;
-                ret = -ENOENT;
-                continue;
-            }
-            kvmap_touch(e->map, r);
-            kvmap_pin(e->map, r);
-        }
-        idx[n] = r;
-        memcpy(tbids + (uint64_t)n * bpc, bids + (uint64_t)i * bpc,
-               bpc * sizeof(uint64_t));
-        n++;
-    }
-    pthread_mutex_unlock(&e->mu);
-
-    xret = run_transfer(e, wctx, store ? KV_D_TO_H : KV_H_TO_D, idx, tbids, n);
-    if (xret < 0 && ret == 0)
-        ret = xret;
-
-    pthread_mutex_lock(&e->mu);
-    for (i = 0; i < n; i++) {
-        if (store) {
-            if (xret == 0) {
-                kvmap_publish(e->map, idx[i]);
-                e->stats.stored++;
-                e->stats.bytes_saved += e->objsize;
-            } else {
-                kvmap_remove(e->map, idx[i]);
-                mempool_free_index(e->pool, idx[i]);
-            }
-        } else {
-            kvmap_unpin(e->map, idx[i]);
-            if (xret == 0) {
-                e->stats.loaded++;
-                e->stats.bytes_loaded += e->objsize;
-            }
-        }
-    }
-    pthread_mutex_unlock(&e->mu);
-    free(idx);
-    free(tbids);
+    a.idx = malloc(a.key_num * sizeof(int64_t));
+    a.kpos = malloc(a.key_num * sizeof(uint32_t));
+    a.from_disk = malloc(a.key_num);
+    a.tbids = malloc((uint64_t)a.key_num * a.bpc * sizeof(uint64_t));
+    if (!a.idx || !a.kpos || !a.from_disk || !a.tbids)
+        ret = -ENOMEM;
+    else
+        ret = store ? do_store(&a) : do_load(&a);
+    free(a.idx);
+    free(a.kpos);
+    free(a.from_disk);
+    free(a.tbids);
     return ret;
 }
 
@@ -490,18 +889,42 @@ static uint32_t prefix_hits_locked(struct rt_entry *e, const uint8_t *keys,
     return i;
 }
 
+/* leading hits of one request: memory first; past the first memory miss,
+ * keys are asked of the disk tier one by one (reference cache.c:733-742),
+ * with the entry lock dropped around each stat */
+static uint32_t prefix_hits(struct rt_entry *e, const uint8_t *keys,
+                            uint32_t key_num, uint32_t key_len)
+{
+    uint32_t i = 0;
+
+    pthread_mutex_lock(&e->mu);
+    for (;;) {
+        i += prefix_hits_locked(e, keys + (uint64_t)i * key_len, key_num - i,
+                                key_len);
+        if (i >= key_num || e->dfd < 0)
+            break;
+        pthread_mutex_unlock(&e->mu);
+        if (disk_stat(e->dfd, keys + (uint64_t)i * key_len, e->objsize)) {
+            pthread_mutex_lock(&e->mu);
+            break;
+        }
+        pthread_mutex_lock(&e->mu);
+        e->stats.lookup_hits++;
+        e->stats.disk_lookup_hits++;
+        i++;
+    }
+    pthread_mutex_unlock(&e->mu);
+    return i;
+}
+
 int cache_lookup(struct worker_context *wctx, uint8_t *keys, uint32_t key_num,
                  uint32_t key_len)
 {
     struct rt_entry *e = get_entry(wctx);
-    uint32_t hits;
 
     if (!e || !keys || key_len < KVMAP_KEY_LEN)
         return 0;
-    pthread_mutex_lock(&e->mu);
-    hits = prefix_hits_locked(e, keys, key_num, key_len);
-    pthread_mutex_unlock(&e->mu);
-    return (int)(hits * key_len);
+    return (int)(prefix_hits(e, keys, key_num, key_len) * key_len);
 }
 
 int cache_lookup_batch(struct worker_context *wctx, const uint8_t *keys,
@@ -521,6 +944,14 @@ int cache_lookup_batch(struct worker_context *wctx, const uint8_t *keys,
     }
     if (key_len < KVMAP_KEY_LEN || (num_req && !keys))
         return -EINVAL;
+    if (e->dfd >= 0) {
+        for (r = 0; r < num_req; r++) {
+            hit_keys[r] = prefix_hits(e, keys + off, key_nums[r], key_len);
+            off += (uint64_t)key_nums[r] * key_len;
+        }
+        return 0;
+    }
+    /* memory only: one lock acquisition for the whole batch */
     pthread_mutex_lock(&e->mu);
     for (r = 0; r < num_req; r++) {
         hit_keys[r] = prefix_hits_locked(e, keys + off, key_nums[r], key_len);
@@ -528,6 +959,15 @@ int cache_lookup_batch(struct worker_context *wctx, const uint8_t *keys,
     }
     pthread_mutex_unlock(&e->mu);
     return 0;
+}
+
+int cache_flush(struct worker_context *wctx)
+{
+    struct rt_entry *e = get_entry(wctx);
+
+    if (!e)
+        return -ENOENT;
+    return drain_writes(e);
 }
 
 int cache_get_stats(struct worker_context *wctx, struct cache_stats *out)
@@ -549,6 +989,7 @@ int cache_clear(struct worker_context *wctx)
 
     if (!e)
         return -ENOENT;
+    drain_writes(e);        /* write-behind pins its records until done */
     pthread_mutex_lock(&e->mu);
     for (i = 0; i < e->stats.records_total; i++) {
         if (kvmap_state(e->map, (int64_t)i) == KVMAP_READY &&

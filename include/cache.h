@@ -7,7 +7,8 @@
  *
  *   cache_init        chunk_size tokens per record, pool_size bytes of pinned
  *                     host memory per registered (model, tp_size, tp_rank),
- *                     root_dir for the disk tier.  CUDA backend.
+ *                     root_dir for the disk tier (NULL or "": memory only;
+ *                     created if missing, one level).  CUDA backend.
  *   cache_register    import the worker's per-layer KV handles, allocate and
  *                     pin the record pool.  0 or -ENOMEM/-EINVAL.
  *   cache_lookup      walk keys in order and stop at the first key that is
@@ -16,6 +17,11 @@
  *   cache_store       save bnum blocks as bnum / (chunk_size / block_size)
  *                     records, one 32-byte key per record (cache.c:513-593).
  *   cache_load        restore records for the keys into the given blocks.
+ *
+ * With a disk tier every stored record is also written to
+ * <root_dir>/<model tag>.tp<tp_size>.<tp_rank>/<64 hex digits of its key>
+ * by IO threads after cache_store returns; lookups and loads fall back to
+ * those files for keys that are not in memory, across restarts too.
  *
  * Additions (new, no reference counterpart) are listed after them.
  */
@@ -79,14 +85,30 @@ struct cache_stats {
     uint64_t evictions;         /* records reclaimed by LRU eviction      */
     uint64_t bytes_saved;
     uint64_t bytes_loaded;
+    /* disk tier */
+    uint64_t disk_writes;       /* record files written                   */
+    uint64_t disk_write_skips;  /* ... already on disk, not rewritten      */
+    uint64_t disk_write_errors;
+    uint64_t disk_reads;        /* records a load read from files         */
+    uint64_t disk_read_errors;  /* files that vanished or failed to read   */
+    uint64_t disk_lookup_hits;  /* lookup keys found on disk only          */
+    uint64_t bytes_written_disk;
+    uint64_t bytes_read_disk;
 };
 
 /* Counters of the (model, world_size, rank_id) entry of wctx.  0 or -ENOENT. */
 int cache_get_stats(struct worker_context *wctx, struct cache_stats *out);
 
-/* Drop every cached record of wctx's entry (the pool stays pinned).
- * 0 or -ENOENT. */
+/* Drop every cached record of wctx's entry from memory (the pool stays
+ * pinned; record files of the disk tier stay).  Waits for pending disk
+ * writes first.  0 or -ENOENT. */
 int cache_clear(struct worker_context *wctx);
+
+/* Wait until every record stored so far through wctx's entry is written to
+ * its file.  Returns 0, the first write error (-errno) since the previous
+ * cache_flush, or -ENOENT when the worker is not registered.  Without a
+ * disk tier it returns 0 at once. */
+int cache_flush(struct worker_context *wctx);
 
 #ifdef __cplusplus
 }
