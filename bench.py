@@ -522,6 +522,82 @@ def _mla_evict(args, dev, cc, lib, LRUPool) -> dict:
 # ---------------------------------------------------------------------------
 # GPU arm
 
+def _fs_type(path: str) -> str:
+    best, kind = "", "unknown"
+    real = os.path.realpath(path)
+    try:
+        with open("/proc/mounts") as f:
+            for ln in f:
+                parts = ln.split()
+                if len(parts) > 2 and (real == parts[1] or real.startswith(parts[1].rstrip("/") + "/")) \
+                        and len(parts[1]) > len(best):
+                    best, kind = parts[1], parts[2]
+    except OSError:
+        pass
+    return kind
+
+
+def _disk_tier_probe(args, cc, L_, layers, layout, kp, vp, hashes, bt_save, bt_load, disjoint, s) -> dict:
+    """Disk tier on a sample of the e2e workload: store the first requests
+    with write-behind (store call, then until every file is written), empty
+    the memory tier, then load them back from the files (parallel O_DIRECT
+    reads + one batched H2D per request).  A fresh directory, removed after."""
+    import shutil
+
+    import torch
+
+    n = min(args.disk_requests, s["n_req"])
+    keys_per = s["n_tok"] // CHUNK
+    nbl = n * s["per_req_blocks"]
+    d_payload = n * keys_per * s["rec_bytes"]
+    root = os.path.join(args.disk_dir, f"crosscache-bench-{os.getpid()}-{s['rank']}")
+    os.makedirs(args.disk_dir, exist_ok=True)
+    free_bytes = shutil.disk_usage(args.disk_dir).free
+    if free_bytes < 2 * d_payload:
+        return {"skipped": f"needs {2 * d_payload} bytes free under the directory, {free_bytes} free"}
+    kb = np.ascontiguousarray(hashes[s["bpc"] - 1::s["bpc"]][: n * keys_per]).tobytes()
+    save = np.ascontiguousarray(bt_save[:nbl])
+    loads = [np.ascontiguousarray(bt_load[r * s["per_req_blocks"]:(r + 1) * s["per_req_blocks"]])
+             for r in range(n)]
+    b_save = torch.from_numpy(save.astype(np.int64)).to(s["dev"])
+    b_load = torch.from_numpy(bt_load[:nbl].astype(np.int64)).to(s["dev"])
+    if disjoint:
+        for t in layers:
+            t[:, b_load] = 0
+    cc.init(CHUNK, (s["nrec"] + 1) * s["rec_bytes"], root)
+    try:
+        w = cc.Worker("llama-3-8b", layout, kp, vp, node_id=s["local"], world_size=s["world"], rank=s["rank"])
+        w.register()
+        t0 = time.perf_counter()
+        assert L_.cache_store(C.byref(w.ctx), kb, 32, save.ctypes.data, nbl) == 0
+        t1 = time.perf_counter()
+        w.flush()
+        t2 = time.perf_counter()
+        w.clear()
+        t3 = time.perf_counter()
+        for r in range(n):
+            kr = kb[r * keys_per * 32:(r + 1) * keys_per * 32]
+            assert L_.cache_load(C.byref(w.ctx), kr, 32, loads[r].ctypes.data, s["per_req_blocks"]) == 0
+        torch.cuda.synchronize()
+        t4 = time.perf_counter()
+        ok = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers) \
+            if disjoint else None
+        st = w.stats()
+        w.unregister()
+    finally:
+        cc.exit()
+        shutil.rmtree(root, ignore_errors=True)
+    return {"records": n * keys_per, "bytes": d_payload, "fs": _fs_type(args.disk_dir),
+            "store_call_gbs": round(d_payload / (t1 - t0) / GB, 3),
+            "write_gbs": round(d_payload / (t2 - t0) / GB, 3),
+            "load_from_files_gbs": round(d_payload / (t4 - t3) / GB, 3),
+            "disk_writes": st["disk_writes"], "disk_reads": st["disk_reads"],
+            "io_threads": int(os.environ.get("CROSSCACHE_IO_THREADS", "4")),
+            "verified_bytes": ok,
+            "note": "sample of the e2e workload: store (records in host memory at return, files written "
+                    "behind), then every file written; memory emptied; loads read the files"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -530,6 +606,9 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--disk-dir", default=None,
+                    help="also time the disk tier in a fresh directory under this path (off by default)")
+    ap.add_argument("--disk-requests", type=int, default=8, help="requests of the disk-tier sample")
     ap.add_argument("--layers", type=int, default=L, help="smaller cases for ncu captures only")
     ap.add_argument("--requests", type=int, default=REQS)
     ap.add_argument("--blocks-per-layer", type=int, default=NUM_BLOCKS)
@@ -746,6 +825,7 @@ def main() -> None:
     e2e = None
     link = None
     p50 = None
+    disk = None
     if not args.skip_e2e:
         # host-link peaks measured in this run: pinned 256 MiB cudaMemcpyAsync,
         # 16 per direction (4 GiB), every rank at once after a barrier -- the
@@ -900,6 +980,11 @@ def main() -> None:
         st = w.stats()
         w.unregister()
         cc.exit()
+        if args.disk_dir:
+            disk = _disk_tier_probe(args, cc, L_, layers, layout, kp, vp, hashes, bt_save, bt_load, disjoint,
+                                    dict(local=local, world=world, rank=rank, n_req=n_req, n_tok=n_tok,
+                                         bpc=bpc, per_req_blocks=per_req_blocks, nrec=nrec,
+                                         rec_bytes=rec_bytes, dev=dev))
         hit_blocks = parts[-1][3] * bpc
         save_s = max_over_ranks(statistics.median(p[1] for p in parts))
         load_s = max_over_ranks(statistics.median(p[2] for p in parts))
@@ -951,7 +1036,7 @@ def main() -> None:
                          "gather_ms": round(gather_ms, 4), "scatter_ms": round(scatter_ms, 4),
                          "scatter_frac": round(2 * payload / (scatter_ms / 1e3) / GB / hbm_peak, 4)},
             "e2e": e2e, "link": link, "p50_load_latency_ms": round(p50, 3) if p50 is not None else None,
-            "block_hash": hash_info,
+            "block_hash": hash_info, "disk_tier": disk,
             "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": clocks.summary(),
             "verified_bytes": bool(ok_value),
         }
