@@ -97,6 +97,24 @@ class Worker:
         self.ctx.v_raw_ptrs = self._v.ctypes.data if self._v is not None else None
         self.registered = False
 
+    @classmethod
+    def from_keys(cls, model_name: str, layout: KVLayout, k_keys: bytes, v_keys: bytes | None,
+                  per_len: int, node_id: int = 0, world_size: int = 1, rank: int = 0) -> "Worker":
+        """A worker registered from per-layer keys of `per_len` bytes each
+        (8: raw pointers of this process, 64: CUDA IPC handles, 72: handle +
+        offset) -- what the server receives in a REGISTER message."""
+        if len(k_keys) != layout.num_layers * per_len or (
+                v_keys is not None and len(v_keys) != layout.num_layers * per_len):
+            raise ValueError("one key of per_len bytes per layer")
+        w = cls(model_name, layout, [0] * layout.num_layers,
+                [0] * layout.num_layers if v_keys is not None else None, node_id, world_size, rank)
+        w._kbuf = C.create_string_buffer(bytes(k_keys), len(k_keys))
+        w._vbuf = C.create_string_buffer(bytes(v_keys), len(v_keys)) if v_keys is not None else None
+        w.ctx.per_len = per_len
+        w.ctx.k_raw_ptrs = C.cast(w._kbuf, C.c_void_p)
+        w.ctx.v_raw_ptrs = C.cast(w._vbuf, C.c_void_p) if w._vbuf is not None else None
+        return w
+
     # -- reference API ------------------------------------------------------
     def register(self) -> None:
         ret = lib.cache_register(C.byref(self.ctx))

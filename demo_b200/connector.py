@@ -11,7 +11,11 @@ RETRIEVE ops, wait_for_save the STORE ops, get_finished reports them.
 
 Configuration (kv_connector_extra_config): "cache.pool_size" bytes of pinned
 host memory per (model, tp_size, tp_rank) entry (default 4 GiB, the
-reference server's default, src/main.c:428).
+reference server's default, src/main.c:428).  With "cache.server.host"
+(e.g. "tcp://localhost") and optionally "cache.server.port" (5555) set, as
+the reference connector reads them (crosscache_connector.py:334-341), both
+roles talk to a CrossCache server (python -m demo_b200.server) through the
+adapters of demo_b200.remote instead of running the cache in-process.
 """
 from __future__ import annotations
 
@@ -162,13 +166,29 @@ class CrossCacheConnector(KVConnectorBase_V1):
         world_size = vllm_config.parallel_config.world_size
         rank = vllm_config.parallel_config.rank
         self.vllm_block_size = vllm_config.cache_config.block_size
+        host = vllm_config.kv_transfer_config.get_from_extra_config("cache.server.host", None)
+        self._remote = host is not None
+        if self._remote:
+            import zmq
+
+            from .remote import RemoteSchedulerAdapter, RemoteWorkerAdapter
+            port = vllm_config.kv_transfer_config.get_from_extra_config("cache.server.port", 5555)
+            url, ctx = f"{host}:{port}", zmq.Context.instance()
         if role == KVConnectorRole.SCHEDULER:
-            self.scheduler_adapter = SchedulerAdapter(model, world_size, rank, self.vllm_block_size)
+            if self._remote:
+                self.scheduler_adapter = RemoteSchedulerAdapter(url, ctx, model, world_size, rank,
+                                                                self.vllm_block_size)
+            else:
+                self.scheduler_adapter = SchedulerAdapter(model, world_size, rank, self.vllm_block_size)
             self.request_trackers: dict[str, CacheRequestTracker] = {}
         elif role == KVConnectorRole.WORKER:
             dev = torch.cuda.current_device()
-            self.worker_adapter = WorkerAdapter(model, world_size, rank, self.vllm_block_size,
-                                                pool_size=pool_size, device=dev)
+            if self._remote:
+                self.worker_adapter = RemoteWorkerAdapter(url, ctx, model, world_size, rank,
+                                                          self.vllm_block_size, device=dev)
+            else:
+                self.worker_adapter = WorkerAdapter(model, world_size, rank, self.vllm_block_size,
+                                                    pool_size=pool_size, device=dev)
         else:
             raise ValueError(f"Unknown KVConnectorRole: {role}")
         self._model = model
@@ -176,7 +196,7 @@ class CrossCacheConnector(KVConnectorBase_V1):
     # ---------------- worker side ----------------
     def register_kv_caches(self, kv_caches: dict[str, torch.Tensor]):
         self.worker_adapter.register(kv_caches)
-        if self.worker_adapter.worker_id == 0:
+        if self.worker_adapter.worker_id == 0 and not self._remote:
             _LOCAL_WORKERS[self._model] = self.worker_adapter
 
     def wait_for_layer_load(self, layer_name: str) -> None:
@@ -212,8 +232,11 @@ class CrossCacheConnector(KVConnectorBase_V1):
 
     def shutdown(self):
         if hasattr(self, "worker_adapter"):
-            _LOCAL_WORKERS.pop(self._model, None)
+            if not self._remote:
+                _LOCAL_WORKERS.pop(self._model, None)
             self.worker_adapter.unregister()
+        if self._remote and hasattr(self, "scheduler_adapter"):
+            self.scheduler_adapter.close()
         return None
 
     # ---------------- scheduler side ----------------
@@ -223,7 +246,7 @@ class CrossCacheConnector(KVConnectorBase_V1):
 
     def get_num_new_matched_tokens(self, request: "Request", num_computed_tokens: int) -> tuple[int | None, bool]:
         tracker = self._get_or_create_request_tracker(request)
-        if self.scheduler_adapter._worker is None:
+        if not self._remote and self.scheduler_adapter._worker is None:
             w = self._lookup_worker()
             if w is not None:
                 self.scheduler_adapter.bind_worker(w)

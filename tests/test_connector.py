@@ -129,3 +129,48 @@ def test_unbound_scheduler_reports_no_hits():
     conn = CrossCacheConnector(_cfg(), vllm_base.KVConnectorRole.SCHEDULER)
     req = _request("D", 512, 4)
     assert conn.get_num_new_matched_tokens(req, 0) == (0, False)
+
+
+def test_remote_scheduler_asks_the_server():
+    """cache.server.host / port set: the scheduler's lookups go to a CrossCache
+    server over ZeroMQ (the reference connector's deployment), answered from
+    the records a worker stored there"""
+    import struct
+    import time
+
+    pytest.importorskip("zmq")
+    from demo_b200 import protocol as P
+    from demo_b200.mq import MessageQueueClient
+    from demo_b200.server import CacheServer
+
+    nb, unit = 256, 64
+    layers = [np.zeros(nb * BS * unit, np.uint8) for _ in range(2)]
+    srv = CacheServer("tcp://127.0.0.1:*", 256, 8 * 2 * 256 * unit, None, CACHE_BACKEND_MEM).start()
+    cli = MessageQueueClient(srv.endpoint)
+    conn = None
+    try:
+        keys_raw = [(struct.pack("<Q", layers[0].ctypes.data), struct.pack("<Q", layers[1].ctypes.data))]
+        assert cli.request(lambda u: P.encode_register(0, u, 1, 0, nb, BS, 2, 32, 8, "m", keys_raw),
+                           timeout=30) == 0
+        req = _request("R", 1024, 5)
+        keys = bh.chunk_keys(req.block_hashes, 256 // BS)
+        assert cli.request(lambda u: P.encode_transfer(P.Op.STORE, 0, u, keys[:3], list(range(48))),
+                           timeout=30) == 0
+        cfg = _cfg()
+        host, port = srv.endpoint.rsplit(":", 1)
+        cfg.kv_transfer_config.kv_connector_extra_config.update({"cache.server.host": host,
+                                                                 "cache.server.port": int(port)})
+        conn = CrossCacheConnector(cfg, vllm_base.KVConnectorRole.SCHEDULER)
+        deadline = time.time() + 30
+        while (res := conn.get_num_new_matched_tokens(req, 0)) == (None, True) and time.time() < deadline:
+            time.sleep(0.01)                 # the answer is asynchronous, as in the reference
+        assert res == (768, True)
+        conn.update_state_after_alloc(req, _Blocks(range(100, 164)), 768)
+        meta = conn.build_connector_meta(_sched_out())
+        (ret,) = meta.requests
+        assert ret.direction == "RETRIEVE" and ret.op.block_ids == list(range(100, 148))
+    finally:
+        if conn is not None:
+            conn.shutdown()
+        cli.close()
+        srv.stop()
