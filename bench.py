@@ -598,6 +598,115 @@ def _disk_tier_probe(args, cc, L_, layers, layout, kp, vp, hashes, bt_save, bt_l
                     "behind), then every file written; memory emptied; loads read the files"}
 
 
+def _serve_for_bench(q, stop, pool_bytes):
+    import torch
+
+    from demo_b200.server import CacheServer
+
+    torch.cuda.set_device(0)
+    try:
+        srv = CacheServer("tcp://127.0.0.1:*", CHUNK, pool_bytes, None).start()
+    except Exception as e:
+        q.put(("error", repr(e)))
+        return
+    q.put(("ok", srv.endpoint))
+    stop.wait(900)
+    srv.stop()
+
+
+def _server_probe(args, layers, hashes, bt_save, bt_load, disjoint, s) -> dict:
+    """Save and load of the e2e workload through a server process: the
+    worker side (this process) registers its layers by 72-byte CUDA IPC keys
+    and sends one STORE and one LOAD message per step carrying every request
+    (what the connector's wait_for_save / start_load_kv send), then 64
+    single-request LOADs for the per-request latency and 64 LOOKUPs for the
+    round trip."""
+    import multiprocessing as mp
+
+    import torch
+    import zmq
+
+    from demo_b200.adaptor import LoadStoreOp
+    from demo_b200.remote import RemoteSchedulerAdapter, RemoteWorkerAdapter
+
+    ctx = mp.get_context("spawn")
+    q, stop = ctx.Queue(), ctx.Event()
+    p = ctx.Process(target=_serve_for_bench, args=(q, stop, (s["nrec"] + 1) * s["rec_bytes"]))
+    p.start()
+    wa = sa = None
+    try:
+        status, endpoint = q.get(timeout=300)
+        if status != "ok":
+            return {"unavailable": endpoint}
+        zctx = zmq.Context.instance()
+        wa = RemoteWorkerAdapter(endpoint, zctx, "llama-3-8b", 1, 0, BS, device=s["dev"].index or 0)
+        wa.register({f"layer.{i}": t for i, t in enumerate(layers)})
+        prb, n_req = s["per_req_blocks"], s["n_req"]
+        def ops_for(step: int, table) -> list:
+            # fresh keys every step (the first byte carries the step) so each
+            # STORE moves every record instead of finding them cached
+            hs = [bytes([step & 0xFF]) + bytes(h[1:]) for h in hashes]
+            return [LoadStoreOp(hs[r * prb:(r + 1) * prb], table[r * prb:(r + 1) * prb].tolist())
+                    for r in range(n_req)]
+
+        ids = [f"r{r}" for r in range(n_req)]
+        if disjoint:
+            for t in layers:
+                t[:, torch.from_numpy(bt_load.astype(np.int64)).to(s["dev"])] = 0
+        torch.cuda.synchronize()
+        t_st, t_ld = [], []
+        for step in range(args.warmup + args.steps):
+            save_ops, load_ops = ops_for(step, bt_save), ops_for(step, bt_load)
+            t0 = time.perf_counter()
+            wa.store_requests(ids, save_ops)
+            assert wa.wait_all(timeout=600) == [0]
+            t1 = time.perf_counter()
+            wa.load_requests(ids, load_ops)
+            assert wa.wait_all(timeout=600) == [0, 0]
+            torch.cuda.synchronize()
+            t2 = time.perf_counter()
+            wa.store_futures.clear()
+            wa.load_futures.clear()
+            if step >= args.warmup:
+                t_st.append(t1 - t0)
+                t_ld.append(t2 - t1)
+        ok = all(torch.equal(t[:, torch.from_numpy(bt_save.astype(np.int64)).to(s["dev"])].view(torch.int16),
+                             t[:, torch.from_numpy(bt_load.astype(np.int64)).to(s["dev"])].view(torch.int16))
+                 for t in layers) if disjoint else None
+        lat = []
+        for r in range(n_req):
+            t0 = time.perf_counter()
+            wa.load_requests([f"l{r}"], [load_ops[r]])
+            assert wa.wait_all(timeout=600)[-1] == 0
+            lat.append(time.perf_counter() - t0)
+            wa.load_futures.clear()
+        sa = RemoteSchedulerAdapter(endpoint, zctx, "llama-3-8b", 1, 0, BS)
+        rtt, hits = [], 0
+        for r in range(n_req):
+            t0 = time.perf_counter()
+            sa.try_lookup(f"q{r}", save_ops[r].block_hashes)
+            h = sa.lookup_futures[f"q{r}"].result(timeout=60)
+            rtt.append(time.perf_counter() - t0)
+            hits += h
+        return {"save_gbs": round(s["payload"] / statistics.median(t_st) / GB, 3),
+                "load_gbs": round(s["payload"] / statistics.median(t_ld) / GB, 3),
+                "p50_request_load_latency_ms": round(statistics.median(lat) * 1e3, 3),
+                "p50_lookup_round_trip_us": round(statistics.median(rtt) * 1e6, 1),
+                "lookup_hit_tokens_per_request": hits // n_req, "verified_bytes": ok,
+                "note": "server in a second process (CUDA backend, pinned pool there), this process "
+                        "registered by 72-byte CUDA IPC keys; one STORE and one LOAD message per step "
+                        "carrying all requests, as the connector sends them"}
+    finally:
+        if sa is not None:
+            sa.close()
+        if wa is not None:
+            wa.unregister()
+        stop.set()
+        p.join(timeout=300)
+        if p.is_alive():
+            p.kill()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -609,6 +718,8 @@ def main() -> None:
     ap.add_argument("--disk-dir", default=None,
                     help="also time the disk tier in a fresh directory under this path (off by default)")
     ap.add_argument("--disk-requests", type=int, default=8, help="requests of the disk-tier sample")
+    ap.add_argument("--via-server", action="store_true",
+                    help="also time save/load through a CrossCache server process (ZeroMQ + CUDA IPC)")
     ap.add_argument("--layers", type=int, default=L, help="smaller cases for ncu captures only")
     ap.add_argument("--requests", type=int, default=REQS)
     ap.add_argument("--blocks-per-layer", type=int, default=NUM_BLOCKS)
@@ -826,6 +937,7 @@ def main() -> None:
     link = None
     p50 = None
     disk = None
+    server = None
     if not args.skip_e2e:
         # host-link peaks measured in this run: pinned 256 MiB cudaMemcpyAsync,
         # 16 per direction (4 GiB), every rank at once after a barrier -- the
@@ -985,6 +1097,10 @@ def main() -> None:
                                     dict(local=local, world=world, rank=rank, n_req=n_req, n_tok=n_tok,
                                          bpc=bpc, per_req_blocks=per_req_blocks, nrec=nrec,
                                          rec_bytes=rec_bytes, dev=dev))
+        if args.via_server and world == 1:
+            server = _server_probe(args, layers, hashes, bt_save, bt_load, disjoint,
+                                   dict(n_req=n_req, n_tok=n_tok, bpc=bpc, per_req_blocks=per_req_blocks,
+                                        nrec=nrec, rec_bytes=rec_bytes, payload=payload, dev=dev))
         hit_blocks = parts[-1][3] * bpc
         save_s = max_over_ranks(statistics.median(p[1] for p in parts))
         load_s = max_over_ranks(statistics.median(p[2] for p in parts))
@@ -1036,7 +1152,7 @@ def main() -> None:
                          "gather_ms": round(gather_ms, 4), "scatter_ms": round(scatter_ms, 4),
                          "scatter_frac": round(2 * payload / (scatter_ms / 1e3) / GB / hbm_peak, 4)},
             "e2e": e2e, "link": link, "p50_load_latency_ms": round(p50, 3) if p50 is not None else None,
-            "block_hash": hash_info, "disk_tier": disk,
+            "block_hash": hash_info, "disk_tier": disk, "via_server": server,
             "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": clocks.summary(),
             "verified_bytes": bool(ok_value),
         }
