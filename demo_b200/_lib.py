@@ -109,6 +109,9 @@ class KvCopyDesc(C.Structure):
         ("num_records", C.c_uint32),
         ("direction", C.c_int32),
         ("flags", C.c_uint32),
+        ("layer_begin", C.c_uint32),
+        ("record_layers", C.c_uint32),
+        ("max_ctas", C.c_uint32),
     ]
 
 
@@ -141,6 +144,15 @@ SIGNATURES: dict[str, tuple] = {
     "cache_get_stats": (C.c_int, [C.POINTER(WorkerContext), C.POINTER(CacheStats)]),
     "cache_clear": (C.c_int, [C.POINTER(WorkerContext)]),
     "cache_flush": (C.c_int, [C.POINTER(WorkerContext)]),
+    "cache_load_async": (C.c_int, [C.POINTER(WorkerContext), C.c_char_p, C.c_uint32, C.c_void_p, C.c_uint32,
+                                   C.POINTER(C.c_void_p)]),
+    "cache_store_async": (C.c_int, [C.POINTER(WorkerContext), C.c_char_p, C.c_uint32, C.c_void_p, C.c_uint32,
+                                    C.POINTER(C.c_void_p)]),
+    "cache_async_layers": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]),
+    "cache_async_stream_wait": (C.c_int, [C.c_void_p, C.c_uint32, C.c_void_p]),
+    "cache_async_query": (C.c_int, [C.c_void_p]),
+    "cache_async_finish": (C.c_int, [C.c_void_p]),
+    "cache_async_records": (C.c_uint32, [C.c_void_p]),
     # include/device.h
     "cuda_adaptor_create": (C.c_void_p, []),
     "cuda_adaptor_destroy": (None, [C.c_void_p]),
@@ -154,6 +166,11 @@ SIGNATURES: dict[str, tuple] = {
     "close_ipc_keys": (None, [C.c_void_p, C.c_void_p]),
     "transfer_kvcache": (C.c_int, [C.c_void_p, C.POINTER(TransferParams)]),
     "transfer_kvcache_batch": (C.c_int, [C.c_void_p, C.POINTER(TransferBatch)]),
+    "transfer_async_begin": (C.c_void_p, [C.c_void_p, C.POINTER(TransferBatch), C.POINTER(C.c_int)]),
+    "transfer_async_layers": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]),
+    "transfer_async_stream_wait": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p]),
+    "transfer_async_query": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "transfer_async_end": (C.c_int, [C.c_void_p, C.c_void_p]),
     "reset_device": (None, [C.c_void_p, C.c_uint8]),
     "crosscache_kernel_launches": (C.c_uint64, []),
     "ipc_export_key": (C.c_int, [C.c_void_p, C.c_void_p]),

@@ -132,11 +132,20 @@ class WorkerAdapter:
         self.finished_stores: set[str] = set()
         self.previously_finished: set[str] = set()
         self.results: dict[str, int] = {}      # return code of each finished store/load, by request
+        # layer-wise mode (connector "cache.layerwise"): per-step async handles
+        self.layer_index: dict[str, int] = {}
+        self._load_stream = None
+        self._save_stream = None
+        self._layer_load: "cc.AsyncTransfer | None" = None
+        self._layer_store: "cc.AsyncTransfer | None" = None
+        self._layer_store_ids: list[str] = []
+        self._layer_load_futures: list[Future] = []
 
     def _block_hashes_to_keys(self, block_hashes: list[bytes]) -> list[bytes]:
         return list(striding_block_hashes(block_hashes, self.blocks_in_chunk))
 
     def register(self, kv_caches: dict[str, torch.Tensor]) -> None:
+        self.layer_index = {name: i for i, name in enumerate(kv_caches)}
         layout, kp, vp = cc.layout_from_kv_tensors(kv_caches.values())
         ensure_cache(self.pool_size)
         self.worker = cc.Worker(self.model_name, layout, kp, vp, node_id=self.device,
@@ -144,6 +153,7 @@ class WorkerAdapter:
         self.worker.register()
 
     def unregister(self) -> None:
+        self.end_layerwise_step()
         self._pool.shutdown(wait=True)
         if self.worker is not None:
             self.worker.unregister()
@@ -175,6 +185,67 @@ class WorkerAdapter:
             block_ids.extend(op.block_ids)
         fut = self._submit(self.worker.load, keys, block_ids)
         self.load_futures[request_ids[0]] = (fut, request_ids[1:])
+
+    # ---- layer-wise transfers -------------------------------------------
+    # The load of a step runs layer by layer on a side stream while the
+    # forward pass runs; wait_layer makes the compute stream wait, on the
+    # GPU, for one layer.  The store of a step gathers each layer right after
+    # the forward wrote it (save_layer), on another side stream, gated on an
+    # event of the compute stream; end_layerwise_step hands the store to the
+    # worker thread, whose completion get_finished reports as for store_requests.
+    def _streams(self):
+        if self._load_stream is None:
+            self._load_stream = torch.cuda.Stream(self.device)
+            self._save_stream = torch.cuda.Stream(self.device)
+
+    def begin_layerwise_load(self, request_ids: list[str], ops: list[LoadStoreOp]) -> None:
+        keys, block_ids = [], []
+        for op in ops:
+            keys.extend(self._block_hashes_to_keys(op.block_hashes))
+            block_ids.extend(op.block_ids)
+        if not keys:
+            return
+        self._streams()
+        # blocks handed to this load may have been read by kernels still queued
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(self.device))
+        h = self.worker.load_async(keys, block_ids)
+        if h.missing:
+            logger.error("Layer-wise load for %s: some records are no longer cached", request_ids)
+        for l in range(self.worker.layout.num_layers):
+            h.layers(l, l + 1, stream=self._load_stream, wait_event=ready if l == 0 else None)
+        self._layer_load = h
+
+    def wait_layer(self, layer_name: str) -> None:
+        if self._layer_load is not None:
+            self._layer_load.stream_wait(self.layer_index[layer_name], torch.cuda.current_stream(self.device))
+
+    def save_layer(self, layer_name: str, request_ids: list[str], ops: list[LoadStoreOp]) -> None:
+        if self._layer_store is None:
+            keys, block_ids = [], []
+            for op in ops:
+                keys.extend(self._block_hashes_to_keys(op.block_hashes))
+                block_ids.extend(op.block_ids)
+            if not keys:
+                return
+            self._streams()
+            self._layer_store = self.worker.store_async(keys, block_ids)
+            self._layer_store_ids = list(request_ids)
+        written = torch.cuda.Event()
+        written.record(torch.cuda.current_stream(self.device))
+        l = self.layer_index[layer_name]
+        self._layer_store.layers(l, l + 1, stream=self._save_stream, wait_event=written)
+
+    def end_layerwise_step(self) -> None:
+        if self._layer_store is not None:
+            ids = self._layer_store_ids
+            self.store_futures[ids[0]] = (self._pool.submit(self._layer_store.finish), ids[1:])
+            self._layer_store = None
+        if self._layer_load is not None:
+            # records stay pinned until the copies end; nothing to report
+            self._layer_load_futures = [f for f in self._layer_load_futures if not f.done()]
+            self._layer_load_futures.append(self._pool.submit(self._layer_load.finish))
+            self._layer_load = None
 
     def lookup_agreed(self, keys_per_request: list[list[bytes]]) -> np.ndarray:
         """Per-request hit keys on this rank, min-reduced over the TP group."""

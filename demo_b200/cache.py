@@ -167,11 +167,79 @@ class Worker:
         if ret:
             raise CacheError("cache_clear", ret)
 
+    def load_async(self, keys: Sequence[bytes], block_ids: Sequence[int]) -> "AsyncTransfer":
+        """cache_load_async: pins the cached records of `keys` (the others are
+        skipped; .missing says whether any was); move them with .layers()."""
+        return self._async(lib.cache_load_async, keys, block_ids)
+
+    def store_async(self, keys: Sequence[bytes], block_ids: Sequence[int]) -> "AsyncTransfer":
+        """cache_store_async: reserves records for the new keys; move them
+        with .layers() (every layer, or .finish() drops them)."""
+        return self._async(lib.cache_store_async, keys, block_ids)
+
+    def _async(self, fn, keys, block_ids) -> "AsyncTransfer":
+        kb = _keys_buffer(keys)
+        b = np.ascontiguousarray(np.asarray(block_ids, dtype=np.uint64))
+        h = C.c_void_p()
+        ret = fn(C.byref(self.ctx), kb, KEY_LEN, b.ctypes.data, len(b), C.byref(h))
+        if ret and ret != -errno.ENOENT:
+            raise CacheError(fn.__name__, ret)
+        return AsyncTransfer(h, missing=ret == -errno.ENOENT)
+
     def flush(self) -> None:
         """cache_flush: wait for the disk writes of every stored record."""
         ret = lib.cache_flush(C.byref(self.ctx))
         if ret:
             raise CacheError("cache_flush", ret)
+
+
+def _handle(x) -> int | None:
+    """cudaStream_t / cudaEvent_t of a torch stream or event, an int, or None"""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    for attr in ("cuda_stream", "cuda_event"):
+        if hasattr(x, attr):
+            return getattr(x, attr)
+    raise TypeError(f"not a CUDA stream or event: {x!r}")
+
+
+class AsyncTransfer:
+    """Handle of cache_load_async / cache_store_async."""
+
+    def __init__(self, handle: C.c_void_p, missing: bool = False):
+        self._h = handle
+        self.missing = missing
+
+    @property
+    def records(self) -> int:
+        return lib.cache_async_records(self._h)
+
+    def layers(self, begin: int, end: int, stream=None, wait_event=None) -> None:
+        """enqueue layers [begin, end) on `stream` after `wait_event`"""
+        ret = lib.cache_async_layers(self._h, begin, end, _handle(stream), _handle(wait_event))
+        if ret:
+            raise CacheError("cache_async_layers", ret)
+
+    def stream_wait(self, layer: int, stream=None) -> None:
+        """make `stream` wait on the GPU for the copy covering `layer`"""
+        ret = lib.cache_async_stream_wait(self._h, layer, _handle(stream))
+        if ret:
+            raise CacheError("cache_async_stream_wait", ret)
+
+    def query(self) -> bool:
+        ret = lib.cache_async_query(self._h)
+        if ret < 0:
+            raise CacheError("cache_async_query", ret)
+        return ret == 1
+
+    def finish(self) -> int:
+        """cache_async_finish: 0 or a negative errno; the handle is released"""
+        if self._h is None:
+            return 0
+        h, self._h = self._h, None
+        return lib.cache_async_finish(h)
 
 
 def layout_from_kv_tensors(kv_caches, tp_heads: int | None = None) -> tuple[KVLayout, list[int], list[int] | None]:

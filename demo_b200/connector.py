@@ -16,6 +16,12 @@ reference server's default, src/main.c:428).  With "cache.server.host"
 the reference connector reads them (crosscache_connector.py:334-341), both
 roles talk to a CrossCache server (python -m demo_b200.server) through the
 adapters of demo_b200.remote instead of running the cache in-process.
+"cache.layerwise": true (in-process only) turns on the layer pipeline the
+reference leaves as no-ops (crosscache_connector.py:381-413): hits are
+loaded inside the step that computes the request (load_async False), layer
+by layer on a side stream, each attention layer waiting on the GPU for its
+own layer (wait_for_layer_load); stores gather each layer as soon as the
+forward has written it (save_kv_layer).
 """
 from __future__ import annotations
 
@@ -168,6 +174,10 @@ class CrossCacheConnector(KVConnectorBase_V1):
         self.vllm_block_size = vllm_config.cache_config.block_size
         host = vllm_config.kv_transfer_config.get_from_extra_config("cache.server.host", None)
         self._remote = host is not None
+        self._layerwise = bool(vllm_config.kv_transfer_config.get_from_extra_config("cache.layerwise", False))
+        if self._layerwise and self._remote:
+            raise ValueError("cache.layerwise needs the in-process cache (no cache.server.host)")
+        self._step_stores: tuple[list[str], list[LoadStoreOp]] | None = None
         if self._remote:
             import zmq
 
@@ -200,10 +210,24 @@ class CrossCacheConnector(KVConnectorBase_V1):
             _LOCAL_WORKERS[self._model] = self.worker_adapter
 
     def wait_for_layer_load(self, layer_name: str) -> None:
-        return
+        if self._layerwise:
+            self.worker_adapter.wait_layer(layer_name)
 
     def save_kv_layer(self, layer_name: str, kv_layer: torch.Tensor, attn_metadata, **kwargs: Any) -> None:
-        return
+        if not self._layerwise:
+            return
+        if self._step_stores is None:
+            metadata = self._get_connector_metadata()
+            assert isinstance(metadata, CacheConnectorMetadata)
+            ids, ops = [], []
+            for m in metadata.requests:
+                if m.direction == "STORE":
+                    ids.append(m.request_id)
+                    ops.append(m.op)
+            self._step_stores = (ids, ops)
+        ids, ops = self._step_stores
+        if ids:
+            self.worker_adapter.save_layer(layer_name, ids, ops)
 
     def start_load_kv(self, forward_context: "ForwardContext", **kwargs: Any) -> None:
         metadata = self._get_connector_metadata()
@@ -214,9 +238,19 @@ class CrossCacheConnector(KVConnectorBase_V1):
                 ids.append(m.request_id)
                 ops.append(m.op)
         if ids:
-            self.worker_adapter.load_requests(ids, ops)
+            if self._layerwise:
+                self.worker_adapter.begin_layerwise_load(ids, ops)
+            else:
+                self.worker_adapter.load_requests(ids, ops)
 
     def wait_for_save(self):
+        if self._layerwise:
+            layered = self._step_stores is not None
+            self._step_stores = None
+            self.worker_adapter.end_layerwise_step()
+            if layered:
+                return
+            # no save_kv_layer call this step: store whole records instead
         metadata = self._get_connector_metadata()
         assert isinstance(metadata, CacheConnectorMetadata)
         ids, ops = [], []
@@ -263,7 +297,8 @@ class CrossCacheConnector(KVConnectorBase_V1):
         tracker.num_vllm_hit_blocks = num_vllm_blocks
         tracker.num_cache_hit_blocks = num_cache_blocks
         need_to_load = max(0, ret - num_computed_tokens)
-        return need_to_load, need_to_load > 0
+        # layer-wise: loaded inside the step that computes the request
+        return need_to_load, need_to_load > 0 and not self._layerwise
 
     def update_state_after_alloc(self, request: "Request", blocks: "KVCacheBlocks", num_external_tokens: int):
         tracker = self._get_request_tracker(request.request_id)

@@ -1001,3 +1001,253 @@ int cache_clear(struct worker_context *wctx)
     pthread_mutex_unlock(&e->mu);
     return 0;
 }
+
+/* ---- asynchronous, layer-ordered store / load ------------------------ */
+
+struct cache_async {
+    struct rt_entry *e;
+    struct transfer_async *x;
+    int store;
+    uint32_t n;                /* records covered */
+    int64_t *idx;
+    uint8_t *keys;             /* store: KVMAP_KEY_LEN bytes per record */
+    uint8_t *layer_done;       /* store: one flag per layer */
+    uint32_t num_layers;
+    int status;                /* first device failure while enqueuing */
+};
+
+static void async_free(struct cache_async *h)
+{
+    free(h->idx);
+    free(h->keys);
+    free(h->layer_done);
+    free(h);
+}
+
+static int async_begin(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                       uint64_t *bids, uint32_t bnum, int store, cache_async_t **out)
+{
+    struct rt_entry *e;
+    struct cache_async *h;
+    struct transfer_batch tb;
+    uint64_t *tbids = NULL;
+    void **recs = NULL;
+    uint32_t bpc, key_num, i, misses = 0;
+    int ret = 0, err = 0, waited;
+
+    if (!out)
+        return -EINVAL;
+    *out = NULL;
+    e = get_entry(wctx);
+    if (!e)
+        return -ENOENT;
+    if (!keys || key_len < KVMAP_KEY_LEN || (bnum && !bids) || !wctx->k_ptrs)
+        return -EINVAL;
+    bpc = g_mgr.chunk_size / wctx->block_size;
+    key_num = bnum / bpc;
+    h = calloc(1, sizeof(*h));
+    if (!h)
+        return -ENOMEM;
+    h->e = e;
+    h->store = store;
+    h->num_layers = wctx->model.num_layers;
+    h->idx = malloc((key_num ? key_num : 1) * sizeof(int64_t));
+    h->keys = store ? malloc((key_num ? key_num : 1) * (size_t)KVMAP_KEY_LEN) : NULL;
+    h->layer_done = store ? calloc(h->num_layers, 1) : NULL;
+    tbids = malloc(((uint64_t)key_num * bpc + 1) * sizeof(uint64_t));
+    recs = malloc((key_num ? key_num : 1) * sizeof(void *));
+    if (!h->idx || (store && (!h->keys || !h->layer_done)) || !tbids || !recs) {
+        free(tbids);
+        free(recs);
+        async_free(h);
+        return -ENOMEM;
+    }
+
+    pthread_mutex_lock(&e->mu);
+    for (i = 0; i < key_num; i++) {
+        const uint8_t *key = keys + (uint64_t)i * key_len;
+        int64_t r;
+    again:
+        r = kvmap_find(e->map, key);
+        if (store) {
+            if (r >= 0) {
+                e->stats.store_dedup++;
+                continue;
+            }
+            r = alloc_record_locked(e, &waited);
+            if (waited)
+                goto again;
+            if (r < 0) {
+                ret = -ENOMEM;
+                break;
+            }
+            kvmap_insert(e->map, r, key, KVMAP_PENDING);
+            memcpy(h->keys + (uint64_t)h->n * KVMAP_KEY_LEN, key, KVMAP_KEY_LEN);
+        } else {
+            if (r < 0 || kvmap_state(e->map, r) != KVMAP_READY) {
+                e->stats.load_misses++;
+                misses++;
+                continue;
+            }
+            kvmap_touch(e->map, r);
+            kvmap_pin(e->map, r);
+        }
+        h->idx[h->n] = r;
+        recs[h->n] = mempool_addr(e->pool, r);
+        memcpy(tbids + (uint64_t)h->n * bpc, bids + (uint64_t)i * bpc, bpc * sizeof(uint64_t));
+        h->n++;
+    }
+    pthread_mutex_unlock(&e->mu);
+
+    memset(&tb, 0, sizeof(tb));
+    tb.keys_ptrs = wctx->k_ptrs;
+    tb.value_ptrs = wctx->v_ptrs;
+    tb.page_buffer_size = (uint64_t)wctx->num_blocks * wctx->block_size;
+    tb.records = recs;
+    tb.block_ids = tbids;
+    tb.num_records = h->n;
+    tb.block_size = wctx->block_size;
+    tb.hidden_dim_size = wctx->model.hidden_dim_size;
+    tb.num_layers = wctx->model.num_layers;
+    tb.num_tokens = (uint16_t)g_mgr.chunk_size;
+    tb.devid = wctx->node_id;
+    tb.caches_element_size = wctx->model.element_size;
+    tb.direction = store ? KV_D_TO_H : KV_H_TO_D;
+    h->x = ret ? NULL : transfer_async_begin(g_mgr.adaptor, &tb, &err);
+    free(tbids);
+    free(recs);
+    if (!h->x) {
+        if (!ret)
+            ret = err ? err : -EIO;
+        pthread_mutex_lock(&e->mu);
+        for (i = 0; i < h->n; i++) {
+            if (store) {
+                kvmap_remove(e->map, h->idx[i]);
+                mempool_free_index(e->pool, h->idx[i]);
+            } else {
+                kvmap_unpin(e->map, h->idx[i]);
+            }
+        }
+        pthread_mutex_unlock(&e->mu);
+        async_free(h);
+        return ret;
+    }
+    *out = h;
+    return misses ? -ENOENT : 0;
+}
+
+int cache_load_async(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                     uint64_t *bids, uint32_t bnum, cache_async_t **out)
+{
+    return async_begin(wctx, keys, key_len, bids, bnum, 0, out);
+}
+
+int cache_store_async(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                      uint64_t *bids, uint32_t bnum, cache_async_t **out)
+{
+    return async_begin(wctx, keys, key_len, bids, bnum, 1, out);
+}
+
+int cache_async_layers(cache_async_t *h, uint32_t layer_begin, uint32_t layer_end,
+                       void *stream, void *wait_event)
+{
+    uint32_t l;
+    int ret;
+
+    if (!h || layer_begin >= layer_end || layer_end > h->num_layers)
+        return -EINVAL;
+    ret = transfer_async_layers(g_mgr.adaptor, h->x, layer_begin, layer_end, stream, wait_event);
+    if (ret) {
+        /* a rejected request (-EINVAL) enqueued nothing; a device failure
+         * fails the whole handle (a store missing layers fails anyway) */
+        if (ret != -EINVAL && !h->status)
+            h->status = ret;
+        return ret;
+    }
+    if (h->store)
+        for (l = layer_begin; l < layer_end; l++)
+            h->layer_done[l] = 1;
+    return 0;
+}
+
+int cache_async_stream_wait(cache_async_t *h, uint32_t layer, void *stream)
+{
+    if (!h)
+        return -EINVAL;
+    return transfer_async_stream_wait(g_mgr.adaptor, h->x, layer, stream);
+}
+
+int cache_async_query(cache_async_t *h)
+{
+    if (!h)
+        return -EINVAL;
+    return transfer_async_query(g_mgr.adaptor, h->x);
+}
+
+uint32_t cache_async_records(const cache_async_t *h)
+{
+    return h ? h->n : 0;
+}
+
+int cache_async_finish(cache_async_t *h)
+{
+    struct rt_entry *e;
+    const uint8_t **wkeys = NULL;
+    uint32_t i, l, nw = 0;
+    int64_t *widx = NULL;
+    int ret, complete = 1;
+
+    if (!h)
+        return -EINVAL;
+    e = h->e;
+    ret = transfer_async_end(g_mgr.adaptor, h->x);
+    if (ret == -ETIMEDOUT) {
+        /* the device may still touch these records: keep them pinned / pending */
+        log_error("async %s of %u records timed out; records stay reserved",
+                  h->store ? "store" : "load", h->n);
+        async_free(h);
+        return ret;
+    }
+    if (!ret && h->status)
+        ret = h->status;
+    if (h->store) {
+        for (l = 0; l < h->num_layers; l++)
+            complete = complete && h->layer_done[l];
+        if (!ret && !complete && h->n)
+            ret = -EINVAL;             /* a record needs every layer */
+        if (!ret && h->n && e->dfd >= 0) {
+            wkeys = malloc(h->n * sizeof(*wkeys));
+            widx = malloc(h->n * sizeof(*widx));
+        }
+    }
+    pthread_mutex_lock(&e->mu);
+    for (i = 0; i < h->n; i++) {
+        if (!h->store) {
+            kvmap_unpin(e->map, h->idx[i]);
+            if (!ret) {
+                e->stats.loaded++;
+                e->stats.bytes_loaded += e->objsize;
+            }
+        } else if (!ret) {
+            kvmap_publish(e->map, h->idx[i]);
+            e->stats.stored++;
+            e->stats.bytes_saved += e->objsize;
+            if (wkeys && widx) {
+                kvmap_pin(e->map, h->idx[i]);
+                e->disk_pending++;
+                wkeys[nw] = h->keys + (uint64_t)i * KVMAP_KEY_LEN;
+                widx[nw++] = h->idx[i];
+            }
+        } else {
+            kvmap_remove(e->map, h->idx[i]);
+            mempool_free_index(e->pool, h->idx[i]);
+        }
+    }
+    pthread_mutex_unlock(&e->mu);
+    if (nw)
+        submit_writes(e, widx, wkeys, nw);
+    free(wkeys);
+    free(widx);
+    async_free(h);
+    return ret;
+}

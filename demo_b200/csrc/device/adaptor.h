@@ -25,6 +25,14 @@ public:
     virtual int TransferKVCache(struct transfer_params *params) = 0;
     virtual int TransferKVCacheBatch(struct transfer_batch *batch) = 0;
     virtual void Reset(uint8_t nid) = 0;
+
+    /* asynchronous layer-ranged transfers (include/device.h) */
+    virtual struct transfer_async *AsyncBegin(const struct transfer_batch *batch, int *err) = 0;
+    virtual int AsyncLayers(struct transfer_async *h, uint32_t l0, uint32_t l1, void *stream,
+                            void *wait_event) = 0;
+    virtual int AsyncStreamWait(struct transfer_async *h, uint32_t layer, void *stream) = 0;
+    virtual int AsyncQuery(struct transfer_async *h) = 0;
+    virtual int AsyncEnd(struct transfer_async *h) = 0;
 };
 
 /* launches of this library's kernels (all devices) */

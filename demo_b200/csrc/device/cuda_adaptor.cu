@@ -229,12 +229,115 @@ struct Lane {
     }
 };
 
+/* one asynchronous layer-ranged transfer (transfer_async_*): its metadata
+ * (block ids, record addresses), error word and one event per enqueued
+ * layer range.  Reused through a per-device free list. */
+struct AsyncOp {
+    struct Mark {
+        uint32_t l0, l1;
+        cudaEvent_t ev;
+    };
+    int dev = -1;
+    cudaStream_t own = nullptr;      /* error readback only */
+    cudaEvent_t uploaded = nullptr;
+    cudaStream_t upload_stream = nullptr;
+    bool is_uploaded = false;
+    uint64_t *d_meta = nullptr;
+    uint64_t *h_meta = nullptr;
+    uint64_t meta_cap = 0;
+    uint64_t meta_words = 0;
+    int32_t *d_err = nullptr;
+    int32_t *h_err = nullptr;
+    std::vector<Mark> marks;
+    std::vector<cudaEvent_t> spare;
+    kv_copy_desc base{};
+    uint32_t total_layers = 0;
+    bool poisoned = false;
+
+    bool init(int device)
+    {
+        dev = device;
+        return CU_OK(cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking)) &&
+               CU_OK(cudaEventCreateWithFlags(&uploaded, cudaEventDisableTiming)) &&
+               CU_OK(cudaMalloc(&d_err, sizeof(int32_t))) &&
+               CU_OK(cudaHostAlloc(&h_err, sizeof(int32_t), cudaHostAllocDefault));
+    }
+
+    bool ensure_meta(uint64_t words)
+    {
+        if (words <= meta_cap)
+            return true;
+        uint64_t cap = std::max<uint64_t>(words, std::max<uint64_t>(1024, meta_cap * 2));
+        if (d_meta)
+            cudaFree(d_meta);
+        if (h_meta)
+            cudaFreeHost(h_meta);
+        d_meta = nullptr;
+        h_meta = nullptr;
+        meta_cap = 0;
+        if (!CU_OK(cudaMalloc(&d_meta, cap * 8)) || !CU_OK(cudaHostAlloc(&h_meta, cap * 8, cudaHostAllocDefault)))
+            return false;
+        meta_cap = cap;
+        return true;
+    }
+
+    cudaEvent_t take_event()
+    {
+        if (!spare.empty()) {
+            cudaEvent_t e = spare.back();
+            spare.pop_back();
+            return e;
+        }
+        cudaEvent_t e = nullptr;
+        return CU_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming)) ? e : nullptr;
+    }
+
+    void reset_for_reuse()
+    {
+        for (auto &m : marks)
+            spare.push_back(m.ev);
+        marks.clear();
+        is_uploaded = false;
+        upload_stream = nullptr;
+        meta_words = 0;
+        base = kv_copy_desc{};
+        total_layers = 0;
+    }
+
+    void release()
+    {
+        if (dev < 0)
+            return;
+        cudaSetDevice(dev);
+        if (own)
+            cudaStreamSynchronize(own);
+        reset_for_reuse();
+        for (cudaEvent_t e : spare)
+            cudaEventDestroy(e);
+        spare.clear();
+        if (uploaded)
+            cudaEventDestroy(uploaded);
+        if (d_meta)
+            cudaFree(d_meta);
+        if (h_meta)
+            cudaFreeHost(h_meta);
+        if (d_err)
+            cudaFree(d_err);
+        if (h_err)
+            cudaFreeHost(h_err);
+        if (own)
+            cudaStreamDestroy(own);
+        *this = AsyncOp();
+    }
+};
+
 struct DeviceCtx {
     int dev;
     std::mutex mu;
     std::condition_variable cv;
     std::vector<Lane *> all;
     std::vector<Lane *> idle;
+    std::vector<AsyncOp *> async_idle;   /* finished async ops, reusable */
     int max_lanes;
     int host_ptr_ok = 0;   /* registered host memory usable at its host address */
 };
@@ -272,6 +375,7 @@ public:
         lanes_per_dev_ = std::max(1, env_int("CROSSCACHE_LANES", 2));
         const char *m = getenv("CROSSCACHE_XFER_MODE");
         direct_ = m && !strcmp(m, "direct");
+        async_ctas_ = (uint32_t)std::max(1, env_int("CROSSCACHE_ASYNC_CTAS", 32));
     }
 
     ~CudaAdaptor() override
@@ -420,6 +524,12 @@ public:
 
     int TransferKVCache(struct transfer_params *p) override;
     int TransferKVCacheBatch(struct transfer_batch *b) override;
+    struct transfer_async *AsyncBegin(const struct transfer_batch *b, int *err) override;
+    int AsyncLayers(struct transfer_async *h, uint32_t l0, uint32_t l1, void *stream,
+                    void *wait_event) override;
+    int AsyncStreamWait(struct transfer_async *h, uint32_t layer, void *stream) override;
+    int AsyncQuery(struct transfer_async *h) override;
+    int AsyncEnd(struct transfer_async *h) override;
 
     void Reset(uint8_t nid) override
     {
@@ -500,6 +610,12 @@ private:
         }
         ctx->all.clear();
         ctx->idle.clear();
+        /* async ops still held by callers stay theirs; the idle ones go */
+        for (AsyncOp *op : ctx->async_idle) {
+            op->release();
+            delete op;
+        }
+        ctx->async_idle.clear();
     }
 
     std::chrono::steady_clock::time_point deadline() const
@@ -540,6 +656,7 @@ private:
     int finish(Lane *l, cudaStream_t last, int ret);
 
     int num_devices_ = 0;
+    uint32_t async_ctas_ = 32;
     int timeout_ms_ = 120000;
     int lanes_per_dev_ = 2;
     bool direct_ = false;
@@ -710,6 +827,202 @@ int CudaAdaptor::TransferKVCacheBatch(struct transfer_batch *b)
         cudaStreamSynchronize(l->cs);
     }
     give_back(ctx, l);
+    return ret;
+}
+
+/* ---- asynchronous layer-ranged transfers -------------------------------- */
+
+struct transfer_async *CudaAdaptor::AsyncBegin(const struct transfer_batch *b, int *err)
+{
+    auto fail = [&](int e) -> struct transfer_async * {
+        if (err)
+            *err = e;
+        return nullptr;
+    };
+    if (!b->keys_ptrs || (b->num_records && (!b->records || !b->block_ids)) || !b->block_size ||
+        !b->num_layers || !b->num_tokens || b->num_tokens % b->block_size || !b->hidden_dim_size ||
+        !b->caches_element_size || b->devid >= num_devices_)
+        return fail(-EINVAL);
+    if (!CU_OK(cudaSetDevice(b->devid)))
+        return fail(-EIO);
+    DeviceCtx *ctx = device(b->devid);
+    AsyncOp *op = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        if (!ctx->async_idle.empty()) {
+            op = ctx->async_idle.back();
+            ctx->async_idle.pop_back();
+        }
+    }
+    if (!op) {
+        op = new (std::nothrow) AsyncOp();
+        if (!op)
+            return fail(-ENOMEM);
+        if (!op->init(b->devid)) {
+            op->release();
+            delete op;
+            return fail(-EIO);
+        }
+    }
+    const uint32_t R = b->num_records;
+    const uint32_t bpr = b->num_tokens / b->block_size;
+    const bool device_recs = b->record_on_device != 0;
+    const uint64_t words = (uint64_t)R * bpr + R;
+    if (!op->ensure_meta(std::max<uint64_t>(words, 1))) {
+        op->release();
+        delete op;
+        return fail(-ENOMEM);
+    }
+    if (R)
+        memcpy(op->h_meta, b->block_ids, (uint64_t)R * bpr * 8);
+    for (uint32_t r = 0; r < R; r++) {
+        void *p = b->records[r];
+        if (!device_recs && !ctx->host_ptr_ok) {
+            void *dp = nullptr;
+            if (!CU_OK(cudaHostGetDevicePointer(&dp, p, 0))) {
+                op->reset_for_reuse();
+                std::lock_guard<std::mutex> lk(ctx->mu);
+                ctx->async_idle.push_back(op);
+                return fail(-EINVAL);
+            }
+            p = dp;
+        }
+        op->h_meta[(uint64_t)R * bpr + r] = (uint64_t)(uintptr_t)p;
+    }
+    op->meta_words = words;
+    kv_copy_desc &d = op->base;
+    d = kv_copy_desc{};
+    d.layer_k = static_cast<const uint64_t *>(b->keys_ptrs);
+    d.layer_v = static_cast<const uint64_t *>(b->value_ptrs);
+    d.error = op->d_err;
+    d.page_buffer_size = b->page_buffer_size;
+    d.unit_bytes = (uint32_t)((uint64_t)b->hidden_dim_size * b->caches_element_size);
+    d.num_tokens = b->num_tokens;
+    d.block_size = b->block_size;
+    d.num_records = R;
+    d.direction = b->direction ? 1 : 0;
+    d.block_ids = op->d_meta;
+    d.records = op->d_meta + (uint64_t)R * bpr;
+    d.record_layers = b->num_layers;
+    d.max_ctas = async_ctas_;
+    bool recs_aligned = device_recs;
+    for (uint32_t r = 0; recs_aligned && r < R; r++)
+        recs_aligned = (uintptr_t)b->records[r] % 16 == 0;
+    if (recs_aligned && layers_aligned(b->keys_ptrs) && layers_aligned(b->value_ptrs))
+        d.flags = KVCOPY_FLAG_BULK;     /* HBM records only: mapped host memory keeps the register path */
+    op->total_layers = b->num_layers;
+    return reinterpret_cast<struct transfer_async *>(op);
+}
+
+int CudaAdaptor::AsyncLayers(struct transfer_async *h, uint32_t l0, uint32_t l1, void *stream, void *wait_event)
+{
+    AsyncOp *op = reinterpret_cast<AsyncOp *>(h);
+    if (op->poisoned)
+        return -EIO;
+    if (l0 >= l1 || l1 > op->total_layers)
+        return -EINVAL;
+    if (!CU_OK(cudaSetDevice(op->dev)))
+        return -EIO;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (wait_event && !CU_OK(cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(wait_event), 0)))
+        return -EIO;
+    if (!op->is_uploaded) {
+        if (!CU_OK(cudaMemsetAsync(op->d_err, 0, sizeof(int32_t), s)) ||
+            !CU_OK(cudaMemcpyAsync(op->d_meta, op->h_meta, op->meta_words * 8, cudaMemcpyHostToDevice, s)) ||
+            !CU_OK(cudaEventRecord(op->uploaded, s)))
+            return -EIO;
+        op->is_uploaded = true;
+        op->upload_stream = s;
+    } else if (s != op->upload_stream && !CU_OK(cudaStreamWaitEvent(s, op->uploaded, 0))) {
+        return -EIO;
+    }
+    if (op->base.num_records) {
+        kv_copy_desc d = op->base;
+        d.layer_begin = l0;
+        d.num_layers = l1 - l0;
+        int ret = kv_copy_launch(&d, s);
+        if (ret)
+            return ret;
+    }
+    cudaEvent_t ev = op->take_event();
+    if (!ev || !CU_OK(cudaEventRecord(ev, s))) {
+        if (ev)
+            op->spare.push_back(ev);
+        return -EIO;
+    }
+    op->marks.push_back(AsyncOp::Mark{l0, l1, ev});
+    return 0;
+}
+
+int CudaAdaptor::AsyncStreamWait(struct transfer_async *h, uint32_t layer, void *stream)
+{
+    AsyncOp *op = reinterpret_cast<AsyncOp *>(h);
+    for (auto it = op->marks.rbegin(); it != op->marks.rend(); ++it) {
+        if (layer >= it->l0 && layer < it->l1) {
+            if (!CU_OK(cudaSetDevice(op->dev)) ||
+                !CU_OK(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), it->ev, 0)))
+                return -EIO;
+            return 0;
+        }
+    }
+    return -ENOENT;
+}
+
+int CudaAdaptor::AsyncQuery(struct transfer_async *h)
+{
+    AsyncOp *op = reinterpret_cast<AsyncOp *>(h);
+    if (op->poisoned)
+        return -EIO;
+    cudaSetDevice(op->dev);
+    for (auto &m : op->marks) {
+        cudaError_t e = cudaEventQuery(m.ev);
+        if (e == cudaErrorNotReady)
+            return 0;
+        if (e != cudaSuccess)
+            return -EIO;
+    }
+    return 1;
+}
+
+int CudaAdaptor::AsyncEnd(struct transfer_async *h)
+{
+    AsyncOp *op = reinterpret_cast<AsyncOp *>(h);
+    if (op->poisoned)
+        return -EIO;
+    if (!CU_OK(cudaSetDevice(op->dev)))
+        return -EIO;
+    int ret = 0;
+    auto dl = deadline();
+    for (auto &m : op->marks) {
+        int w = wait_event(m.ev, dl);
+        if (w == -ETIMEDOUT) {
+            log_error("device(%d) async transfer timed out after %d ms", op->dev, timeout_ms_);
+            op->poisoned = true;     /* its memory may still be in use: never reused or freed */
+            return -ETIMEDOUT;
+        }
+        if (w && !ret)
+            ret = w;
+    }
+    if (op->is_uploaded && ret == 0) {
+        /* every mark (and the upload with the error-word reset) has completed on
+         * the host's clock, so this readback comes after every kernel */
+        int w = wait_event(op->uploaded, dl);
+        if (w == -ETIMEDOUT) {
+            op->poisoned = true;
+            return -ETIMEDOUT;
+        }
+        if (w || !CU_OK(cudaMemcpyAsync(op->h_err, op->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, op->own)) ||
+            !CU_OK(cudaStreamSynchronize(op->own)))
+            ret = -EIO;
+        if (ret == 0 && *op->h_err) {
+            log_error("device(%d) async kv copy reported error bits 0x%x", op->dev, *op->h_err);
+            ret = -EINVAL;
+        }
+    }
+    op->reset_for_reuse();
+    DeviceCtx *ctx = device(op->dev);
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ctx->async_idle.push_back(op);
     return ret;
 }
 

@@ -51,6 +51,37 @@ int transfer_kvcache_batch(adaptor_t *adaptor, struct transfer_batch *batch)
     return (adaptor && batch) ? adaptor->TransferKVCacheBatch(batch) : -EINVAL;
 }
 
+struct transfer_async *transfer_async_begin(adaptor_t *adaptor, const struct transfer_batch *batch, int *err)
+{
+    if (!adaptor || !batch) {
+        if (err)
+            *err = -EINVAL;
+        return nullptr;
+    }
+    return adaptor->AsyncBegin(batch, err);
+}
+
+int transfer_async_layers(adaptor_t *adaptor, struct transfer_async *h, uint32_t layer_begin,
+                          uint32_t layer_end, void *stream, void *wait_event)
+{
+    return (adaptor && h) ? adaptor->AsyncLayers(h, layer_begin, layer_end, stream, wait_event) : -EINVAL;
+}
+
+int transfer_async_stream_wait(adaptor_t *adaptor, struct transfer_async *h, uint32_t layer, void *stream)
+{
+    return (adaptor && h) ? adaptor->AsyncStreamWait(h, layer, stream) : -EINVAL;
+}
+
+int transfer_async_query(adaptor_t *adaptor, struct transfer_async *h)
+{
+    return (adaptor && h) ? adaptor->AsyncQuery(h) : -EINVAL;
+}
+
+int transfer_async_end(adaptor_t *adaptor, struct transfer_async *h)
+{
+    return (adaptor && h) ? adaptor->AsyncEnd(h) : -EINVAL;
+}
+
 void reset_device(adaptor_t *adaptor, uint8_t nid)
 {
     if (adaptor)

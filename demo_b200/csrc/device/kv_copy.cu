@@ -83,10 +83,13 @@ struct Params {
     uint32_t num_tokens;
     uint32_t block_size;
     uint32_t bpr;            /* blocks per record */
-    uint32_t num_layers;
+    uint32_t num_layers;     /* layers this launch copies */
     uint32_t num_kv;
     uint32_t tile_tokens;
     uint32_t num_tiles;
+    uint32_t layer0;         /* first record layer this launch copies */
+    uint32_t rec_layers;     /* layers a record holds */
+    uint32_t max_grid;       /* CTA cap, 0 = none */
     FastDiv div_vpu, div_bs, div_tpl, div_layers, div_kv;
 };
 
@@ -156,7 +159,7 @@ __global__ void __launch_bounds__(Shape::threads, Shape::min_blocks) kv_copy_ker
         uint32_t n = min(p.tile_tokens, p.num_tokens - t0);
         uint8_t *layer = reinterpret_cast<uint8_t *>((kv ? p.layer_v : p.layer_k)[l]);
         uint8_t *rec = reinterpret_cast<uint8_t *>(p.records[r]) +
-                       (((uint64_t)kv * p.num_layers + l) * p.num_tokens + t0) * p.unit;
+                       (((uint64_t)kv * p.rec_layers + p.layer0 + l) * p.num_tokens + t0) * p.unit;
         if (!layer) {
             if (threadIdx.x == 0 && p.error)
                 atomicOr(p.error, KVCOPY_ERR_NULL_LAYER);
@@ -224,6 +227,8 @@ int launch_variant(const Params &p, cudaStream_t stream)
         sm_count[dev] = sms > 0 ? sms : 1;
     });
     uint64_t grid = (uint64_t)sm_count[dev] * blocks_per_sm[dev];
+    if (p.max_grid && grid > p.max_grid)
+        grid = p.max_grid;
     if (grid > p.num_tiles)
         grid = p.num_tiles;
     kv_copy_kernel<VEC, TO_RECORD, Shape><<<(unsigned)grid, kThreads, 0, stream>>>(p);
@@ -282,9 +287,12 @@ struct BulkParams {
     uint64_t layer_rec_bytes;   /* num_tokens * unit: one layer of one record part */
     uint32_t bpr;               /* blocks per record */
     uint32_t gpt;               /* blocks per tile */
-    uint32_t num_layers;
+    uint32_t num_layers;        /* layers this launch copies */
     uint32_t num_kv;
     uint32_t num_tiles;
+    uint32_t layer0;            /* first record layer this launch copies */
+    uint32_t rec_layers;        /* layers a record holds */
+    uint32_t max_grid;          /* CTA cap, 0 = none */
     FastDiv div_tpl, div_layers, div_kv;
 };
 
@@ -366,7 +374,7 @@ __device__ __forceinline__ BulkTile bulk_decode(const BulkParams &p, uint32_t w)
     uint32_t b0 = g * p.gpt;
     t.nb = min(p.gpt, p.bpr - b0);
     t.layer = reinterpret_cast<uint8_t *>((kv ? p.layer_v : p.layer_k)[l]);
-    t.rec = reinterpret_cast<uint8_t *>(p.records[r]) + ((uint64_t)kv * p.num_layers + l) * p.layer_rec_bytes +
+    t.rec = reinterpret_cast<uint8_t *>(p.records[r]) + ((uint64_t)kv * p.rec_layers + p.layer0 + l) * p.layer_rec_bytes +
             (uint64_t)b0 * p.run_bytes;
     t.bids = p.block_ids + (uint64_t)r * p.bpr + b0;
     return t;
@@ -479,6 +487,8 @@ int launch_bulk(const BulkParams &bp, bool to_record, cudaStream_t stream)
     if (attr_err[dev] != cudaSuccess)
         return -EIO;
     uint32_t grid = (uint32_t)sm_count[dev];
+    if (bp.max_grid && grid > bp.max_grid)
+        grid = bp.max_grid;
     if (grid > bp.num_tiles)
         grid = bp.num_tiles;
     if (to_record)
@@ -519,14 +529,23 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
         return 0;
     if (!d->slots && (!d->block_ids || d->num_tokens % d->block_size))
         return -EINVAL;
+    const uint32_t rec_layers = d->record_layers ? d->record_layers : d->num_layers;
+    if ((uint64_t)d->layer_begin + d->num_layers > rec_layers)
+        return -EINVAL;
+    /* the layer pointer arrays are indexed from the first layer copied */
+    const uint64_t *lk = d->layer_k + d->layer_begin;
+    const uint64_t *lv = d->layer_v ? d->layer_v + d->layer_begin : nullptr;
 
     const uint64_t run_bytes = (uint64_t)d->block_size * d->unit_bytes;
     if ((d->flags & KVCOPY_FLAG_BULK) && !d->slots && d->unit_bytes % 16 == 0 &&
         run_bytes >= kBulkMinRunBytes && run_bytes <= kBulkTileBytes &&
         d->page_buffer_size % d->block_size == 0 && bulk_allowed_by_env()) {
         BulkParams bp{};
-        bp.layer_k = d->layer_k;
-        bp.layer_v = d->layer_v;
+        bp.layer_k = lk;
+        bp.layer_v = lv;
+        bp.layer0 = d->layer_begin;
+        bp.rec_layers = rec_layers;
+        bp.max_grid = d->max_ctas;
         bp.records = d->records;
         bp.block_ids = d->block_ids;
         bp.error = d->error;
@@ -551,8 +570,11 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
     }
 
     Params p{};
-    p.layer_k = d->layer_k;
-    p.layer_v = d->layer_v;
+    p.layer_k = lk;
+    p.layer_v = lv;
+    p.layer0 = d->layer_begin;
+    p.rec_layers = rec_layers;
+    p.max_grid = d->max_ctas;
     p.records = d->records;
     p.slots = d->slots;
     p.block_ids = d->block_ids;

@@ -22,6 +22,8 @@ extern "C" {
 #include <cstring>
 #include <new>
 #include <sys/mman.h>
+#include <utility>
+#include <vector>
 
 namespace {
 
@@ -31,16 +33,19 @@ struct RecordJob {
     cc_latch_t *latch;
 };
 
-/* copy one record; slot(t) from per-token slots or from block ids */
+/* copy record layers [l0, l1) of one record holding L layers; slot(t) from
+ * per-token slots or from block ids */
 int copy_record(uint8_t *rec, const uint64_t *kl, const uint64_t *vl,
                 const int64_t *slots, const uint64_t *bids, uint32_t bs,
                 uint64_t page_buffer_size, uint32_t L, uint32_t C,
-                uint64_t unit, bool to_record)
+                uint64_t unit, bool to_record, uint32_t l0 = 0, uint32_t l1 = UINT32_MAX)
 {
     const int nkv = vl ? 2 : 1;
+    if (l1 > L)
+        l1 = L;
     for (int kv = 0; kv < nkv; kv++) {
         const uint64_t *layers = kv ? vl : kl;
-        for (uint32_t l = 0; l < L; l++) {
+        for (uint32_t l = l0; l < l1; l++) {
             uint8_t *base = reinterpret_cast<uint8_t *>(layers[l]);
             uint8_t *rl = rec + ((uint64_t)kv * L + l) * C * unit;
             if (!base)
@@ -175,7 +180,84 @@ public:
 
     void Reset(uint8_t) override {}
 
+    /* asynchronous API, done synchronously: the copy happens in AsyncLayers */
+    struct transfer_async *AsyncBegin(const struct transfer_batch *tb, int *err) override
+    {
+        int e = 0;
+        if (!tb || (tb->num_records && (!tb->records || !tb->block_ids || !tb->keys_ptrs ||
+                                        !tb->block_size || tb->num_tokens % tb->block_size)))
+            e = -EINVAL;
+        MemAsync *h = e ? nullptr : new (std::nothrow) MemAsync();
+        if (!e && !h)
+            e = -ENOMEM;
+        if (e) {
+            if (err)
+                *err = e;
+            return nullptr;
+        }
+        h->tb = *tb;
+        const uint32_t bpr = tb->block_size ? tb->num_tokens / tb->block_size : 0;
+        h->recs.assign(tb->records, tb->records + tb->num_records);
+        h->bids.assign(tb->block_ids, tb->block_ids + (uint64_t)tb->num_records * bpr);
+        h->tb.records = h->recs.data();
+        h->tb.block_ids = h->bids.data();
+        return reinterpret_cast<struct transfer_async *>(h);
+    }
+
+    int AsyncLayers(struct transfer_async *ha, uint32_t l0, uint32_t l1, void *stream,
+                    void *wait_event) override
+    {
+        MemAsync *h = reinterpret_cast<MemAsync *>(ha);
+        const struct transfer_batch *tb = &h->tb;
+        if (stream || wait_event || l0 >= l1 || l1 > tb->num_layers)
+            return -EINVAL;
+        const uint32_t bpr = tb->num_tokens / tb->block_size;
+        const uint64_t unit = (uint64_t)tb->hidden_dim_size * tb->caches_element_size;
+        for (uint32_t r = 0; r < tb->num_records; r++) {
+            int ret = copy_record(static_cast<uint8_t *>(tb->records[r]),
+                                  static_cast<const uint64_t *>(tb->keys_ptrs),
+                                  static_cast<const uint64_t *>(tb->value_ptrs), nullptr,
+                                  tb->block_ids + (uint64_t)r * bpr, tb->block_size,
+                                  tb->page_buffer_size, tb->num_layers, tb->num_tokens, unit,
+                                  tb->direction, l0, l1);
+            if (ret) {
+                h->err = ret;
+                return 0;       /* reported by AsyncEnd, as the device backend does */
+            }
+        }
+        h->covered.push_back({l0, l1});
+        return 0;
+    }
+
+    int AsyncStreamWait(struct transfer_async *ha, uint32_t layer, void *stream) override
+    {
+        MemAsync *h = reinterpret_cast<MemAsync *>(ha);
+        if (stream)
+            return -EINVAL;
+        for (auto &rg : h->covered)
+            if (layer >= rg.first && layer < rg.second)
+                return 0;
+        return -ENOENT;
+    }
+
+    int AsyncQuery(struct transfer_async *) override { return 1; }
+
+    int AsyncEnd(struct transfer_async *ha) override
+    {
+        MemAsync *h = reinterpret_cast<MemAsync *>(ha);
+        int ret = h->err;
+        delete h;
+        return ret;
+    }
+
 private:
+    struct MemAsync {
+        struct transfer_batch tb;
+        std::vector<void *> recs;
+        std::vector<uint64_t> bids;
+        std::vector<std::pair<uint32_t, uint32_t>> covered;
+        int err = 0;
+    };
     threadpool_t *pool_;
 };
 

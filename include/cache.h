@@ -110,6 +110,47 @@ int cache_clear(struct worker_context *wctx);
  * disk tier it returns 0 at once. */
 int cache_flush(struct worker_context *wctx);
 
+/* ---- asynchronous, layer-ordered store / load (new) -------------------
+ * For a caller that overlaps the transfer with its own kernels layer by
+ * layer (vLLM's wait_for_layer_load / save_kv_layer).  The kernels move the
+ * records straight between the paged cache and the pinned host pool (no
+ * staging), each launch capped to a few CTAs (CROSSCACHE_ASYNC_CTAS, 32).
+ *
+ *   cache_load_async    pins the cached records of the keys (keys that are
+ *                       not cached are skipped: -ENOENT, with a valid handle
+ *                       for the others) and returns a handle; nothing moves
+ *                       yet.  Memory tier only.
+ *   cache_store_async   reserves a record per new key (keys already cached
+ *                       are skipped, as cache_store does); nothing moves yet.
+ *   cache_async_layers  enqueue the copy of layers [layer_begin, layer_end)
+ *                       on `stream` (cudaStream_t of the worker's device)
+ *                       after `wait_event` (cudaEvent_t or NULL).  The CPU
+ *                       backend copies at once and takes NULL for both.
+ *   cache_async_stream_wait
+ *                       make `stream` wait (on the GPU) for the enqueued
+ *                       copy covering `layer`; -ENOENT if none was enqueued.
+ *   cache_async_query   1 when all enqueued copies finished, 0 if not.
+ *   cache_async_finish  wait for them (deadline CROSSCACHE_TIMEOUT_MS) and
+ *                       release the handle.  A load unpins its records; a
+ *                       store publishes its records when every layer was
+ *                       enqueued and the kernels succeeded (then the disk
+ *                       tier writes them), else drops them.  0, -EINVAL
+ *                       (bad block id, or a store missing layers),
+ *                       -ETIMEDOUT (records stay reserved).
+ *   cache_async_records number of records the handle moves. */
+typedef struct cache_async cache_async_t;
+
+int cache_load_async(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                     uint64_t *bids, uint32_t bnum, cache_async_t **out);
+int cache_store_async(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                      uint64_t *bids, uint32_t bnum, cache_async_t **out);
+int cache_async_layers(cache_async_t *h, uint32_t layer_begin, uint32_t layer_end,
+                       void *stream, void *wait_event);
+int cache_async_stream_wait(cache_async_t *h, uint32_t layer, void *stream);
+int cache_async_query(cache_async_t *h);
+int cache_async_finish(cache_async_t *h);
+uint32_t cache_async_records(const cache_async_t *h);
+
 #ifdef __cplusplus
 }
 #endif

@@ -108,6 +108,39 @@ struct transfer_batch {
 
 int transfer_kvcache_batch(adaptor_t *adaptor, struct transfer_batch *batch);
 
+/* new: asynchronous, layer-ranged transfers of a batch (no reference
+ * counterpart; the reference moves whole records synchronously).  The
+ * kernels read or write the records where they are -- mapped pinned host
+ * memory, or HBM when record_on_device -- with no staging, so layers can
+ * move while the caller's kernels run.
+ *   transfer_async_begin   validate the batch and copy its block ids and
+ *                          record addresses aside; nothing runs yet.  NULL
+ *                          and *err = -errno on failure.
+ *   transfer_async_layers  on `stream` (a cudaStream_t of the batch's
+ *                          device), after `wait_event` (a cudaEvent_t, or
+ *                          NULL), copy record layers [layer_begin, layer_end)
+ *                          of every record; the launch is capped to a few
+ *                          CTAs (CROSSCACHE_ASYNC_CTAS, default 32).
+ *   transfer_async_stream_wait
+ *                          make `stream` wait for the copy that covered
+ *                          `layer` (-ENOENT if none has been enqueued).
+ *   transfer_async_query   1 when everything enqueued has finished, 0 if not.
+ *   transfer_async_end     wait (deadline CROSSCACHE_TIMEOUT_MS) for it,
+ *                          read the kernels' error bits and release the
+ *                          handle: 0, -EINVAL (bad block id), -ETIMEDOUT.
+ * The CPU (MEM) backend copies inside transfer_async_layers and takes NULL
+ * streams and events only. */
+struct transfer_async;
+
+struct transfer_async *transfer_async_begin(adaptor_t *adaptor, const struct transfer_batch *batch,
+                                            int *err);
+int transfer_async_layers(adaptor_t *adaptor, struct transfer_async *h, uint32_t layer_begin,
+                          uint32_t layer_end, void *stream, void *wait_event);
+int transfer_async_stream_wait(adaptor_t *adaptor, struct transfer_async *h, uint32_t layer,
+                               void *stream);
+int transfer_async_query(adaptor_t *adaptor, struct transfer_async *h);
+int transfer_async_end(adaptor_t *adaptor, struct transfer_async *h);
+
 /* new: CUDA counterpart of CrossCache's ipckey_from_tensor
  * (python/ipckey_utils.cpp:19-33, aclrtIpcMemGetExportKey, 64 bytes).
  * Writes the 72-byte key of device address dptr into key_out: the

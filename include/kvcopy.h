@@ -60,6 +60,12 @@ struct kv_copy_desc {
     uint32_t num_records;
     int32_t direction;           /* 1: paged -> record, 0: record -> paged   */
     uint32_t flags;              /* KVCOPY_FLAG_*                            */
+    /* layer sub-range (new): copy record layers [layer_begin, layer_begin +
+     * num_layers) of records holding record_layers layers (0: num_layers);
+     * layer_k / layer_v still list every layer of the cache */
+    uint32_t layer_begin;
+    uint32_t record_layers;
+    uint32_t max_ctas;           /* cap on the launch's CTAs, 0 = fill the GPU */
 };
 
 /* Launch the gather/scatter on `stream` (a cudaStream_t, NULL = legacy

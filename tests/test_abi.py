@@ -63,6 +63,7 @@ int main(void) {
   S(transfer_batch); F(transfer_batch, records); F(transfer_batch, num_records);
   F(transfer_batch, num_layers); F(transfer_batch, direction);
   S(kv_copy_desc); F(kv_copy_desc, page_buffer_size); F(kv_copy_desc, direction); F(kv_copy_desc, flags);
+  F(kv_copy_desc, layer_begin); F(kv_copy_desc, record_layers); F(kv_copy_desc, max_ctas);
   S(cache_stats);
   return 0;
 }

@@ -174,3 +174,19 @@ def test_remote_scheduler_asks_the_server():
             conn.shutdown()
         cli.close()
         srv.stop()
+
+
+def test_layerwise_scheduler_loads_inside_the_step(sched):
+    """cache.layerwise: hits are loaded synchronously (load_async False)"""
+    conn, w = sched
+    cfg = _cfg()
+    cfg.kv_transfer_config.kv_connector_extra_config["cache.layerwise"] = True
+    lw = CrossCacheConnector(cfg, vllm_base.KVConnectorRole.SCHEDULER)
+    lw.scheduler_adapter.bind_worker(w)
+    req = _request("LW", 1024, 6)
+    keys = bh.chunk_keys(req.block_hashes, 256 // BS)
+    assert w.store(keys[:2], np.arange(32)) == 0
+    assert lw.get_num_new_matched_tokens(req, 0) == (512, False)
+    lw.update_state_after_alloc(req, _Blocks(range(64)), 512)
+    meta = lw.build_connector_meta(_sched_out(new=[("LW", 1024)]))
+    assert [m.direction for m in meta.requests] == ["RETRIEVE", "STORE"]

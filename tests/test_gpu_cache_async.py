@@ -1,0 +1,138 @@
+"""Asynchronous layer-ordered store / load on the GPU: copies enqueued per
+layer on a side stream, a compute stream that waits (on the GPU) for each
+layer before reading it, a store gated on an event recorded after the
+compute stream rewrote the layer.  Bytes against the oracle."""
+import errno
+
+import numpy as np
+import pytest
+import torch
+
+from demo_b200 import cache as cc
+from demo_b200._lib import lib
+from oracle import kvcopy as ok
+from tests.golden import gen
+from tests.gpu_util import DeviceKV
+from tests.test_gpu_cache import keys_for, worker
+
+pytestmark = pytest.mark.gpu
+
+CASE = dict(next(c for c in gen.KV_CASES if c["name"] == "gqa_bs16"), num_layers=6, num_blocks=256, chunks=8)
+BPC = CASE["chunk_size"] // CASE["block_size"]
+UNIT = gen.unit_of(CASE)
+
+
+@pytest.fixture
+def cuda_cache():
+    cc.init(CASE["chunk_size"], (2 * CASE["chunks"] + 2) * gen.record_bytes(CASE), None)
+    yield
+    cc.exit()
+
+
+def _expected(bids, dst_bids):
+    k, v = gen.paged_layers(CASE)
+    recs = ok.gather(k, v, bids, CASE["chunk_size"], CASE["block_size"], UNIT)
+    ek, ev = gen.paged_layers(CASE, zero=True)
+    ok.scatter(recs, ek, ev, dst_bids, CASE["chunk_size"], CASE["block_size"], UNIT)
+    return ek, ev
+
+
+def test_layerwise_load_with_gpu_side_waits(cuda_cache):
+    src, dst = DeviceKV(CASE), DeviceKV(CASE, zero=True)
+    ws, wd = worker(src), worker(dst)
+    ws.register()
+    wd.register()
+    keys = keys_for(CASE["chunks"], seed=41)
+    bids, b2 = gen.block_ids(CASE), gen.block_ids(CASE, seed_offset=1)
+    assert ws.store(keys, bids) == 0
+    ek, ev = _expected(bids, b2)
+    load_stream, compute = torch.cuda.Stream(), torch.cuda.Stream()
+    n0 = lib.crosscache_kernel_launches()
+    h = wd.load_async(keys, b2)
+    assert h.records == CASE["chunks"] and not h.missing
+    for l in range(CASE["num_layers"]):
+        h.layers(l, l + 1, stream=load_stream)
+    # the compute stream reads each layer right after its GPU-side wait
+    sums = []
+    with torch.cuda.stream(compute):
+        for l in range(CASE["num_layers"]):
+            h.stream_wait(l, compute)
+            sums.append((dst.k[l].to(torch.int64).sum(), dst.v[l].to(torch.int64).sum()))
+    compute.synchronize()
+    assert h.finish() == 0
+    assert lib.crosscache_kernel_launches() - n0 == CASE["num_layers"]
+    for l in range(CASE["num_layers"]):
+        assert int(sums[l][0]) == int(ek[l].astype(np.int64).sum()), l
+        assert int(sums[l][1]) == int(ev[l].astype(np.int64).sum()), l
+    kh, vh = dst.host()
+    assert all(np.array_equal(a, b) for a, b in zip(kh, ek))
+    assert all(np.array_equal(a, b) for a, b in zip(vh, ev))
+    wd.unregister()
+    ws.unregister()
+
+
+def test_layerwise_store_gated_on_compute_events(cuda_cache):
+    """the compute stream rewrites each layer, records an event, and the
+    store of that layer waits for it: the records hold the new bytes"""
+    src = DeviceKV(CASE, zero=True)
+    ws = worker(src)
+    ws.register()
+    keys = keys_for(CASE["chunks"], seed=42)
+    bids = gen.block_ids(CASE)
+    k_new, v_new = gen.paged_layers(CASE, seed=777)
+    save_stream, compute = torch.cuda.Stream(), torch.cuda.Stream()
+    h = ws.store_async(keys, bids)
+    assert h.records == CASE["chunks"]
+    host_k = [torch.from_numpy(a).pin_memory() for a in k_new]
+    host_v = [torch.from_numpy(a).pin_memory() for a in v_new]
+    for l in range(CASE["num_layers"]):
+        with torch.cuda.stream(compute):
+            torch.cuda._sleep(2_000_000)          # the "layer" takes a while
+            src.k[l].copy_(host_k[l], non_blocking=True)
+            src.v[l].copy_(host_v[l], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(compute)
+        h.layers(l, l + 1, stream=save_stream, wait_event=ev)
+    assert ws.lookup(keys) == 0
+    assert h.finish() == 0
+    assert ws.lookup(keys) == 32 * CASE["chunks"]
+    # load the records into a zeroed cache and compare with the new bytes
+    dst = DeviceKV(CASE, zero=True)
+    wd = worker(dst)
+    wd.register()
+    b2 = gen.block_ids(CASE, seed_offset=1)
+    assert wd.load(keys, b2) == 0
+    recs = ok.gather(k_new, v_new, bids, CASE["chunk_size"], CASE["block_size"], UNIT)
+    ek, ev_ = gen.paged_layers(CASE, zero=True)
+    ok.scatter(recs, ek, ev_, b2, CASE["chunk_size"], CASE["block_size"], UNIT)
+    kh, vh = dst.host()
+    assert all(np.array_equal(a, b) for a, b in zip(kh, ek))
+    assert all(np.array_equal(a, b) for a, b in zip(vh, ev_))
+    wd.unregister()
+    ws.unregister()
+
+
+def test_async_errors(cuda_cache):
+    src = DeviceKV(CASE)
+    ws = worker(src)
+    ws.register()
+    keys = keys_for(2, seed=43)
+    bids = gen.block_ids(CASE)[:2 * BPC]
+    assert ws.store(keys, bids) == 0
+    s = torch.cuda.Stream()
+    # a block id past the paged cache: the kernel flags it, finish reports it
+    h = ws.load_async(keys[:1], np.full(BPC, 1 << 40, np.uint64))
+    h.layers(0, CASE["num_layers"], stream=s)
+    assert h.finish() == -errno.EINVAL
+    # a store that never enqueued its last layer is dropped
+    fresh = keys_for(1, seed=44)
+    h = ws.store_async(fresh, bids[:BPC])
+    h.layers(0, CASE["num_layers"] - 1, stream=s)
+    assert h.finish() == -errno.EINVAL
+    assert ws.lookup(fresh) == 0
+    # nothing pinned or pending is left behind
+    st = ws.stats()
+    assert st["records_used"] == 2
+    ws.clear()
+    assert ws.stats()["records_used"] == 0
+    ws.unregister()
