@@ -598,6 +598,94 @@ def _disk_tier_probe(args, cc, L_, layers, layout, kp, vp, hashes, bt_save, bt_l
                     "behind), then every file written; memory emptied; loads read the files"}
 
 
+def _layerwise_probe(args, cc, layers, layout, kp, vp, hashes, bt_save, bt_load, s) -> dict:
+    """A prefix hit served inside the step that computes the request: 4
+    requests of 2048 cached tokens (1 GiB of KV) are loaded while a per-layer
+    compute proxy for 512 new tokens per request runs (two bf16 GEMMs per
+    layer, 2048 x 4096 x 14336 and back: the MLP of Llama-3-8B).  Timed
+    (CUDA events, median of the steps): the load alone, the compute alone,
+    load then compute, and the layer pipeline (cache_load_async, one launch
+    per layer on a side stream, the compute stream waiting on the GPU for
+    each layer before its GEMMs)."""
+    import torch
+
+    n_req = 4
+    prb, bpc = s["per_req_blocks"], s["bpc"]
+    keys_per = s["n_tok"] // CHUNK
+    kb = [bytes(h) for h in hashes[bpc - 1::bpc][: n_req * keys_per]]
+    save = bt_save[: n_req * prb]
+    load = bt_load[: n_req * prb]
+    dev = s["dev"]
+    cc.init(CHUNK, (n_req * keys_per + 1) * s["rec_bytes"], None)
+    try:
+        w = cc.Worker("llama-3-8b", layout, kp, vp, node_id=s["local"])
+        w.register()
+        assert w.store(kb, save) == 0
+        g = torch.Generator(device=dev).manual_seed(9)
+        x = torch.randn(n_req * 512, 4096, generator=g, device=dev).to(torch.bfloat16)
+        w1 = (torch.randn(4096, 14336, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        w2 = (torch.randn(14336, 4096, generator=g, device=dev) * 0.01).to(torch.bfloat16)
+        L = layout.num_layers
+        compute, side = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+        def forward(h=None):
+            y = x
+            for l in range(L):
+                if h is not None:
+                    h.stream_wait(l, compute)
+                y = (y @ w1) @ w2
+            return y
+
+        def timed(fn):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            with torch.cuda.stream(compute):
+                a.record(compute)
+                fn()
+                b.record(compute)
+            torch.cuda.synchronize()
+            return a.elapsed_time(b)
+
+        def pipelined():
+            h = w.load_async(kb, load)
+            ready = torch.cuda.Event()
+            ready.record(compute)
+            for l in range(L):
+                h.layers(l, l + 1, stream=side, wait_event=ready if l == 0 else None)
+            forward(h)
+            return h
+
+        res = {"load": [], "compute": [], "sequential": [], "pipelined": []}
+        for it in range(args.warmup + args.steps):
+            t_load = timed(lambda: w.load(kb, load))
+            t_comp = timed(forward)
+            t_seq = timed(lambda: (w.load(kb, load), forward()))
+            hs = []
+            t_pipe = timed(lambda: hs.append(pipelined()))
+            assert hs[0].finish() == 0
+            if it >= args.warmup:
+                for k, v in (("load", t_load), ("compute", t_comp), ("sequential", t_seq), ("pipelined", t_pipe)):
+                    res[k].append(v)
+        ok = all(torch.equal(t[:, torch.from_numpy(save.astype(np.int64)).to(dev)].view(torch.int16),
+                             t[:, torch.from_numpy(load.astype(np.int64)).to(dev)].view(torch.int16))
+                 for t in layers)
+        w.unregister()
+    finally:
+        cc.exit()
+    med = {k: statistics.median(v) for k, v in res.items()}
+    hidden = (med["sequential"] - med["pipelined"]) / med["load"] if med["load"] else 0.0
+    # 1.0: the shorter of load and compute disappears entirely under the longer
+    overlap = (med["load"] + med["compute"] - med["pipelined"]) / min(med["load"], med["compute"])
+    return {"requests": n_req, "kv_bytes": n_req * keys_per * s["rec_bytes"],
+            "load_ms": round(med["load"], 3), "compute_ms": round(med["compute"], 3),
+            "sequential_ms": round(med["sequential"], 3), "pipelined_ms": round(med["pipelined"], 3),
+            "load_hidden_frac": round(hidden, 4), "overlap_efficiency": round(overlap, 4),
+            "verified_bytes": bool(ok),
+            "note": "compute proxy: per layer (2048 x 4096) @ (4096 x 14336) @ (14336 x 4096) bf16; "
+                    "load = cache_load (staged, copy engines); pipelined = cache_load_async, one "
+                    "launch per layer (<= 32 CTAs, mapped host records) on a side stream"}
+
+
 def _serve_for_bench(q, stop, pool_bytes):
     import torch
 
@@ -718,6 +806,8 @@ def main() -> None:
     ap.add_argument("--disk-dir", default=None,
                     help="also time the disk tier in a fresh directory under this path (off by default)")
     ap.add_argument("--disk-requests", type=int, default=8, help="requests of the disk-tier sample")
+    ap.add_argument("--layerwise", action="store_true",
+                    help="also time a layer-pipelined load against a per-layer compute proxy")
     ap.add_argument("--via-server", action="store_true",
                     help="also time save/load through a CrossCache server process (ZeroMQ + CUDA IPC)")
     ap.add_argument("--layers", type=int, default=L, help="smaller cases for ncu captures only")
@@ -938,6 +1028,7 @@ def main() -> None:
     p50 = None
     disk = None
     server = None
+    layerwise = None
     if not args.skip_e2e:
         # host-link peaks measured in this run: pinned 256 MiB cudaMemcpyAsync,
         # 16 per direction (4 GiB), every rank at once after a barrier -- the
@@ -1097,6 +1188,10 @@ def main() -> None:
                                     dict(local=local, world=world, rank=rank, n_req=n_req, n_tok=n_tok,
                                          bpc=bpc, per_req_blocks=per_req_blocks, nrec=nrec,
                                          rec_bytes=rec_bytes, dev=dev))
+        if args.layerwise and world == 1:
+            layerwise = _layerwise_probe(args, cc, layers, layout, kp, vp, hashes, bt_save, bt_load,
+                                         dict(n_tok=n_tok, bpc=bpc, per_req_blocks=per_req_blocks,
+                                              rec_bytes=rec_bytes, dev=dev, local=local))
         if args.via_server and world == 1:
             server = _server_probe(args, layers, hashes, bt_save, bt_load, disjoint,
                                    dict(n_req=n_req, n_tok=n_tok, bpc=bpc, per_req_blocks=per_req_blocks,
@@ -1152,7 +1247,7 @@ def main() -> None:
                          "gather_ms": round(gather_ms, 4), "scatter_ms": round(scatter_ms, 4),
                          "scatter_frac": round(2 * payload / (scatter_ms / 1e3) / GB / hbm_peak, 4)},
             "e2e": e2e, "link": link, "p50_load_latency_ms": round(p50, 3) if p50 is not None else None,
-            "block_hash": hash_info, "disk_tier": disk, "via_server": server,
+            "block_hash": hash_info, "disk_tier": disk, "via_server": server, "layerwise": layerwise,
             "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": clocks.summary(),
             "verified_bytes": bool(ok_value),
         }

@@ -190,6 +190,11 @@ SIGNATURES: dict[str, tuple] = {
                                             C.c_void_p]),
     "kv_block_hash_host_algo": (C.c_int64, [C.c_int, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
                                             C.c_void_p, C.c_void_p, C.c_int]),
+    "kv_block_hash_launch_ext": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_void_p, C.c_int, C.c_void_p]),
+    "kv_block_hash_host_ext": (C.c_int64, [C.c_int, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32,
+                                           C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]),
 }
 
 

@@ -19,6 +19,14 @@
  *   74 | 85 | 86 | 87         TUPLE, or TUPLE1/2/3 for block_size 1..3
  *   94 4e 87 94 2e            MEMOIZE NONE TUPLE3 MEMOIZE STOP
  *
+ * With vLLM's per-block extra keys (LoRA name, multimodal hashes, cache
+ * salt: kv_cache_utils.py generate_block_hash_extra_keys) the tuple's third
+ * item is their tuple instead of None.  Protocol 5 memoizes without indices
+ * (MEMOIZE) and canonical CBOR has no back-references, so the serialised
+ * extra keys are one position-independent byte segment that takes the place
+ * of the 0x4e (pickle) or 0xf6 (CBOR) byte; the caller supplies the segment
+ * per block (include/kvhash.h kv_block_hash_launch_ext).
+ *
  * (CPython _pickle.c save_bytes/save_tuple/save_long; a 0..255 token is
  * BININT1, 256..65535 BININT2, anything else BININT 4-byte two's complement.)
  *
@@ -104,7 +112,8 @@ __device__ __forceinline__ void sha_compress(uint32_t st[8], const uint8_t *blk)
  * one int32 token, and the trailer. */
 struct PickleFmt {
     static __device__ __forceinline__ uint32_t hdr_len(uint32_t bs) { return bs > 3 ? 47u : 46u; }
-    static constexpr uint32_t kTrailer = 6;   /* tuple op, MEMOIZE NONE TUPLE3 MEMOIZE STOP */
+    /* tuple op, MEMOIZE, NONE or the extra segment, TUPLE3 MEMOIZE STOP */
+    static __device__ __forceinline__ uint32_t trailer_len(uint32_t xlen) { return xlen ? 5u + xlen : 6u; }
     static __device__ __forceinline__ uint32_t header_byte(uint32_t p, uint32_t bs, uint64_t frame,
                                                            const uint8_t *par)
     {
@@ -129,10 +138,16 @@ struct PickleFmt {
         const uint32_t op = (v >= 0 && v <= 0xff) ? 0x4bu : ((v >= 0 && v <= 0xffff) ? 0x4du : 0x4au);
         return k == 0 ? op : (u >> (8 * (k - 1))) & 0xffu;
     }
-    static __device__ __forceinline__ uint32_t trailer_byte(uint32_t k, uint32_t bs)
+    static __device__ __forceinline__ uint32_t trailer_byte(uint32_t k, uint32_t bs, const uint8_t *x, uint32_t xlen)
     {
         const uint32_t tuple_op = bs > 3 ? 0x74u : (0x84u + bs);    /* TUPLE or TUPLE1..3 */
-        return k == 0 ? tuple_op : (k == 1 ? 0x94u : (k == 2 ? 0x4eu : (k == 3 ? 0x87u : (k == 4 ? 0x94u : 0x2eu))));
+        if (k < 2)
+            return k == 0 ? tuple_op : 0x94u;
+        const uint32_t xl = xlen ? xlen : 1u;
+        if (k < 2 + xl)
+            return xlen ? x[k - 2] : 0x4eu;
+        k -= 2 + xl;
+        return k == 0 ? 0x87u : (k == 1 ? 0x94u : 0x2eu);
     }
 };
 
@@ -140,7 +155,7 @@ struct CborFmt {
     /* array(3), bytes(32) head, parent, array(bs) head of 1, 2 or 3 bytes */
     static __device__ __forceinline__ uint32_t arr_head(uint32_t bs) { return bs < 24 ? 1u : (bs < 256 ? 2u : 3u); }
     static __device__ __forceinline__ uint32_t hdr_len(uint32_t bs) { return 35u + arr_head(bs); }
-    static constexpr uint32_t kTrailer = 1;   /* null */
+    static __device__ __forceinline__ uint32_t trailer_len(uint32_t xlen) { return xlen ? xlen : 1u; }  /* null */
     static __device__ __forceinline__ uint32_t header_byte(uint32_t p, uint32_t bs, uint64_t, const uint8_t *par)
     {
         if (p < 3)
@@ -169,7 +184,10 @@ struct CborFmt {
             return w == 1 ? (major | n) : (major | (w == 2 ? 24u : (w == 3 ? 25u : 26u)));
         return (n >> (8 * (w - 1 - k))) & 0xffu;
     }
-    static __device__ __forceinline__ uint32_t trailer_byte(uint32_t, uint32_t) { return 0xf6u; }
+    static __device__ __forceinline__ uint32_t trailer_byte(uint32_t k, uint32_t, const uint8_t *x, uint32_t xlen)
+    {
+        return xlen ? x[k] : 0xf6u;
+    }
 };
 
 struct HashArgs {
@@ -178,6 +196,8 @@ struct HashArgs {
     const int32_t *num_blocks;
     const int64_t *out_offsets;
     const uint8_t *parents;
+    const uint8_t *extra;            /* per-block extra-key segments, or null */
+    const int64_t *extra_offsets;    /* [total blocks + 1] into extra */
     uint8_t *out;
     uint32_t num_req;
     uint32_t block_size;
@@ -218,12 +238,21 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
 
     const uint32_t bs = a.block_size;
     const uint32_t hdr_len = F::hdr_len(bs);
-    const uint32_t fixed = hdr_len + F::kTrailer;
     const int32_t *tok = a.tokens + a.tok_offsets[r];
     uint8_t *out = a.out + (uint64_t)a.out_offsets[r] * 32;
     const int nblk = a.num_blocks[r];
 
     for (int i = 0; i < nblk; i++, tok += bs) {
+        const uint8_t *x = nullptr;
+        uint32_t xlen = 0;
+        if (a.extra) {
+            const uint64_t gb = (uint64_t)a.out_offsets[r] + i;
+            const int64_t x0 = a.extra_offsets[gb];
+            x = a.extra + x0;
+            xlen = (uint32_t)(a.extra_offsets[gb + 1] - x0);
+        }
+        const uint32_t tl = F::trailer_len(xlen);
+        const uint32_t fixed = hdr_len + tl;
         /* (1) message length */
         uint32_t wsum = 0;
         for (uint32_t j = lane; j < bs; j += 32)
@@ -259,13 +288,26 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
                     ring[(off + k) % kRing] = (uint8_t)F::token_byte(v, k);
                 pos += __shfl_sync(0xffffffffu, incl, 31);
             } else {
-                /* trailer bytes, then 0x80, zeros, 64-bit big-endian bit length */
+                const uint32_t tbase = len - tl;   /* the trailer starts here (== pos) */
+                /* a long trailer (extra keys) passes the ring in 256-byte pieces */
+                while (len - pos > 256) {
+                    for (uint32_t p = lane; p < 256; p += 32)
+                        ring[(pos + p) % kRing] = (uint8_t)F::trailer_byte(pos + p - tbase, bs, x, xlen);
+                    pos += 256;
+                    __syncwarp();
+                    while (pos - done >= 64) {
+                        sha_compress(st, ring + (done % kRing));
+                        done += 64;
+                    }
+                    __syncwarp();
+                }
+                /* the rest of the trailer, then 0x80, zeros, 64-bit big-endian bit length */
                 const uint32_t tail0 = pos;
                 const uint64_t bits = (uint64_t)len * 8;
                 for (uint32_t p = tail0 + lane; p < total; p += 32) {
                     uint32_t v;
                     if (p < len) {
-                        v = F::trailer_byte(p - (len - F::kTrailer), bs);
+                        v = F::trailer_byte(p - tbase, bs, x, xlen);
                     } else if (p == len) {
                         v = 0x80u;
                     } else if (p < total - 8) {
@@ -314,18 +356,19 @@ HostWorkspace g_ws[64];
 
 }  // namespace
 
-extern "C" int kv_block_hash_launch_algo(const int32_t *tokens, const int64_t *tok_offsets,
-                                         const int32_t *num_blocks, const int64_t *out_offsets,
-                                         const uint8_t *parents, uint32_t num_req,
-                                         uint32_t block_size, const uint8_t *none_hash,
-                                         uint8_t *out, int algo, void *stream)
+extern "C" int kv_block_hash_launch_ext(const int32_t *tokens, const int64_t *tok_offsets,
+                                        const int32_t *num_blocks, const int64_t *out_offsets,
+                                        const uint8_t *parents, uint32_t num_req,
+                                        uint32_t block_size, const uint8_t *none_hash,
+                                        const uint8_t *extra, const int64_t *extra_offsets,
+                                        uint8_t *out, int algo, void *stream)
 {
     if (algo != KVHASH_SHA256_PICKLE && algo != KVHASH_SHA256_CBOR)
         return -EINVAL;
     if (!num_req)
         return 0;
     if (!tokens || !tok_offsets || !num_blocks || !out_offsets || !out || !block_size ||
-        block_size > KVHASH_MAX_BLOCK_SIZE || (!parents && !none_hash))
+        block_size > KVHASH_MAX_BLOCK_SIZE || (!parents && !none_hash) || (extra && !extra_offsets))
         return -EINVAL;
     HashArgs a{};
     a.tokens = tokens;
@@ -333,6 +376,8 @@ extern "C" int kv_block_hash_launch_algo(const int32_t *tokens, const int64_t *t
     a.num_blocks = num_blocks;
     a.out_offsets = out_offsets;
     a.parents = parents;
+    a.extra = extra;
+    a.extra_offsets = extra ? extra_offsets : nullptr;
     a.out = out;
     a.num_req = num_req;
     a.block_size = block_size;
@@ -349,6 +394,16 @@ extern "C" int kv_block_hash_launch_algo(const int32_t *tokens, const int64_t *t
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
 }
 
+extern "C" int kv_block_hash_launch_algo(const int32_t *tokens, const int64_t *tok_offsets,
+                                         const int32_t *num_blocks, const int64_t *out_offsets,
+                                         const uint8_t *parents, uint32_t num_req,
+                                         uint32_t block_size, const uint8_t *none_hash,
+                                         uint8_t *out, int algo, void *stream)
+{
+    return kv_block_hash_launch_ext(tokens, tok_offsets, num_blocks, out_offsets, parents, num_req, block_size,
+                                    none_hash, nullptr, nullptr, out, algo, stream);
+}
+
 extern "C" int kv_block_hash_launch(const int32_t *tokens, const int64_t *tok_offsets,
                                     const int32_t *num_blocks, const int64_t *out_offsets,
                                     const uint8_t *parents, uint32_t num_req,
@@ -359,9 +414,10 @@ extern "C" int kv_block_hash_launch(const int32_t *tokens, const int64_t *tok_of
                                      block_size, none_hash, out, KVHASH_SHA256_PICKLE, stream);
 }
 
-extern "C" int64_t kv_block_hash_host_algo(int devid, const int32_t *tokens, const int64_t *tok_lens,
-                                           uint32_t num_req, uint32_t block_size,
-                                           const uint8_t *none_hash, uint8_t *out_hashes, int algo)
+extern "C" int64_t kv_block_hash_host_ext(int devid, const int32_t *tokens, const int64_t *tok_lens,
+                                          uint32_t num_req, uint32_t block_size, const uint8_t *none_hash,
+                                          const uint8_t *extra, const int64_t *extra_offsets,
+                                          uint8_t *out_hashes, int algo)
 {
     if (algo != KVHASH_SHA256_PICKLE && algo != KVHASH_SHA256_CBOR)
         return -EINVAL;
@@ -386,14 +442,25 @@ extern "C" int64_t kv_block_hash_host_algo(int devid, const int32_t *tokens, con
         return 0;
     if (!tokens)
         return -EINVAL;
-    /* one workspace per device: [tokens | toff | ooff | nblk | out] */
+    int64_t xbytes = 0;
+    if (extra) {
+        if (!extra_offsets || extra_offsets[0] != 0)
+            return -EINVAL;
+        for (int64_t k = 0; k < nout; k++)
+            if (extra_offsets[k + 1] < extra_offsets[k])
+                return -EINVAL;
+        xbytes = extra_offsets[nout];
+    }
+    /* one workspace per device: [tokens | toff | ooff | nblk | out | xoff | extra] */
     auto align = [](size_t x) { return (x + 255) & ~(size_t)255; };
     size_t o_tok = 0;
     size_t o_toff = align(o_tok + ntok * 4);
     size_t o_ooff = align(o_toff + num_req * 8);
     size_t o_nblk = align(o_ooff + num_req * 8);
     size_t o_out = align(o_nblk + num_req * 4);
-    size_t total = align(o_out + (size_t)nout * 32);
+    size_t o_xoff = align(o_out + (size_t)nout * 32);
+    size_t o_x = align(o_xoff + (extra ? (size_t)(nout + 1) * 8 : 0));
+    size_t total = align(o_x + (size_t)xbytes);
 
     HostWorkspace &ws = g_ws[devid];
     std::lock_guard<std::mutex> g(ws.mu);
@@ -418,11 +485,17 @@ extern "C" int64_t kv_block_hash_host_algo(int devid, const int32_t *tokens, con
         cudaMemcpyAsync(b + o_ooff, ooff.data(), num_req * 8, cudaMemcpyHostToDevice, s) != cudaSuccess ||
         cudaMemcpyAsync(b + o_nblk, nblk.data(), num_req * 4, cudaMemcpyHostToDevice, s) != cudaSuccess)
         ret = -EIO;
-    if (ret > 0 && kv_block_hash_launch_algo(reinterpret_cast<int32_t *>(b + o_tok),
-                                             reinterpret_cast<int64_t *>(b + o_toff),
-                                             reinterpret_cast<int32_t *>(b + o_nblk),
-                                             reinterpret_cast<int64_t *>(b + o_ooff), nullptr, num_req,
-                                             block_size, none_hash, b + o_out, algo, s))
+    if (ret > 0 && extra &&
+        (cudaMemcpyAsync(b + o_xoff, extra_offsets, (size_t)(nout + 1) * 8, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+         (xbytes && cudaMemcpyAsync(b + o_x, extra, (size_t)xbytes, cudaMemcpyHostToDevice, s) != cudaSuccess)))
+        ret = -EIO;
+    if (ret > 0 && kv_block_hash_launch_ext(reinterpret_cast<int32_t *>(b + o_tok),
+                                            reinterpret_cast<int64_t *>(b + o_toff),
+                                            reinterpret_cast<int32_t *>(b + o_nblk),
+                                            reinterpret_cast<int64_t *>(b + o_ooff), nullptr, num_req,
+                                            block_size, none_hash, extra ? b + o_x : nullptr,
+                                            extra ? reinterpret_cast<int64_t *>(b + o_xoff) : nullptr,
+                                            b + o_out, algo, s))
         ret = -EIO;
     if (ret > 0 && cudaMemcpyAsync(out_hashes, b + o_out, (size_t)nout * 32, cudaMemcpyDeviceToHost, s) != cudaSuccess)
         ret = -EIO;
@@ -430,6 +503,14 @@ extern "C" int64_t kv_block_hash_host_algo(int devid, const int32_t *tokens, con
         ret = -EIO;
     cudaStreamDestroy(s);
     return ret;
+}
+
+extern "C" int64_t kv_block_hash_host_algo(int devid, const int32_t *tokens, const int64_t *tok_lens,
+                                           uint32_t num_req, uint32_t block_size,
+                                           const uint8_t *none_hash, uint8_t *out_hashes, int algo)
+{
+    return kv_block_hash_host_ext(devid, tokens, tok_lens, num_req, block_size, none_hash, nullptr, nullptr,
+                                  out_hashes, algo);
 }
 
 extern "C" int64_t kv_block_hash_host(int devid, const int32_t *tokens, const int64_t *tok_lens,

@@ -40,6 +40,7 @@ extern "C" {
 #include <chrono>
 #include <condition_variable>
 #include <cstdlib>
+#include <deque>
 #include <cstring>
 #include <map>
 #include <string>
@@ -55,6 +56,7 @@ namespace {
 
 constexpr int kNumSub = 3;                       /* staging ring depth per lane */
 constexpr uint64_t kGroupTarget = 32ull << 20;   /* staging sub-slot target size */
+constexpr uint64_t kAsyncRingMax = 768ull << 20; /* HBM ring of one staged async transfer */
 
 #define CU_OK(expr)                                                              \
     ([&]() -> bool {                                                             \
@@ -254,13 +256,64 @@ struct AsyncOp {
     uint32_t total_layers = 0;
     bool poisoned = false;
 
+    /* staged mode (host records): each layer's slices cross the host link on
+     * a copy engine into an HBM ring slot, and the kernel moves them between
+     * the slot and the paged cache -- the SMs never wait on the link */
+    static constexpr int kRing = 3;
+    bool staged = false;
+    cudaStream_t cs = nullptr;
+    uint8_t *ring = nullptr;
+    uint64_t ring_cap = 0;
+    uint64_t slot_bytes = 0;      /* records * kv * layer_bytes */
+    uint64_t layer_bytes = 0;     /* num_tokens * unit: one layer of one K/V part */
+    uint32_t nkv = 1;
+    uint32_t nrec = 0;
+    uint32_t rec_words = 0;       /* block id words before the slot record tables */
+    uint32_t next_slot = 0;
+    bool slot_used[kRing] = {};
+    cudaEvent_t slot_ready[kRing] = {};
+    cudaEvent_t slot_free[kRing] = {};
+    std::vector<uint8_t *> host_recs;
+
+    /* the caller's thread queues jobs, the device's async worker thread
+     * enqueues them: marks, counters and spare events are shared */
+    std::mutex mu;
+    std::condition_variable cv;
+    uint32_t jobs_submitted = 0;
+    uint32_t jobs_done = 0;
+    int enqueue_err = 0;
+    std::vector<std::pair<uint32_t, uint32_t>> requested;
+    cudaStream_t gate = nullptr;   /* turns a caller's event into one of ours */
+
     bool init(int device)
     {
         dev = device;
-        return CU_OK(cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking)) &&
-               CU_OK(cudaEventCreateWithFlags(&uploaded, cudaEventDisableTiming)) &&
-               CU_OK(cudaMalloc(&d_err, sizeof(int32_t))) &&
-               CU_OK(cudaHostAlloc(&h_err, sizeof(int32_t), cudaHostAllocDefault));
+        if (!CU_OK(cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking)) ||
+            !CU_OK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking)) ||
+            !CU_OK(cudaStreamCreateWithFlags(&gate, cudaStreamNonBlocking)) ||
+            !CU_OK(cudaEventCreateWithFlags(&uploaded, cudaEventDisableTiming)) ||
+            !CU_OK(cudaMalloc(&d_err, sizeof(int32_t))) ||
+            !CU_OK(cudaHostAlloc(&h_err, sizeof(int32_t), cudaHostAllocDefault)))
+            return false;
+        for (int i = 0; i < kRing; i++)
+            if (!CU_OK(cudaEventCreateWithFlags(&slot_ready[i], cudaEventDisableTiming)) ||
+                !CU_OK(cudaEventCreateWithFlags(&slot_free[i], cudaEventDisableTiming)))
+                return false;
+        return true;
+    }
+
+    bool ensure_ring(uint64_t bytes)
+    {
+        if (bytes <= ring_cap)
+            return true;
+        if (ring)
+            cudaFree(ring);
+        ring = nullptr;
+        ring_cap = 0;
+        if (!CU_OK(cudaMalloc(&ring, bytes)))
+            return false;
+        ring_cap = bytes;
+        return true;
     }
 
     bool ensure_meta(uint64_t words)
@@ -283,6 +336,7 @@ struct AsyncOp {
 
     cudaEvent_t take_event()
     {
+        std::lock_guard<std::mutex> lk(mu);
         if (!spare.empty()) {
             cudaEvent_t e = spare.back();
             spare.pop_back();
@@ -302,6 +356,14 @@ struct AsyncOp {
         meta_words = 0;
         base = kv_copy_desc{};
         total_layers = 0;
+        staged = false;
+        next_slot = 0;
+        for (int i = 0; i < kRing; i++)
+            slot_used[i] = false;
+        host_recs.clear();
+        jobs_submitted = jobs_done = 0;
+        enqueue_err = 0;
+        requested.clear();
     }
 
     void release()
@@ -317,6 +379,22 @@ struct AsyncOp {
         spare.clear();
         if (uploaded)
             cudaEventDestroy(uploaded);
+        if (cs)
+            cudaStreamSynchronize(cs);
+        for (int i = 0; i < kRing; i++) {
+            if (slot_ready[i])
+                cudaEventDestroy(slot_ready[i]);
+            if (slot_free[i])
+                cudaEventDestroy(slot_free[i]);
+        }
+        if (ring)
+            cudaFree(ring);
+        if (cs)
+            cudaStreamDestroy(cs);
+        if (gate) {
+            cudaStreamSynchronize(gate);
+            cudaStreamDestroy(gate);
+        }
         if (d_meta)
             cudaFree(d_meta);
         if (h_meta)
@@ -327,9 +405,105 @@ struct AsyncOp {
             cudaFreeHost(h_err);
         if (own)
             cudaStreamDestroy(own);
-        *this = AsyncOp();
+        dev = -1;
     }
 };
+
+struct AsyncJob {
+    AsyncOp *op;
+    uint32_t l0, l1;
+    cudaStream_t s;
+    cudaEvent_t gate;     /* completes after the caller's wait event, or null */
+};
+
+/* Enqueue one job's copies on the GPU (the device's async worker thread).
+ * Appends one mark per layer range it covered to `out`. */
+int async_enqueue(AsyncOp *op, const AsyncJob &j, std::vector<AsyncOp::Mark> &out)
+{
+    cudaStream_t s = j.s;
+    if (j.gate && !CU_OK(cudaStreamWaitEvent(s, j.gate, 0)))
+        return -EIO;
+    if (!op->is_uploaded) {
+        if (!CU_OK(cudaMemsetAsync(op->d_err, 0, sizeof(int32_t), s)) ||
+            !CU_OK(cudaMemcpyAsync(op->d_meta, op->h_meta, op->meta_words * 8, cudaMemcpyHostToDevice, s)) ||
+            !CU_OK(cudaEventRecord(op->uploaded, s)))
+            return -EIO;
+        op->is_uploaded = true;
+        op->upload_stream = s;
+    } else if (s != op->upload_stream && !CU_OK(cudaStreamWaitEvent(s, op->uploaded, 0))) {
+        return -EIO;
+    }
+    auto mark = [&](uint32_t l0, uint32_t l1, cudaStream_t on) -> int {
+        cudaEvent_t ev = op->take_event();
+        if (!ev || !CU_OK(cudaEventRecord(ev, on)))
+            return -EIO;
+        out.push_back(AsyncOp::Mark{l0, l1, ev});
+        return 0;
+    };
+    if (!op->staged) {
+        if (op->base.num_records) {
+            kv_copy_desc d = op->base;
+            d.layer_begin = j.l0;
+            d.num_layers = j.l1 - j.l0;
+            int ret = kv_copy_launch(&d, s);
+            if (ret)
+                return ret;
+        }
+        return mark(j.l0, j.l1, s);
+    }
+    const bool load = op->base.direction == 0;
+    const uint64_t lb = op->layer_bytes;
+    const uint64_t hp = (uint64_t)op->total_layers * lb;   /* K part -> V part in a host record */
+    for (uint32_t l = j.l0; l < j.l1; l++) {
+        const int sl = (int)(op->next_slot++ % AsyncOp::kRing);
+        uint8_t *slot = op->ring + (uint64_t)sl * op->slot_bytes;
+        kv_copy_desc d = op->base;
+        d.records = op->d_meta + op->rec_words + (uint64_t)sl * op->nrec;
+        d.layer_k = op->base.layer_k + l;
+        d.layer_v = op->base.layer_v ? op->base.layer_v + l : nullptr;
+        d.num_layers = 1;
+        d.layer_begin = 0;
+        d.record_layers = 1;
+        if (load) {
+            if (op->slot_used[sl] && !CU_OK(cudaStreamWaitEvent(op->cs, op->slot_free[sl], 0)))
+                return -EIO;
+            for (uint32_t r = 0; r < op->nrec; r++)
+                if (!CU_OK(cudaMemcpy2DAsync(slot + (uint64_t)r * op->nkv * lb, lb, op->host_recs[r] + l * lb, hp,
+                                             lb, op->nkv, cudaMemcpyHostToDevice, op->cs)))
+                    return -EIO;
+            if (!CU_OK(cudaEventRecord(op->slot_ready[sl], op->cs)) ||
+                !CU_OK(cudaStreamWaitEvent(s, op->slot_ready[sl], 0)))
+                return -EIO;
+            int ret = kv_copy_launch(&d, s);
+            if (ret)
+                return ret;
+            if (!CU_OK(cudaEventRecord(op->slot_free[sl], s)))
+                return -EIO;
+            op->slot_used[sl] = true;
+            if ((ret = mark(l, l + 1, s)))
+                return ret;
+        } else {
+            if (op->slot_used[sl] && !CU_OK(cudaStreamWaitEvent(s, op->slot_free[sl], 0)))
+                return -EIO;
+            int ret = kv_copy_launch(&d, s);
+            if (ret)
+                return ret;
+            if (!CU_OK(cudaEventRecord(op->slot_ready[sl], s)) ||
+                !CU_OK(cudaStreamWaitEvent(op->cs, op->slot_ready[sl], 0)))
+                return -EIO;
+            for (uint32_t r = 0; r < op->nrec; r++)
+                if (!CU_OK(cudaMemcpy2DAsync(op->host_recs[r] + l * lb, hp, slot + (uint64_t)r * op->nkv * lb, lb,
+                                             lb, op->nkv, cudaMemcpyDeviceToHost, op->cs)))
+                    return -EIO;
+            if (!CU_OK(cudaEventRecord(op->slot_free[sl], op->cs)))
+                return -EIO;
+            op->slot_used[sl] = true;
+            if ((ret = mark(l, l + 1, op->cs)))
+                return ret;
+        }
+    }
+    return 0;
+}
 
 struct DeviceCtx {
     int dev;
@@ -340,6 +514,61 @@ struct DeviceCtx {
     std::vector<AsyncOp *> async_idle;   /* finished async ops, reusable */
     int max_lanes;
     int host_ptr_ok = 0;   /* registered host memory usable at its host address */
+
+    /* async worker: enqueues the jobs of every async op of this device in
+     * submission order, off the callers' threads */
+    std::mutex jmu;
+    std::condition_variable jcv;
+    std::deque<AsyncJob> jobs;
+    bool jstop = false;
+    std::thread worker;
+
+    void submit(const AsyncJob &j)
+    {
+        std::lock_guard<std::mutex> lk(jmu);
+        if (!worker.joinable())
+            worker = std::thread([this] { run_jobs(); });
+        jobs.push_back(j);
+        jcv.notify_one();
+    }
+
+    void run_jobs()
+    {
+        cudaSetDevice(dev);
+        for (;;) {
+            AsyncJob j;
+            {
+                std::unique_lock<std::mutex> lk(jmu);
+                jcv.wait(lk, [&] { return jstop || !jobs.empty(); });
+                if (jobs.empty())
+                    return;
+                j = jobs.front();
+                jobs.pop_front();
+            }
+            std::vector<AsyncOp::Mark> marks;
+            int ret = j.op->poisoned ? -EIO : async_enqueue(j.op, j, marks);
+            std::lock_guard<std::mutex> lk(j.op->mu);
+            for (auto &m : marks)
+                j.op->marks.push_back(m);
+            if (j.gate)
+                j.op->spare.push_back(j.gate);   /* its wait is already enqueued */
+            if (ret && !j.op->enqueue_err)
+                j.op->enqueue_err = ret;
+            j.op->jobs_done++;
+            j.op->cv.notify_all();
+        }
+    }
+
+    ~DeviceCtx()
+    {
+        {
+            std::lock_guard<std::mutex> lk(jmu);
+            jstop = true;
+            jcv.notify_all();
+        }
+        if (worker.joinable())
+            worker.join();
+    }
 };
 
 struct IpcSet {
@@ -864,30 +1093,57 @@ struct transfer_async *CudaAdaptor::AsyncBegin(const struct transfer_batch *b, i
             return fail(-EIO);
         }
     }
+    auto give_back = [&]() {
+        op->reset_for_reuse();
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        ctx->async_idle.push_back(op);
+    };
     const uint32_t R = b->num_records;
     const uint32_t bpr = b->num_tokens / b->block_size;
     const bool device_recs = b->record_on_device != 0;
-    const uint64_t words = (uint64_t)R * bpr + R;
+    const uint32_t nkv = b->value_ptrs ? 2 : 1;
+    const uint64_t unit = (uint64_t)b->hidden_dim_size * b->caches_element_size;
+    const uint64_t lb = (uint64_t)b->num_tokens * unit;
+    const uint64_t slot_bytes = (uint64_t)R * nkv * lb;
+    /* host records go through the copy engines unless the mode is direct or
+     * the ring would be too large; HBM records are read in place */
+    bool staged = !device_recs && !direct_ && R && slot_bytes * AsyncOp::kRing <= kAsyncRingMax;
+    if (staged && !op->ensure_ring(slot_bytes * AsyncOp::kRing))
+        staged = false;
+    const uint64_t words = (uint64_t)R * bpr + (staged ? (uint64_t)AsyncOp::kRing * R : R);
     if (!op->ensure_meta(std::max<uint64_t>(words, 1))) {
-        op->release();
-        delete op;
+        give_back();
         return fail(-ENOMEM);
     }
     if (R)
         memcpy(op->h_meta, b->block_ids, (uint64_t)R * bpr * 8);
-    for (uint32_t r = 0; r < R; r++) {
-        void *p = b->records[r];
-        if (!device_recs && !ctx->host_ptr_ok) {
-            void *dp = nullptr;
-            if (!CU_OK(cudaHostGetDevicePointer(&dp, p, 0))) {
-                op->reset_for_reuse();
-                std::lock_guard<std::mutex> lk(ctx->mu);
-                ctx->async_idle.push_back(op);
-                return fail(-EINVAL);
+    op->staged = staged;
+    op->nrec = R;
+    op->nkv = nkv;
+    op->layer_bytes = lb;
+    op->slot_bytes = slot_bytes;
+    op->rec_words = (uint32_t)((uint64_t)R * bpr);
+    if (staged) {
+        op->host_recs.resize(R);
+        for (uint32_t r = 0; r < R; r++)
+            op->host_recs[r] = static_cast<uint8_t *>(b->records[r]);
+        for (int s = 0; s < AsyncOp::kRing; s++)
+            for (uint32_t r = 0; r < R; r++)
+                op->h_meta[(uint64_t)R * bpr + (uint64_t)s * R + r] =
+                    (uint64_t)(uintptr_t)(op->ring + (uint64_t)s * slot_bytes + (uint64_t)r * nkv * lb);
+    } else {
+        for (uint32_t r = 0; r < R; r++) {
+            void *p = b->records[r];
+            if (!device_recs && !ctx->host_ptr_ok) {
+                void *dp = nullptr;
+                if (!CU_OK(cudaHostGetDevicePointer(&dp, p, 0))) {
+                    give_back();
+                    return fail(-EINVAL);
+                }
+                p = dp;
             }
-            p = dp;
+            op->h_meta[(uint64_t)R * bpr + r] = (uint64_t)(uintptr_t)p;
         }
-        op->h_meta[(uint64_t)R * bpr + r] = (uint64_t)(uintptr_t)p;
     }
     op->meta_words = words;
     kv_copy_desc &d = op->base;
@@ -896,7 +1152,7 @@ struct transfer_async *CudaAdaptor::AsyncBegin(const struct transfer_batch *b, i
     d.layer_v = static_cast<const uint64_t *>(b->value_ptrs);
     d.error = op->d_err;
     d.page_buffer_size = b->page_buffer_size;
-    d.unit_bytes = (uint32_t)((uint64_t)b->hidden_dim_size * b->caches_element_size);
+    d.unit_bytes = (uint32_t)unit;
     d.num_tokens = b->num_tokens;
     d.block_size = b->block_size;
     d.num_records = R;
@@ -904,12 +1160,11 @@ struct transfer_async *CudaAdaptor::AsyncBegin(const struct transfer_batch *b, i
     d.block_ids = op->d_meta;
     d.records = op->d_meta + (uint64_t)R * bpr;
     d.record_layers = b->num_layers;
+    /* these kernels run next to the caller's own: a few register-path CTAs
+     * (no shared memory) fit beside its kernels, where a TMA-bulk CTA with
+     * 128 KiB of shared memory would wait for an SM to drain */
     d.max_ctas = async_ctas_;
-    bool recs_aligned = device_recs;
-    for (uint32_t r = 0; recs_aligned && r < R; r++)
-        recs_aligned = (uintptr_t)b->records[r] % 16 == 0;
-    if (recs_aligned && layers_aligned(b->keys_ptrs) && layers_aligned(b->value_ptrs))
-        d.flags = KVCOPY_FLAG_BULK;     /* HBM records only: mapped host memory keeps the register path */
+    d.flags = 0;
     op->total_layers = b->num_layers;
     return reinterpret_cast<struct transfer_async *>(op);
 }
@@ -923,49 +1178,47 @@ int CudaAdaptor::AsyncLayers(struct transfer_async *h, uint32_t l0, uint32_t l1,
         return -EINVAL;
     if (!CU_OK(cudaSetDevice(op->dev)))
         return -EIO;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (wait_event && !CU_OK(cudaStreamWaitEvent(s, static_cast<cudaEvent_t>(wait_event), 0)))
-        return -EIO;
-    if (!op->is_uploaded) {
-        if (!CU_OK(cudaMemsetAsync(op->d_err, 0, sizeof(int32_t), s)) ||
-            !CU_OK(cudaMemcpyAsync(op->d_meta, op->h_meta, op->meta_words * 8, cudaMemcpyHostToDevice, s)) ||
-            !CU_OK(cudaEventRecord(op->uploaded, s)))
+    /* the caller may drop or re-record its event at once: gate it here */
+    cudaEvent_t gate = nullptr;
+    if (wait_event) {
+        gate = op->take_event();
+        if (!gate || !CU_OK(cudaStreamWaitEvent(op->gate, static_cast<cudaEvent_t>(wait_event), 0)) ||
+            !CU_OK(cudaEventRecord(gate, op->gate)))
             return -EIO;
-        op->is_uploaded = true;
-        op->upload_stream = s;
-    } else if (s != op->upload_stream && !CU_OK(cudaStreamWaitEvent(s, op->uploaded, 0))) {
-        return -EIO;
     }
-    if (op->base.num_records) {
-        kv_copy_desc d = op->base;
-        d.layer_begin = l0;
-        d.num_layers = l1 - l0;
-        int ret = kv_copy_launch(&d, s);
-        if (ret)
-            return ret;
+    {
+        std::lock_guard<std::mutex> lk(op->mu);
+        op->requested.push_back({l0, l1});
+        op->jobs_submitted++;
     }
-    cudaEvent_t ev = op->take_event();
-    if (!ev || !CU_OK(cudaEventRecord(ev, s))) {
-        if (ev)
-            op->spare.push_back(ev);
-        return -EIO;
-    }
-    op->marks.push_back(AsyncOp::Mark{l0, l1, ev});
+    device(op->dev)->submit(AsyncJob{op, l0, l1, static_cast<cudaStream_t>(stream), gate});
     return 0;
 }
 
 int CudaAdaptor::AsyncStreamWait(struct transfer_async *h, uint32_t layer, void *stream)
 {
     AsyncOp *op = reinterpret_cast<AsyncOp *>(h);
-    for (auto it = op->marks.rbegin(); it != op->marks.rend(); ++it) {
-        if (layer >= it->l0 && layer < it->l1) {
-            if (!CU_OK(cudaSetDevice(op->dev)) ||
-                !CU_OK(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), it->ev, 0)))
-                return -EIO;
-            return 0;
+    std::unique_lock<std::mutex> lk(op->mu);
+    bool asked = false;
+    for (auto &rg : op->requested)
+        asked = asked || (layer >= rg.first && layer < rg.second);
+    if (!asked)
+        return -ENOENT;
+    auto dl = deadline();
+    for (;;) {
+        for (auto it = op->marks.rbegin(); it != op->marks.rend(); ++it) {
+            if (layer >= it->l0 && layer < it->l1) {
+                if (!CU_OK(cudaSetDevice(op->dev)) ||
+                    !CU_OK(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), it->ev, 0)))
+                    return -EIO;
+                return 0;
+            }
         }
+        if (op->jobs_done == op->jobs_submitted)
+            return op->enqueue_err ? op->enqueue_err : -EIO;   /* its job failed */
+        if (op->cv.wait_until(lk, dl) == std::cv_status::timeout)
+            return -ETIMEDOUT;
     }
-    return -ENOENT;
 }
 
 int CudaAdaptor::AsyncQuery(struct transfer_async *h)
@@ -973,12 +1226,20 @@ int CudaAdaptor::AsyncQuery(struct transfer_async *h)
     AsyncOp *op = reinterpret_cast<AsyncOp *>(h);
     if (op->poisoned)
         return -EIO;
-    cudaSetDevice(op->dev);
-    for (auto &m : op->marks) {
-        cudaError_t e = cudaEventQuery(m.ev);
-        if (e == cudaErrorNotReady)
+    std::vector<cudaEvent_t> evs;
+    {
+        std::lock_guard<std::mutex> lk(op->mu);
+        if (op->jobs_done < op->jobs_submitted)
             return 0;
-        if (e != cudaSuccess)
+        for (auto &m : op->marks)
+            evs.push_back(m.ev);
+    }
+    cudaSetDevice(op->dev);
+    for (cudaEvent_t e : evs) {
+        cudaError_t r = cudaEventQuery(e);
+        if (r == cudaErrorNotReady)
+            return 0;
+        if (r != cudaSuccess)
             return -EIO;
     }
     return 1;
@@ -991,10 +1252,24 @@ int CudaAdaptor::AsyncEnd(struct transfer_async *h)
         return -EIO;
     if (!CU_OK(cudaSetDevice(op->dev)))
         return -EIO;
-    int ret = 0;
     auto dl = deadline();
-    for (auto &m : op->marks) {
-        int w = wait_event(m.ev, dl);
+    std::vector<cudaEvent_t> evs;
+    int ret;
+    {
+        std::unique_lock<std::mutex> lk(op->mu);
+        while (op->jobs_done < op->jobs_submitted) {
+            if (op->cv.wait_until(lk, dl) == std::cv_status::timeout) {
+                log_error("device(%d) async jobs not enqueued after %d ms", op->dev, timeout_ms_);
+                op->poisoned = true;   /* the worker still holds it: never reused */
+                return -ETIMEDOUT;
+            }
+        }
+        for (auto &m : op->marks)
+            evs.push_back(m.ev);
+        ret = op->enqueue_err;
+    }
+    for (cudaEvent_t e : evs) {
+        int w = wait_event(e, dl);
         if (w == -ETIMEDOUT) {
             log_error("device(%d) async transfer timed out after %d ms", op->dev, timeout_ms_);
             op->poisoned = true;     /* its memory may still be in use: never reused or freed */
@@ -1003,7 +1278,14 @@ int CudaAdaptor::AsyncEnd(struct transfer_async *h)
         if (w && !ret)
             ret = w;
     }
-    if (op->is_uploaded && ret == 0) {
+    if (ret) {
+        /* a failed job may have left work queued behind its last mark:
+         * this op is never reused */
+        log_error("device(%d) async transfer failed to enqueue: %d", op->dev, ret);
+        op->poisoned = true;
+        return ret;
+    }
+    if (op->is_uploaded) {
         /* every mark (and the upload with the error-word reset) has completed on
          * the host's clock, so this readback comes after every kernel */
         int w = wait_event(op->uploaded, dl);

@@ -55,10 +55,43 @@ def block_hashes_device(tokens: torch.Tensor, tok_offsets: torch.Tensor, num_blo
         raise RuntimeError(f"kv_block_hash_launch failed: {ret}")
 
 
+_FRAME_LIMIT = 1 << 16      # pickle protocol 5 commits a new frame past 64 KiB
+
+
+def extra_segment(extra_keys, algo: str = "sha256") -> bytes:
+    """The bytes extra_keys occupy inside the serialised (parent, tokens,
+    extra_keys) tuple -- what include/kvhash.h's _ext entry points splice in
+    place of the None byte.  Taken from the hash function's own serialiser
+    (pickle protocol 5 / canonical CBOR) on a template tuple; protocol 5
+    memoizes without indices and CBOR has no back-references, so the segment
+    does not depend on where it sits.  b"" for None."""
+    if extra_keys is None:
+        return b""
+    parent = bytes(32)
+    if algo == "sha256_cbor":
+        import cbor2
+        base = cbor2.dumps((parent, (0,), None), canonical=True)
+        full = cbor2.dumps((parent, (0,), extra_keys), canonical=True)
+        if full[:len(base) - 1] != base[:-1]:
+            raise ValueError("unexpected CBOR layout")
+        return full[len(base) - 1:]
+    import pickle
+    base = pickle.dumps((parent, (0,), None), protocol=5)
+    full = pickle.dumps((parent, (0,), extra_keys), protocol=5)
+    cut = len(base) - 4                     # NONE, then TUPLE3 MEMOIZE STOP
+    if (full[:3] != base[:3] or full[11:cut] != base[11:cut] or full[-3:] != base[-3:]
+            or len(full) >= _FRAME_LIMIT):
+        raise ValueError("extra keys do not serialise as one pickle frame segment")
+    return full[cut:len(full) - 3]
+
+
 def block_hashes(token_lists: Sequence[Sequence[int]], block_size: int, none_hash: bytes,
-                 device: int = 0, algo: str = "sha256") -> list[list[bytes]]:
+                 device: int = 0, algo: str = "sha256",
+                 extra_keys: Sequence[Sequence] | None = None) -> list[list[bytes]]:
     """Chained block hashes of each request (host lists in, host bytes out),
-    computed on `device` through kv_block_hash_host."""
+    computed on `device` through kv_block_hash_host_ext.  extra_keys[r][i]
+    (optional) is request r's block i extra_keys tuple, or None, as vLLM's
+    generate_block_hash_extra_keys returns it."""
     import numpy as np
 
     lens = np.array([len(t) for t in token_lists], dtype=np.int64)
@@ -69,8 +102,25 @@ def block_hashes(token_lists: Sequence[Sequence[int]], block_size: int, none_has
     flat = flat.astype(np.int32)
     nblk = lens // block_size
     out = np.zeros((int(nblk.sum()), 32), dtype=np.uint8)
-    ret = lib.kv_block_hash_host_algo(device, flat.ctypes.data, lens.ctypes.data, len(lens), block_size,
-                                      none_hash, out.ctypes.data, KVHASH_ALGOS[algo])
+    xbuf = xoff = None
+    if extra_keys is not None:
+        segs = []
+        for r, n in enumerate(nblk):
+            ek = extra_keys[r] if extra_keys[r] is not None else [None] * int(n)
+            if len(ek) < n:
+                raise ValueError("one extra_keys entry per full block")
+            for i in range(int(n)):
+                s = extra_segment(ek[i], algo)
+                if algo == "sha256" and 47 + 5 * block_size + 6 + len(s) >= _FRAME_LIMIT:
+                    raise ValueError("block with extra keys does not fit one pickle frame")
+                segs.append(s)
+        xoff = np.zeros(len(segs) + 1, dtype=np.int64)
+        xoff[1:] = np.cumsum([len(s) for s in segs])
+        xbuf = np.frombuffer(b"".join(segs) or b"\0", dtype=np.uint8).copy()
+    ret = lib.kv_block_hash_host_ext(device, flat.ctypes.data, lens.ctypes.data, len(lens), block_size,
+                                     none_hash, xbuf.ctypes.data if xbuf is not None else None,
+                                     xoff.ctypes.data if xoff is not None else None, out.ctypes.data,
+                                     KVHASH_ALGOS[algo])
     if ret < 0:
         raise RuntimeError(f"kv_block_hash_host failed: {ret}")
     res, off = [], 0

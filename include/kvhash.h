@@ -78,6 +78,28 @@ int64_t kv_block_hash_host_algo(int devid, const int32_t *tokens,
                                 uint32_t block_size, const uint8_t *none_hash,
                                 uint8_t *out_hashes, int algo);
 
+/* With vLLM's per-block extra keys (hash_block_tokens' extra_keys: LoRA
+ * name, multimodal hashes, cache salt).  Block g of the output order (request
+ * by request, block by block) hashes (parent, tokens, extra_keys_g) where the
+ * bytes extra[extra_offsets[g] .. extra_offsets[g + 1]) are the serialised
+ * extra_keys_g exactly as they appear inside the pickle protocol-5 (or
+ * canonical CBOR) stream of that tuple -- they replace the None byte; an
+ * empty range means None.  demo_b200.hashing.extra_segment builds them.
+ * extra_offsets has total blocks + 1 entries (device memory for _launch_ext,
+ * host memory for _host_ext); extra NULL = no extra keys anywhere. */
+int kv_block_hash_launch_ext(const int32_t *tokens, const int64_t *tok_offsets,
+                             const int32_t *num_blocks, const int64_t *out_offsets,
+                             const uint8_t *parents, uint32_t num_req,
+                             uint32_t block_size, const uint8_t *none_hash,
+                             const uint8_t *extra, const int64_t *extra_offsets,
+                             uint8_t *out, int algo, void *stream);
+
+int64_t kv_block_hash_host_ext(int devid, const int32_t *tokens,
+                               const int64_t *tok_lens, uint32_t num_req,
+                               uint32_t block_size, const uint8_t *none_hash,
+                               const uint8_t *extra, const int64_t *extra_offsets,
+                               uint8_t *out_hashes, int algo);
+
 #ifdef __cplusplus
 }
 #endif

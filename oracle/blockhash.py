@@ -96,13 +96,32 @@ def none_hash(seed: str, algo: str = "sha256") -> bytes:
     return hashlib.sha256(msg).digest()
 
 
-def block_hashes(tokens: Sequence[int], block_size: int, parent: bytes, algo: str = "sha256") -> list[bytes]:
-    """Chained hashes of the full blocks of `tokens` starting from `parent`."""
+def serialise_with_extra(parent: bytes, tokens: Sequence[int], extra, algo: str = "sha256") -> bytes:
+    """vLLM's hash input with extra keys, by definition: hash_fn's own
+    serialiser applied to (parent, tuple(tokens), extra_keys)
+    (vllm/utils/hashing.py sha256 / sha256_cbor)."""
+    obj = (parent, tuple(int(t) for t in tokens), extra)
+    if algo == "sha256_cbor":
+        import cbor2
+        return cbor2.dumps(obj, canonical=True)
+    import pickle
+    return pickle.dumps(obj, protocol=5)
+
+
+def block_hashes(tokens: Sequence[int], block_size: int, parent: bytes, algo: str = "sha256",
+                 extra: Sequence | None = None) -> list[bytes]:
+    """Chained hashes of the full blocks of `tokens` starting from `parent`;
+    extra[i] (optional) is block i's extra_keys tuple or None."""
     ser = cbor_block if algo == "sha256_cbor" else pickle_block
     out = []
     h = parent
     for i in range(len(tokens) // block_size):
-        h = hashlib.sha256(ser(h, tokens[i * block_size:(i + 1) * block_size])).digest()
+        blk = tokens[i * block_size:(i + 1) * block_size]
+        if extra is not None and extra[i] is not None:
+            msg = serialise_with_extra(h, blk, extra[i], algo)
+        else:
+            msg = ser(h, blk)
+        h = hashlib.sha256(msg).digest()
         out.append(h)
     return out
 
@@ -113,5 +132,7 @@ def chunk_keys(hashes: Sequence[bytes], blocks_in_chunk: int) -> list[bytes]:
 
 
 def batch_block_hashes(requests: Iterable[Sequence[int]], block_size: int, parent: bytes,
-                       algo: str = "sha256") -> list[list[bytes]]:
-    return [block_hashes(t, block_size, parent, algo) for t in requests]
+                       algo: str = "sha256", extra: Sequence | None = None) -> list[list[bytes]]:
+    reqs = list(requests)
+    return [block_hashes(t, block_size, parent, algo, extra[r] if extra is not None else None)
+            for r, t in enumerate(reqs)]

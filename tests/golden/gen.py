@@ -108,3 +108,45 @@ def hash_tokens(spec, case_index: int) -> list[int]:
                 -2, 2, 2**31 - 2, -(2**31) + 1, 255, -255, 65535, -65535] * 2
     lo, hi, n = spec
     return rng.integers(lo, hi, n).astype(np.int64).tolist()
+
+
+# block-hash cases with vLLM's per-block extra keys (hash_block_tokens'
+# extra_keys: LoRA name, multimodal (identifier, offset), cache salt, prompt-
+# embeds digest): (name, algo, block_size, seed, token spec, extra spec).
+# Token generator seeds are 200 + index.
+HASH_CASES_EXTRA = [
+    ("x_lora_bs16", "sha256", 16, "0", (0, 128256, 4 * 16), "lora"),
+    ("x_salt_mm_bs16", "sha256", 16, "0", (0, 128256, 6 * 16 + 5), "salt_mm"),
+    ("x_embeds_bs4", "sha256", 4, "3", (0, 70000, 5 * 4), "embeds"),
+    ("x_long_bs16", "sha256", 16, "0", (0, 128256, 3 * 16), "long"),
+    ("x_mixed_bs1", "sha256", 1, "7", (0, 300, 7), "mixed"),
+    ("x_cbor_lora_bs16", "sha256_cbor", 16, "0", (0, 128256, 4 * 16), "lora"),
+    ("x_cbor_salt_mm_bs16", "sha256_cbor", 16, "0", (0, 128256, 6 * 16 + 5), "salt_mm"),
+    ("x_cbor_long_bs64", "sha256_cbor", 64, "5", (0, 128256, 3 * 64), "long"),
+    ("x_cbor_embeds_bs3", "sha256_cbor", 3, "7", (-1000, 70000, 4 * 3), "embeds"),
+]
+
+
+def hash_extra(spec: str, nblocks: int) -> list:
+    """per-block extra_keys (a tuple, or None) of an extra spec"""
+    if spec == "lora":
+        return [("sql-lora-7",)] * nblocks
+    if spec == "salt_mm":
+        # cache salt on the first block; an image spanning blocks 2-4
+        out = []
+        for b in range(nblocks):
+            keys = []
+            if b == 0:
+                keys.append("tenant-salt-0001")
+            if 2 <= b <= 4:
+                keys.append(("6f1c0a93d2e84b57a3c9e0f1b2d4c6a8e0f2b4d6c8a0e2f4b6d8c0a2e4f6b8d0", 16 * (2 - b) + 5))
+            out.append(tuple(keys) if keys else None)
+        return out
+    if spec == "embeds":
+        return [(hashlib.sha256(b"prompt-embeds block %d" % b).digest(),) for b in range(nblocks)]
+    if spec == "long":
+        # segments longer than 256 bytes pass the kernel's ring in pieces
+        return [("adapter-" + "x" * (300 + 97 * b), ("mm-" + "ab" * (150 + b), b)) for b in range(nblocks)]
+    if spec == "mixed":
+        return [None if b % 3 == 0 else ("lora-b", b * 1000 - 7, ("id", -b)) for b in range(nblocks)]
+    raise ValueError(spec)

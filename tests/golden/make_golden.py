@@ -5,7 +5,8 @@
 block_hashes.json  chained block hashes computed by the INSTALLED vLLM
                    (vllm.v1.core.kv_cache_utils.hash_block_tokens with
                    vllm.utils.hashing.sha256 and sha256_cbor, NONE_HASH from
-                   init_none_hash under PYTHONHASHSEED=<seed>) -- the function
+                   init_none_hash under PYTHONHASHSEED=<seed>; some cases with
+                   per-block extra_keys from gen.hash_extra) -- the function
                    CrossCache's keys come from
                    (python/crosscache_connector.py:133).
 kv_records.json    SHA-256 digests of records gathered, and of paged layers
@@ -48,6 +49,21 @@ def make_hashes() -> list[dict]:
             hashes.append(bytes(parent).hex())
         out.append(dict(name=name, algo=algo, block_size=bs, pythonhashseed=seed,
                         none_hash=bytes(kcu.NONE_HASH).hex(), tokens=tokens, hashes=hashes))
+    # extra keys: the per-block extra_keys tuples are regenerated from their
+    # spec by tests/golden/gen.py hash_extra
+    fns = {"sha256": sha256, "sha256_cbor": sha256_cbor}
+    for i, (name, algo, bs, seed, spec, xspec) in enumerate(gen.HASH_CASES_EXTRA):
+        os.environ["PYTHONHASHSEED"] = seed
+        kcu.init_none_hash(fns[algo])
+        tokens = gen.hash_tokens(spec, 200 + i)
+        extra = gen.hash_extra(xspec, len(tokens) // bs)
+        hashes = []
+        parent = None
+        for b in range(len(tokens) // bs):
+            parent = kcu.hash_block_tokens(fns[algo], parent, tokens[b * bs:(b + 1) * bs], extra[b])
+            hashes.append(bytes(parent).hex())
+        out.append(dict(name=name, algo=algo, block_size=bs, pythonhashseed=seed,
+                        none_hash=bytes(kcu.NONE_HASH).hex(), tokens=tokens, extra=xspec, hashes=hashes))
     return out
 
 

@@ -6,6 +6,7 @@ import torch
 
 from demo_b200 import hashing
 from oracle import blockhash as bh
+from tests.golden import gen
 
 pytestmark = pytest.mark.gpu
 
@@ -13,8 +14,41 @@ pytestmark = pytest.mark.gpu
 def test_golden_vectors_host_entry(golden_hashes):
     for case in golden_hashes:
         nh = bytes.fromhex(case["none_hash"])
-        got = hashing.block_hashes([case["tokens"]], case["block_size"], nh, algo=case["algo"])[0]
+        extra = ([gen.hash_extra(case["extra"], len(case["tokens"]) // case["block_size"])]
+                 if "extra" in case else None)
+        got = hashing.block_hashes([case["tokens"]], case["block_size"], nh, algo=case["algo"],
+                                   extra_keys=extra)[0]
         assert [h.hex() for h in got] == case["hashes"], case["name"]
+
+
+@pytest.mark.parametrize("algo", ["sha256", "sha256_cbor"])
+def test_random_extra_keys_match_oracle(algo):
+    """a batch mixing requests without extra keys, with LoRA / salt / image
+    keys, and with segments far longer than the kernel's ring"""
+    import hashlib as hl
+
+    rng = np.random.default_rng(77)
+    bs = 16
+    reqs, extra = [], []
+    for r in range(40):
+        toks = rng.integers(0, 128256, int(rng.integers(0, 12 * bs))).tolist()
+        nb = len(toks) // bs
+        kind = r % 4
+        if kind == 0:
+            ek = None
+        elif kind == 1:
+            ek = [("lora-%d" % r,)] * nb
+        elif kind == 2:
+            ek = [(("img-" + hl.sha256(b"%d" % b).hexdigest(), b * 3 - 8),) if b % 2 else None
+                  for b in range(nb)]
+        else:
+            ek = [("s" * int(rng.integers(200, 3000)), hl.sha256(b"e%d" % b).digest(), b) for b in range(nb)]
+        reqs.append(toks)
+        extra.append(ek)
+    nh = bh.none_hash("0", algo)
+    got = hashing.block_hashes(reqs, bs, nh, algo=algo, extra_keys=extra)
+    exp = bh.batch_block_hashes(reqs, bs, nh, algo, extra)
+    assert got == exp
 
 
 def test_golden_vectors_batched_device_entry(golden_hashes):
@@ -22,6 +56,8 @@ def test_golden_vectors_batched_device_entry(golden_hashes):
     chains of later cases continued from explicit parents"""
     by_bs = {}
     for c in golden_hashes:
+        if "extra" in c:
+            continue                       # the host entry covers extra keys
         by_bs.setdefault((c["block_size"], c["none_hash"], c["algo"]), []).append(c)
     for (bs, nh_hex, algo), cases in by_bs.items():
         toks = [c["tokens"] for c in cases]

@@ -3,6 +3,7 @@ the installed vLLM hasher and by CrossCache's own compiled mem.cpp."""
 import hashlib
 import pickle
 import random
+import struct
 
 import numpy as np
 import pytest
@@ -13,13 +14,45 @@ from tests.golden import gen
 
 
 def test_hash_restatement_matches_vllm_golden(golden_hashes):
-    assert len(golden_hashes) == len(gen.HASH_CASES) + len(gen.HASH_CASES_CBOR)
+    assert len(golden_hashes) == len(gen.HASH_CASES) + len(gen.HASH_CASES_CBOR) + len(gen.HASH_CASES_EXTRA)
     assert {c["algo"] for c in golden_hashes} == {"sha256", "sha256_cbor"}
     for case in golden_hashes:
         nh = bytes.fromhex(case["none_hash"])
         assert nh == bh.none_hash(case["pythonhashseed"], case["algo"]), case["name"]
-        got = bh.block_hashes(case["tokens"], case["block_size"], nh, case["algo"])
+        extra = (gen.hash_extra(case["extra"], len(case["tokens"]) // case["block_size"])
+                 if "extra" in case else None)
+        got = bh.block_hashes(case["tokens"], case["block_size"], nh, case["algo"], extra)
         assert [h.hex() for h in got] == case["hashes"], case["name"]
+
+
+@pytest.mark.parametrize("algo", ["sha256", "sha256_cbor"])
+def test_extra_key_segments_splice_into_the_none_byte(algo, golden_hashes):
+    """the segment demo_b200.hashing.extra_segment hands the kernel, put in
+    place of None, gives the hash function's own serialisation"""
+    from demo_b200.hashing import extra_segment
+
+    par = bytes(range(32))
+    n = 0
+    for case in golden_hashes:
+        if case.get("extra") is None or case["algo"] != algo:
+            continue
+        bs = case["block_size"]
+        toks = case["tokens"]
+        for i, ek in enumerate(gen.hash_extra(case["extra"], len(toks) // bs)):
+            blk = toks[i * bs:(i + 1) * bs]
+            seg = extra_segment(ek, algo)
+            if ek is None:
+                assert seg == b""
+                continue
+            if algo == "sha256_cbor":
+                spliced = bh.cbor_block(par, blk)[:-1] + seg
+            else:
+                base = bh.pickle_block(par, blk)
+                body = base[11:-4] + seg + base[-3:]
+                spliced = base[:3] + struct.pack("<Q", len(body)) + body
+            assert spliced == bh.serialise_with_extra(par, blk, ek, algo), (case["name"], i)
+            n += 1
+    assert n > 10
 
 
 @pytest.mark.parametrize("bs", [1, 3, 16, 23, 24, 255, 256, 300])
