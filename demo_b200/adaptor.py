@@ -51,10 +51,24 @@ def release_cache() -> None:
             cc.exit()
 
 
+def cache_key(block_hash: bytes) -> bytes:
+    """The 32-byte record key of a vLLM block hash.  sha256 / sha256_cbor
+    hashes are 32 bytes and used as they are; xxhash / xxhash_cbor give 16
+    (vllm/utils/hashing.py xxh3_128), which the reference's 32-byte key
+    compare (src/cache/cache.c:139-145) cannot take: they are zero-padded,
+    which keeps distinct digests distinct.  Longer hashes are rejected."""
+    b = bytes(block_hash)
+    if len(b) == 32:
+        return b
+    if len(b) < 32:
+        return b + bytes(32 - len(b))
+    raise ValueError(f"block hash of {len(b)} bytes: keys are 32 bytes")
+
+
 def striding_block_hashes(block_hashes: list[bytes], blocks_in_chunk: int) -> Iterable[bytes]:
-    """Hashes of blocks blocks_in_chunk-1, 2*blocks_in_chunk-1, ...
+    """Keys of blocks blocks_in_chunk-1, 2*blocks_in_chunk-1, ...
     (python/adaptor.py:32-40): one key per 256-token record."""
-    return islice(block_hashes, blocks_in_chunk - 1, None, blocks_in_chunk)
+    return (cache_key(h) for h in islice(block_hashes, blocks_in_chunk - 1, None, blocks_in_chunk))
 
 
 @dataclass

@@ -190,3 +190,21 @@ def test_layerwise_scheduler_loads_inside_the_step(sched):
     lw.update_state_after_alloc(req, _Blocks(range(64)), 512)
     meta = lw.build_connector_meta(_sched_out(new=[("LW", 1024)]))
     assert [m.direction for m in meta.requests] == ["RETRIEVE", "STORE"]
+
+
+def test_xxhash_block_hashes_become_32_byte_keys(sched):
+    """vLLM configured with xxhash (16-byte digests): the connector stores
+    and finds the records under zero-padded 32-byte keys"""
+    from demo_b200.adaptor import cache_key
+
+    conn, w = sched
+    rng = np.random.default_rng(9)
+    hashes = [rng.integers(0, 256, 16, dtype=np.uint8).tobytes() for _ in range(64)]
+    req = _request("X", 1024, 7)
+    req.block_hashes = hashes
+    keys = [cache_key(h) for h in hashes[15::16]]
+    assert all(len(k) == 32 and k[16:] == bytes(16) for k in keys)
+    assert w.store(keys[:3], np.arange(48)) == 0
+    assert conn.get_num_new_matched_tokens(req, 0) == (768, True)
+    with pytest.raises(ValueError):
+        cache_key(bytes(48))
