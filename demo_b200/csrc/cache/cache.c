@@ -135,9 +135,9 @@ static struct rt_entry *get_entry(struct worker_context *wctx)
     return e;
 }
 
-/* wait until every write-behind job of e finished; returns and clears the
- * first write error since the previous call */
-static int drain_writes(struct rt_entry *e)
+/* wait until every write-behind job of e finished; returns the first write
+ * error since the last cache_flush, clearing it when `consume` is set */
+static int drain_writes(struct rt_entry *e, int consume)
 {
     int ret;
 
@@ -145,14 +145,15 @@ static int drain_writes(struct rt_entry *e)
     while (e->disk_pending)
         pthread_cond_wait(&e->cv, &e->mu);
     ret = e->disk_err;
-    e->disk_err = 0;
+    if (consume)
+        e->disk_err = 0;
     pthread_mutex_unlock(&e->mu);
     return ret;
 }
 
 static void destroy_entry(struct rt_entry *e)
 {
-    drain_writes(e);
+    drain_writes(e, 1);
     kvmap_destroy(e->map);
     mempool_destroy(e->pool);
     if (e->host_base)
@@ -967,7 +968,7 @@ int cache_flush(struct worker_context *wctx)
 
     if (!e)
         return -ENOENT;
-    return drain_writes(e);
+    return drain_writes(e, 1);
 }
 
 int cache_get_stats(struct worker_context *wctx, struct cache_stats *out)
@@ -989,7 +990,7 @@ int cache_clear(struct worker_context *wctx)
 
     if (!e)
         return -ENOENT;
-    drain_writes(e);        /* write-behind pins its records until done */
+    drain_writes(e, 0);     /* write-behind pins its records until done */
     pthread_mutex_lock(&e->mu);
     for (i = 0; i < e->stats.records_total; i++) {
         if (kvmap_state(e->map, (int64_t)i) == KVMAP_READY &&
