@@ -217,6 +217,17 @@ def cpu_sample_run(impl: str, seconds: float | None, iters: int | None, threads:
             "times_s": [round(t, 4) for t in times]}
 
 
+def _cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def _params(ref, rec, k, v, slots, direction):
     from oracle.kvcopy import _RefParams
     kp = np.array([a.ctypes.data for a in k], np.uint64)
@@ -1224,6 +1235,10 @@ def main() -> None:
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         cpu = cpu_sample_run("port", args.cpu_seconds, None, os.cpu_count() or 1)
         cpu.pop("times_s", None)
+        # the reference's own concurrency: 4 CaCopy threads (src/cache/cache.c:777)
+        four = cpu_sample_run("port", args.cpu_seconds / 2, None, 4)
+        cpu["value_4_threads"] = round(four["value"], 3)
+        cpu["cpu_model"] = _cpu_model()
 
     if rank == 0:
         line = {

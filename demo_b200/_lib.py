@@ -144,6 +144,10 @@ SIGNATURES: dict[str, tuple] = {
     "cache_get_stats": (C.c_int, [C.POINTER(WorkerContext), C.POINTER(CacheStats)]),
     "cache_clear": (C.c_int, [C.POINTER(WorkerContext)]),
     "cache_flush": (C.c_int, [C.POINTER(WorkerContext)]),
+    "cache_store_batch": (C.c_int, [C.POINTER(WorkerContext), C.c_char_p, C.c_uint32, C.c_void_p, C.c_uint32,
+                                    C.c_void_p, C.c_void_p]),
+    "cache_load_batch": (C.c_int, [C.POINTER(WorkerContext), C.c_char_p, C.c_uint32, C.c_void_p, C.c_uint32,
+                                   C.c_void_p, C.c_void_p]),
     "cache_load_async": (C.c_int, [C.POINTER(WorkerContext), C.c_char_p, C.c_uint32, C.c_void_p, C.c_uint32,
                                    C.POINTER(C.c_void_p)]),
     "cache_store_async": (C.c_int, [C.POINTER(WorkerContext), C.c_char_p, C.c_uint32, C.c_void_p, C.c_uint32,

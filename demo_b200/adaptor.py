@@ -154,6 +154,8 @@ class WorkerAdapter:
         self._layer_store: "cc.AsyncTransfer | None" = None
         self._layer_store_ids: list[str] = []
         self._layer_load_futures: list[Future] = []
+        self._failed_load_blocks: set[int] = set()
+        self._failed_lock = threading.Lock()
 
     def _block_hashes_to_keys(self, block_hashes: list[bytes]) -> list[bytes]:
         return list(striding_block_hashes(block_hashes, self.blocks_in_chunk))
@@ -184,21 +186,39 @@ class WorkerAdapter:
             return fn(*args)
         return self._pool.submit(run)
 
+    def _per_request(self, ops: list[LoadStoreOp]) -> tuple[list[list[bytes]], list[list[int]]]:
+        kreq = [list(self._block_hashes_to_keys(op.block_hashes)) for op in ops]
+        # whole records only (cache_op ignores a trailing partial chunk too)
+        breq = [list(op.block_ids[:len(k) * self.blocks_in_chunk]) for op, k in zip(ops, kreq)]
+        return kreq, breq
+
     def store_requests(self, request_ids: list[str], ops: list[LoadStoreOp]) -> None:
-        keys, block_ids = [], []
-        for op in ops:
-            keys.extend(self._block_hashes_to_keys(op.block_hashes))
-            block_ids.extend(op.block_ids)
-        fut = self._submit(self.worker.store, keys, block_ids)
-        self.store_futures[request_ids[0]] = (fut, request_ids[1:])
+        kreq, breq = self._per_request(ops)
+
+        def run():
+            ret, st = self.worker.store_batch(kreq, breq)
+            return ret, {rid: int(s) for rid, s in zip(request_ids, st)}
+        self.store_futures[request_ids[0]] = (self._submit(run), request_ids[1:])
 
     def load_requests(self, request_ids: list[str], ops: list[LoadStoreOp]) -> None:
-        keys, block_ids = [], []
-        for op in ops:
-            keys.extend(self._block_hashes_to_keys(op.block_hashes))
-            block_ids.extend(op.block_ids)
-        fut = self._submit(self.worker.load, keys, block_ids)
-        self.load_futures[request_ids[0]] = (fut, request_ids[1:])
+        kreq, breq = self._per_request(ops)
+
+        def run():
+            ret, st = self.worker.load_batch(kreq, breq)
+            failed = [b for s, b in zip(st, breq) if s]
+            if failed:
+                with self._failed_lock:
+                    for b in failed:
+                        self._failed_load_blocks.update(int(x) for x in b)
+            return ret, {rid: int(s) for rid, s in zip(request_ids, st)}
+        self.load_futures[request_ids[0]] = (self._submit(run), request_ids[1:])
+
+    def take_failed_load_blocks(self) -> set[int]:
+        """block ids whose load failed since the last call (for vLLM's
+        get_block_ids_with_load_errors: recompute them instead)"""
+        with self._failed_lock:
+            out, self._failed_load_blocks = self._failed_load_blocks, set()
+        return out
 
     # ---- layer-wise transfers -------------------------------------------
     # The load of a step runs layer by layer on a side stream while the
@@ -225,7 +245,11 @@ class WorkerAdapter:
         ready.record(torch.cuda.current_stream(self.device))
         h = self.worker.load_async(keys, block_ids)
         if h.missing:
+            # sync loads report failures in the pass that finds them: the
+            # blocks of this step's loads are recomputed
             logger.error("Layer-wise load for %s: some records are no longer cached", request_ids)
+            with self._failed_lock:
+                self._failed_load_blocks.update(int(b) for b in block_ids)
         for l in range(self.worker.layout.num_layers):
             h.layers(l, l + 1, stream=self._load_stream, wait_event=ready if l == 0 else None)
         self._layer_load = h
@@ -282,9 +306,10 @@ class WorkerAdapter:
                     continue
                 done.add(rid)
                 done.update(others)
-                ret = fut.result() if fut.exception() is None else -1
+                out = fut.result() if fut.exception() is None else -1
+                ret, per = out if isinstance(out, tuple) else (out, {})
                 for r in [rid, *others]:
-                    self.results[r] = ret
+                    self.results[r] = per.get(r, ret)
                 if ret != 0:   # reported but still finished, as the reference does (adaptor.py:243-265)
                     logger.error("Something went wrong when processing the %s request for request_id=%s, "
                                  "result=%s", what, rid, ret)
@@ -307,5 +332,6 @@ class WorkerAdapter:
         out = []
         for d in (self.store_futures, self.load_futures):
             for fut, _ in d.values():
-                out.append(fut.result(timeout=timeout))
+                r = fut.result(timeout=timeout)
+                out.append(r[0] if isinstance(r, tuple) else r)
         return out

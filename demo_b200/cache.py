@@ -20,6 +20,7 @@ from ._lib import (CACHE_BACKEND_CUDA, CACHE_BACKEND_MEM, CacheStats, ModelInfo,
                    lib)
 
 KEY_LEN = 32
+_chunk_size = 256          # tokens per record of the running cache (init)
 
 
 class CacheError(RuntimeError):
@@ -32,9 +33,11 @@ class CacheError(RuntimeError):
 def init(chunk_size: int = 256, pool_size: int = 4 << 30, root_dir: str | None = None,
          backend: int = CACHE_BACKEND_CUDA) -> None:
     """cache_init (CrossCache cache.c:759-787) with an explicit backend."""
+    global _chunk_size
     ret = lib.cache_init_backend(chunk_size, pool_size, root_dir.encode() if root_dir else None, backend)
     if ret:
         raise CacheError("cache_init", ret)
+    _chunk_size = chunk_size
 
 
 def exit() -> None:  # noqa: A001 - mirrors cache_exit
@@ -154,6 +157,30 @@ class Worker:
         if ret and ret != -errno.ENOENT:
             raise CacheError("cache_lookup_batch", ret)
         return out
+
+    def store_batch(self, keys_per_request: Sequence[Sequence[bytes]],
+                    block_ids_per_request: Sequence[Sequence[int]]) -> tuple[int, np.ndarray]:
+        """cache_store_batch: (overall result, per-request results)"""
+        return self._batch(lib.cache_store_batch, keys_per_request, block_ids_per_request)
+
+    def load_batch(self, keys_per_request: Sequence[Sequence[bytes]],
+                   block_ids_per_request: Sequence[Sequence[int]]) -> tuple[int, np.ndarray]:
+        """cache_load_batch: (overall result, per-request results)"""
+        return self._batch(lib.cache_load_batch, keys_per_request, block_ids_per_request)
+
+    def _batch(self, fn, keys_per_request, block_ids_per_request):
+        nums = np.array([len(k) for k in keys_per_request], dtype=np.uint32)
+        bpc = _chunk_size // self.layout.block_size
+        if len(keys_per_request) != len(block_ids_per_request) or any(
+                len(bl) != len(k) * bpc for k, bl in zip(keys_per_request, block_ids_per_request)):
+            raise ValueError(f"each request needs {bpc} block ids per key")
+        kb = b"".join(_keys_buffer(k) for k in keys_per_request)
+        b = np.ascontiguousarray(np.concatenate(
+            [np.asarray(x, dtype=np.uint64) for x in block_ids_per_request]) if len(nums) else
+            np.zeros(0, np.uint64))
+        st = np.zeros(len(nums), dtype=np.int32)
+        ret = fn(C.byref(self.ctx), kb, KEY_LEN, nums.ctypes.data, len(nums), b.ctypes.data, st.ctypes.data)
+        return ret, st
 
     def stats(self) -> dict:
         s = CacheStats()

@@ -264,6 +264,14 @@ class CrossCacheConnector(KVConnectorBase_V1):
     def get_finished(self, finished_req_ids: set[str]) -> tuple[set[str] | None, set[str] | None]:
         return self.worker_adapter.get_finished(finished_req_ids)
 
+    def get_block_ids_with_load_errors(self) -> set[int]:
+        """Blocks whose load failed (a record evicted or unreadable between
+        lookup and load): vLLM recomputes them.  The reference logs the
+        failure and lets the request run on whatever the blocks held."""
+        take = getattr(self.worker_adapter, "take_failed_load_blocks", None) if hasattr(
+            self, "worker_adapter") else None
+        return take() if take is not None else set()
+
     def shutdown(self):
         if hasattr(self, "worker_adapter"):
             if not self._remote:

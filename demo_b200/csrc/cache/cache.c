@@ -596,7 +596,15 @@ struct op_args {
     uint64_t *tbids;           /* [key_num * bpc] their block ids */
     uint32_t *kpos;            /* [key_num] key index of each transfer */
     uint8_t *from_disk;        /* [key_num] load: record read from a file */
+    int32_t *kstat;            /* [key_num] per-key result, or NULL */
 };
+
+/* the first failure of key i, for the batch entry points */
+static void key_fail(struct op_args *a, uint32_t i, int ret)
+{
+    if (a->kstat && !a->kstat[i])
+        a->kstat[i] = ret;
+}
 
 static void add_transfer(struct op_args *a, uint32_t *n, uint32_t i,
                          int64_t r, int from_disk)
@@ -632,6 +640,8 @@ static int do_store(struct op_args *a)
         if (r < 0) {
             log_warn("store: pool exhausted (all records pinned/in flight)");
             ret = -ENOMEM;
+            for (; i < a->key_num; i++)
+                key_fail(a, i, -ENOMEM);
             break;
         }
         kvmap_insert(e->map, r, key, KVMAP_PENDING);
@@ -642,6 +652,8 @@ static int do_store(struct op_args *a)
     xret = n ? run_transfer(e, a->wctx, KV_D_TO_H, a->idx, a->tbids, n) : 0;
     if (xret < 0 && ret == 0)
         ret = xret;
+    for (i = 0; xret && i < n; i++)
+        key_fail(a, a->kpos[i], xret);
 
     if (xret == 0 && n && e->dfd >= 0)
         wkeys = malloc(n * sizeof(*wkeys));
@@ -701,16 +713,20 @@ static int do_load(struct op_args *a)
             cand[nc++] = i;
         } else {
             e->stats.load_misses++;
+            key_fail(a, i, -ENOENT);
             ret = -ENOENT;
         }
     }
     pthread_mutex_unlock(&e->mu);
 
     /* 2. which candidates have a file (no lock held) */
-    for (i = 0; i < nc; i++)
+    for (i = 0; i < nc; i++) {
         if (disk_stat(e->dfd, a->keys + (uint64_t)cand[i] * a->key_len,
                       e->objsize) == 0)
             cand[nd++] = cand[i];
+        else
+            key_fail(a, cand[i], -ENOENT);
+    }
 
     /* 3. a PENDING record per file; a key another thread cached meanwhile
      *    is a memory hit after all */
@@ -731,6 +747,7 @@ static int do_load(struct op_args *a)
                 add_transfer(a, &n, cand[i], r, 0);
             } else {
                 e->stats.load_misses++;
+                key_fail(a, cand[i], -ENOENT);
                 ret = -ENOENT;
             }
             continue;
@@ -741,6 +758,7 @@ static int do_load(struct op_args *a)
         if (r < 0) {
             log_warn("load: no pool record free for a disk read");
             e->stats.load_misses++;
+            key_fail(a, cand[i], -ENOMEM);
             ret = -ENOMEM;
             continue;
         }
@@ -794,6 +812,7 @@ static int do_load(struct op_args *a)
         e->stats.disk_read_errors++;
         e->stats.load_misses++;
         pthread_mutex_unlock(&e->mu);
+        key_fail(a, a->kpos[i], rr == -ENOENT ? -ENOENT : -EIO);
         if (ret == 0)
             ret = rr == -ENOENT ? -ENOENT : -EIO;
     }
@@ -804,6 +823,8 @@ static int do_load(struct op_args *a)
     xret = n ? run_transfer(e, a->wctx, KV_H_TO_D, a->idx, a->tbids, n) : 0;
     if (xret < 0 && ret == 0)
         ret = xret;
+    for (i = 0; xret && i < n; i++)
+        key_fail(a, a->kpos[i], xret);
 
     /* 6. records read from disk join the memory tier (their host copy is
      *    valid even when the device transfer failed) */
@@ -827,12 +848,13 @@ static int do_load(struct op_args *a)
 
 static int cache_op(struct worker_context *wctx, uint8_t *keys,
                     uint32_t key_len, uint64_t *bids, uint32_t bnum,
-                    bool store)
+                    bool store, int32_t *kstat)
 {
     struct op_args a;
     int ret;
 
     memset(&a, 0, sizeof(a));
+    a.kstat = kstat;
     a.e = get_entry(wctx);
     if (!a.e)
         return -ENOENT;
@@ -866,13 +888,64 @@ static int cache_op(struct worker_context *wctx, uint8_t *keys,
 int cache_store(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
                 uint64_t *bids, uint32_t bnum)
 {
-    return cache_op(wctx, keys, key_len, bids, bnum, true);
+    return cache_op(wctx, keys, key_len, bids, bnum, true, NULL);
 }
 
 int cache_load(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
                uint64_t *bids, uint32_t bnum)
 {
-    return cache_op(wctx, keys, key_len, bids, bnum, false);
+    return cache_op(wctx, keys, key_len, bids, bnum, false, NULL);
+}
+
+/* several requests in one batched transfer, with a result per request */
+static int batch_op(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                    const uint32_t *key_nums, uint32_t num_req, uint64_t *bids,
+                    int32_t *req_status, bool store)
+{
+    uint64_t total = 0, off = 0;
+    uint32_t r, k, bpc;
+    int32_t *kstat;
+    int ret;
+
+    if (!req_status || (num_req && !key_nums))
+        return -EINVAL;
+    if (!get_entry(wctx)) {
+        for (r = 0; r < num_req; r++)
+            req_status[r] = -ENOENT;
+        return -ENOENT;
+    }
+    bpc = g_mgr.chunk_size / wctx->block_size;
+    for (r = 0; r < num_req; r++)
+        total += key_nums[r];
+    if (total * bpc > UINT32_MAX)
+        return -E2BIG;
+    kstat = calloc(total ? total : 1, sizeof(*kstat));
+    if (!kstat)
+        return -ENOMEM;
+    ret = cache_op(wctx, keys, key_len, bids, (uint32_t)(total * bpc), store, kstat);
+    for (r = 0; r < num_req; r++) {
+        req_status[r] = 0;
+        for (k = 0; k < key_nums[r]; k++)
+            if (kstat[off + k] && !req_status[r])
+                req_status[r] = kstat[off + k];
+        off += key_nums[r];
+    }
+    free(kstat);
+    return ret;
+}
+
+int cache_store_batch(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                      const uint32_t *key_nums, uint32_t num_req, uint64_t *bids,
+                      int32_t *req_status)
+{
+    return batch_op(wctx, keys, key_len, key_nums, num_req, bids, req_status, true);
+}
+
+int cache_load_batch(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                     const uint32_t *key_nums, uint32_t num_req, uint64_t *bids,
+                     int32_t *req_status)
+{
+    return batch_op(wctx, keys, key_len, key_nums, num_req, bids, req_status, false);
 }
 
 static uint32_t prefix_hits_locked(struct rt_entry *e, const uint8_t *keys,

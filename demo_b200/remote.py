@@ -12,6 +12,7 @@ sent only after the KV writes queued on the compute stream have finished.
 """
 from __future__ import annotations
 
+import threading
 from concurrent.futures import Future, ThreadPoolExecutor
 
 import torch
@@ -91,6 +92,8 @@ class RemoteWorkerAdapter(WorkerAdapter):
         self.previously_finished = set()
         self.results = {}
         self.registered = False
+        self._failed_load_blocks: set[int] = set()
+        self._failed_lock = threading.Lock()
 
     def register(self, kv_caches: dict[str, torch.Tensor]) -> None:
         tensors = list(kv_caches.values())
@@ -121,15 +124,21 @@ class RemoteWorkerAdapter(WorkerAdapter):
 
         def run() -> int:
             ev.synchronize()     # the server reads HBM this process wrote
-            return self.mq_client.request(
+            ret = self.mq_client.request(
                 lambda uid: P.encode_transfer(op, self.instance_id, uid, keys, block_ids), timeout=self.timeout)
+            if ret and op == P.Op.LOAD:       # one status per message: all its blocks
+                with self._failed_lock:
+                    self._failed_load_blocks.update(int(b) for b in block_ids)
+            return ret
         return self._pool.submit(run)
 
     def _gather(self, ops: list[LoadStoreOp]) -> tuple[list[bytes], list[int]]:
+        """all ops in one message, each trimmed to whole records (the server
+        answers -EINVAL when keys and blocks disagree)"""
         keys, block_ids = [], []
-        for op in ops:
-            keys.extend(self._block_hashes_to_keys(op.block_hashes))
-            block_ids.extend(op.block_ids)
+        for k, b in zip(*self._per_request(ops)):
+            keys.extend(k)
+            block_ids.extend(b)
         return keys, block_ids
 
     def store_requests(self, request_ids: list[str], ops: list[LoadStoreOp]) -> None:

@@ -73,6 +73,22 @@ int cache_lookup_batch(struct worker_context *wctx, const uint8_t *keys,
                        const uint32_t *key_nums, uint32_t num_req,
                        uint32_t key_len, uint32_t *hit_keys);
 
+/* cache_store / cache_load of num_req requests in one batched transfer.
+ * Request r owns key_nums[r] consecutive keys (key_len bytes each) and the
+ * key_nums[r] * (chunk_size / block_size) consecutive block ids that go with
+ * them.  req_status[r] receives request r's own result: 0, or the first
+ * error among its keys (-ENOENT for a key that is not cached, -ENOMEM, a
+ * transfer error), so a miss of one request does not fail the others.
+ * Returns 0 when every request succeeded, else the first error (the
+ * cache_store / cache_load convention), or -EINVAL / -ENOENT (unregistered
+ * worker: every req_status is -ENOENT). */
+int cache_store_batch(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                      const uint32_t *key_nums, uint32_t num_req, uint64_t *bids,
+                      int32_t *req_status);
+int cache_load_batch(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
+                     const uint32_t *key_nums, uint32_t num_req, uint64_t *bids,
+                     int32_t *req_status);
+
 struct cache_stats {
     uint64_t records_total;     /* records the pinned pool holds          */
     uint64_t records_used;      /* records currently mapped to a key      */

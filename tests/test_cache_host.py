@@ -376,3 +376,52 @@ def test_key_stride_wider_than_32_bytes_and_empty_calls(mem_cache):
     assert cc.lib.cache_load(C.byref(w.ctx), buf, stride, bids.ctypes.data, 0) == 0
     assert cc.lib.cache_lookup(C.byref(w.ctx), buf, 0, stride) == 0
     w.unregister()
+
+
+def test_batch_entry_points_report_per_request(mem_cache):
+    """cache_store_batch / cache_load_batch: one transfer, a result per
+    request -- a request with a missing key fails alone"""
+    case = next(c for c in CACHE_CASES if c["name"] == "gqa_bs16")
+    case = dict(case, chunks=6, num_blocks=128)
+    bpc = case["chunk_size"] // case["block_size"]
+    mem_cache(8, case)
+    src, dst = HostKV(case), HostKV(case, zero=True)
+    ws, wd = src.worker(), dst.worker()
+    ws.register()
+    wd.register()
+    keys = keys_for(6, seed=51)
+    bids, b2 = gen.block_ids(case), gen.block_ids(case, seed_offset=1)
+    split = [(0, 2), (2, 3), (3, 6)]
+    kreq = [keys[a:b] for a, b in split]
+    breq = [bids[a * bpc:b * bpc] for a, b in split]
+    ret, st = ws.store_batch(kreq, breq)
+    assert ret == 0 and st.tolist() == [0, 0, 0]
+    assert ws.stats()["stored"] == 6
+    # request 1 asks for a key that was never stored
+    missing = keys_for(1, seed=52)
+    lreq = [keys[0:2], missing + keys[2:3], keys[3:6]]
+    lb = [b2[0:2 * bpc], b2[2 * bpc:4 * bpc], b2[4 * bpc:7 * bpc]] if len(b2) >= 7 * bpc else None
+    if lb is None:
+        b2 = np.random.default_rng(5).permutation(case["num_blocks"])[:7 * bpc].astype(np.uint64)
+        lb = [b2[0:2 * bpc], b2[2 * bpc:4 * bpc], b2[4 * bpc:7 * bpc]]
+    ret, st = wd.load_batch(lreq, lb)
+    assert ret == -errno.ENOENT
+    assert st.tolist() == [0, -errno.ENOENT, 0]
+    # every cached key was still loaded where it was asked for
+    src_sel = np.concatenate([bids[0:2 * bpc], bids[2 * bpc:3 * bpc], bids[3 * bpc:6 * bpc]])
+    dst_sel = np.concatenate([lb[0], lb[1][bpc:], lb[2]])
+    recs = ok.gather(src.k, src.v, src_sel, case["chunk_size"], case["block_size"], gen.unit_of(case))
+    ek, ev = gen.paged_layers(case, zero=True)
+    ok.scatter(recs, ek, ev, dst_sel, case["chunk_size"], case["block_size"], gen.unit_of(case))
+    assert all(np.array_equal(a, b) for a, b in zip(dst.k, ek))
+    assert all(np.array_equal(a, b) for a, b in zip(dst.v, ev))
+    # more new keys in one call than the pool has records (8): the keys past
+    # that point fail, and only the request that holds them
+    more = keys_for(10, seed=53)
+    blk = np.tile(bids[:bpc], 10)
+    ret, st = ws.store_batch([more[:6], more[6:]], [blk[:6 * bpc], blk[6 * bpc:]])
+    assert ret == -errno.ENOMEM and st.tolist() == [0, -errno.ENOMEM]
+    with pytest.raises(ValueError):
+        ws.store_batch([keys[:1]], [bids[:bpc - 1]])
+    wd.unregister()
+    ws.unregister()

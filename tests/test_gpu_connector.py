@@ -138,3 +138,51 @@ def test_layerwise_worker_steps():
             assert torch.equal(kv[name][:, dst_t].view(torch.int16), new[name].view(torch.int16)), name
     finally:
         conn.shutdown()
+
+
+def test_failed_loads_are_reported_per_request():
+    """two requests in one RETRIEVE step, one of them never stored: it alone
+    fails, and its blocks come back from get_block_ids_with_load_errors"""
+    import torch
+
+    from demo_b200.adaptor import LoadStoreOp
+    from demo_b200.connector import CacheConnectorMetadata, CacheRequestMetadata, CrossCacheConnector
+    from oracle import blockhash as bh
+
+    cfg = SimpleNamespace(kv_transfer_config=_KVT(), model_config=SimpleNamespace(model="m-errors"),
+                          parallel_config=SimpleNamespace(world_size=1, rank=0),
+                          cache_config=SimpleNamespace(block_size=16))
+    conn = CrossCacheConnector(cfg, vllm_base.KVConnectorRole.WORKER)
+    kv = {f"layer.{i}": torch.randn(2, 256, 16, 8, 128, device="cuda").to(torch.bfloat16) for i in range(4)}
+    conn.register_kv_caches(kv)
+    good = bh.block_hashes(list(range(100, 100 + 512)), 16, bh.none_hash("0"))     # 32 blocks
+    bad = bh.block_hashes(list(range(900, 900 + 512)), 16, bh.none_hash("0"))
+    try:
+        m = CacheConnectorMetadata()
+        m.add_request_metadata(CacheRequestMetadata("G", "STORE", LoadStoreOp(good, list(range(32)))))
+        conn.bind_connector_metadata(m)
+        conn.wait_for_save()
+        conn.clear_connector_metadata()
+        assert conn.worker_adapter.wait_all(timeout=60) == [0]
+        m = CacheConnectorMetadata()
+        m.add_request_metadata(CacheRequestMetadata("LG", "RETRIEVE", LoadStoreOp(good, list(range(100, 132)))))
+        m.add_request_metadata(CacheRequestMetadata("LB", "RETRIEVE", LoadStoreOp(bad, list(range(140, 172)))))
+        conn.bind_connector_metadata(m)
+        conn.start_load_kv(None)
+        conn.clear_connector_metadata()
+        deadline = time.time() + 60
+        done = set()
+        while done != {"LG", "LB"} and time.time() < deadline:
+            _, l = conn.get_finished(set())
+            done |= l or set()
+            time.sleep(0.01)
+        assert done == {"LG", "LB"}
+        assert conn.get_block_ids_with_load_errors() == set(range(140, 172))
+        assert conn.get_block_ids_with_load_errors() == set()
+        res = conn.worker_adapter.results
+        assert res["G"] == 0 and res["LG"] == 0 and res["LB"] == -2
+        torch.cuda.synchronize()
+        for t in kv.values():
+            assert torch.equal(t[:, 0:32].view(torch.int16), t[:, 100:132].view(torch.int16))
+    finally:
+        conn.shutdown()
