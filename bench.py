@@ -693,8 +693,9 @@ def _layerwise_probe(args, cc, layers, layout, kp, vp, hashes, bt_save, bt_load,
             "load_hidden_frac": round(hidden, 4), "overlap_efficiency": round(overlap, 4),
             "verified_bytes": bool(ok),
             "note": "compute proxy: per layer (2048 x 4096) @ (4096 x 14336) @ (14336 x 4096) bf16; "
-                    "load = cache_load (staged, copy engines); pipelined = cache_load_async, one "
-                    "launch per layer (<= 32 CTAs, mapped host records) on a side stream"}
+                    "load = cache_load (staged, copy engines); pipelined = cache_load_async: per "
+                    "layer, copy-engine copies of the layer's slices (one command per run of "
+                    "contiguous records) into an HBM ring and a <= 32-CTA scatter, on a side stream"}
 
 
 def _serve_for_bench(q, stop, pool_bytes):

@@ -274,6 +274,17 @@ struct AsyncOp {
     cudaEvent_t slot_ready[kRing] = {};
     cudaEvent_t slot_free[kRing] = {};
     std::vector<uint8_t *> host_recs;
+    /* records in host-address order, grouped into runs of consecutive
+     * records (stride = record bytes): one copy command per run and K/V part
+     * instead of one per record -- a command costs ~4 us of copy-engine time,
+     * as much as 220 KB of transfer */
+    struct Run {
+        uint8_t *host;      /* first record of the run */
+        uint32_t pos;       /* its place in a ring slot, in records */
+        uint32_t count;
+    };
+    std::vector<Run> runs;
+    uint64_t rec_bytes = 0;
 
     /* the caller's thread queues jobs, the device's async worker thread
      * enqueues them: marks, counters and spare events are shared */
@@ -361,6 +372,7 @@ struct AsyncOp {
         for (int i = 0; i < kRing; i++)
             slot_used[i] = false;
         host_recs.clear();
+        runs.clear();
         jobs_submitted = jobs_done = 0;
         enqueue_err = 0;
         requested.clear();
@@ -416,6 +428,37 @@ struct AsyncJob {
     cudaEvent_t gate;     /* completes after the caller's wait event, or null */
 };
 
+/* Layer l of every record between the host records and ring slot `slot`
+ * (slot layout: record at position p holds K then V of the layer, nkv *
+ * layer_bytes each), on the op's copy stream. */
+bool copy_runs(AsyncOp *op, uint8_t *slot, uint32_t l, cudaMemcpyKind kind)
+{
+    const uint64_t lb = op->layer_bytes;
+    const uint64_t hp = (uint64_t)op->total_layers * lb;   /* K part -> V part in a host record */
+    const uint64_t sp = (uint64_t)op->nkv * lb;            /* record stride in the slot */
+    const bool h2d = kind == cudaMemcpyHostToDevice;
+    for (const AsyncOp::Run &rn : op->runs) {
+        uint8_t *dev = slot + (uint64_t)rn.pos * sp;
+        uint8_t *host = rn.host + (uint64_t)l * lb;
+        if (rn.count == 1) {
+            /* K and V slices of one record: two rows of the record's pitch */
+            if (!CU_OK(h2d ? cudaMemcpy2DAsync(dev, lb, host, hp, lb, op->nkv, kind, op->cs)
+                           : cudaMemcpy2DAsync(host, hp, dev, lb, lb, op->nkv, kind, op->cs)))
+                return false;
+            continue;
+        }
+        /* a run of records: one row per record, for the K part then the V part */
+        for (uint32_t kv = 0; kv < op->nkv; kv++) {
+            uint8_t *d = dev + kv * lb;
+            uint8_t *h = host + kv * hp;
+            if (!CU_OK(h2d ? cudaMemcpy2DAsync(d, sp, h, op->rec_bytes, lb, rn.count, kind, op->cs)
+                           : cudaMemcpy2DAsync(h, op->rec_bytes, d, sp, lb, rn.count, kind, op->cs)))
+                return false;
+        }
+    }
+    return true;
+}
+
 /* Enqueue one job's copies on the GPU (the device's async worker thread).
  * Appends one mark per layer range it covered to `out`. */
 int async_enqueue(AsyncOp *op, const AsyncJob &j, std::vector<AsyncOp::Mark> &out)
@@ -452,8 +495,6 @@ int async_enqueue(AsyncOp *op, const AsyncJob &j, std::vector<AsyncOp::Mark> &ou
         return mark(j.l0, j.l1, s);
     }
     const bool load = op->base.direction == 0;
-    const uint64_t lb = op->layer_bytes;
-    const uint64_t hp = (uint64_t)op->total_layers * lb;   /* K part -> V part in a host record */
     for (uint32_t l = j.l0; l < j.l1; l++) {
         const int sl = (int)(op->next_slot++ % AsyncOp::kRing);
         uint8_t *slot = op->ring + (uint64_t)sl * op->slot_bytes;
@@ -467,10 +508,8 @@ int async_enqueue(AsyncOp *op, const AsyncJob &j, std::vector<AsyncOp::Mark> &ou
         if (load) {
             if (op->slot_used[sl] && !CU_OK(cudaStreamWaitEvent(op->cs, op->slot_free[sl], 0)))
                 return -EIO;
-            for (uint32_t r = 0; r < op->nrec; r++)
-                if (!CU_OK(cudaMemcpy2DAsync(slot + (uint64_t)r * op->nkv * lb, lb, op->host_recs[r] + l * lb, hp,
-                                             lb, op->nkv, cudaMemcpyHostToDevice, op->cs)))
-                    return -EIO;
+            if (!copy_runs(op, slot, l, cudaMemcpyHostToDevice))
+                return -EIO;
             if (!CU_OK(cudaEventRecord(op->slot_ready[sl], op->cs)) ||
                 !CU_OK(cudaStreamWaitEvent(s, op->slot_ready[sl], 0)))
                 return -EIO;
@@ -491,10 +530,8 @@ int async_enqueue(AsyncOp *op, const AsyncJob &j, std::vector<AsyncOp::Mark> &ou
             if (!CU_OK(cudaEventRecord(op->slot_ready[sl], s)) ||
                 !CU_OK(cudaStreamWaitEvent(op->cs, op->slot_ready[sl], 0)))
                 return -EIO;
-            for (uint32_t r = 0; r < op->nrec; r++)
-                if (!CU_OK(cudaMemcpy2DAsync(op->host_recs[r] + l * lb, hp, slot + (uint64_t)r * op->nkv * lb, lb,
-                                             lb, op->nkv, cudaMemcpyDeviceToHost, op->cs)))
-                    return -EIO;
+            if (!copy_runs(op, slot, l, cudaMemcpyDeviceToHost))
+                return -EIO;
             if (!CU_OK(cudaEventRecord(op->slot_free[sl], op->cs)))
                 return -EIO;
             op->slot_used[sl] = true;
@@ -1107,7 +1144,9 @@ struct transfer_async *CudaAdaptor::AsyncBegin(const struct transfer_batch *b, i
     const uint64_t slot_bytes = (uint64_t)R * nkv * lb;
     /* host records go through the copy engines unless the mode is direct or
      * the ring would be too large; HBM records are read in place */
-    bool staged = !device_recs && !direct_ && R && slot_bytes * AsyncOp::kRing <= kAsyncRingMax;
+    /* (a record is the row pitch of the copies: keep it inside int range) */
+    bool staged = !device_recs && !direct_ && R && slot_bytes * AsyncOp::kRing <= kAsyncRingMax &&
+                  (uint64_t)nkv * b->num_layers * lb <= (uint64_t)INT32_MAX;
     if (staged && !op->ensure_ring(slot_bytes * AsyncOp::kRing))
         staged = false;
     const uint64_t words = (uint64_t)R * bpr + (staged ? (uint64_t)AsyncOp::kRing * R : R);
@@ -1127,10 +1166,26 @@ struct transfer_async *CudaAdaptor::AsyncBegin(const struct transfer_batch *b, i
         op->host_recs.resize(R);
         for (uint32_t r = 0; r < R; r++)
             op->host_recs[r] = static_cast<uint8_t *>(b->records[r]);
+        op->rec_bytes = (uint64_t)nkv * b->num_layers * lb;
+        /* slot positions in host-address order, then runs of consecutive records */
+        std::vector<uint32_t> order(R);
+        for (uint32_t r = 0; r < R; r++)
+            order[r] = r;
+        std::sort(order.begin(), order.end(),
+                  [&](uint32_t a, uint32_t c) { return op->host_recs[a] < op->host_recs[c]; });
+        std::vector<uint32_t> pos(R);
+        for (uint32_t k = 0; k < R; k++) {
+            pos[order[k]] = k;
+            uint8_t *h = op->host_recs[order[k]];
+            if (k && op->runs.back().host + (uint64_t)op->runs.back().count * op->rec_bytes == h)
+                op->runs.back().count++;
+            else
+                op->runs.push_back(AsyncOp::Run{h, k, 1});
+        }
         for (int s = 0; s < AsyncOp::kRing; s++)
             for (uint32_t r = 0; r < R; r++)
                 op->h_meta[(uint64_t)R * bpr + (uint64_t)s * R + r] =
-                    (uint64_t)(uintptr_t)(op->ring + (uint64_t)s * slot_bytes + (uint64_t)r * nkv * lb);
+                    (uint64_t)(uintptr_t)(op->ring + (uint64_t)s * slot_bytes + (uint64_t)pos[r] * nkv * lb);
     } else {
         for (uint32_t r = 0; r < R; r++) {
             void *p = b->records[r];

@@ -136,3 +136,52 @@ def test_async_errors(cuda_cache):
     ws.clear()
     assert ws.stats()["records_used"] == 0
     ws.unregister()
+
+
+def test_layerwise_copies_on_a_fragmented_pool():
+    """records of one handle in descending runs (slabs freed by a clear come
+    back last-first), ascending runs and singletons: the copy engine moves
+    runs with one command each; every byte lands where the oracle says"""
+    case = dict(CASE, num_blocks=512, chunks=12)
+    rec = gen.record_bytes(case)
+    cc.init(case["chunk_size"], 12 * rec, None)
+    try:
+        src = DeviceKV(case)
+        ws = worker(src)
+        ws.register()
+        bids = gen.block_ids(case)
+        a_keys, b_keys, c_keys = keys_for(8, seed=61), keys_for(8, seed=62), keys_for(3, seed=63)
+        assert ws.store(a_keys, bids[:8 * BPC]) == 0          # slabs 0..7
+        ws.clear()
+        s = torch.cuda.Stream()
+        # async store into slabs 7, 6, ..., 0 (descending)
+        h = ws.store_async(b_keys, bids[:8 * BPC])
+        h.layers(0, CASE["num_layers"], stream=s)
+        assert h.finish() == 0
+        assert ws.store(c_keys, bids[8 * BPC:11 * BPC]) == 0   # slabs 8, 9, 10
+        pick = [(b_keys, 0), (c_keys, 0), (b_keys, 1), (c_keys, 1), (b_keys, 5), (b_keys, 2), (c_keys, 2),
+                (b_keys, 7)]
+        keys = [k[i] for k, i in pick]
+        src_chunks = [i if k is b_keys else 8 + i for k, i in pick]
+        dst = DeviceKV(case, zero=True)
+        wd = worker(dst)
+        wd.register()
+        b2 = gen.block_ids(case, seed_offset=1)[:len(pick) * BPC]
+        h = wd.load_async(keys, b2)
+        assert h.records == len(pick)
+        for l in range(CASE["num_layers"]):
+            h.layers(l, l + 1, stream=s)
+        assert h.finish() == 0
+        torch.cuda.synchronize()
+        sel = np.concatenate([bids[c * BPC:(c + 1) * BPC] for c in src_chunks])
+        k, v = gen.paged_layers(case)
+        recs = ok.gather(k, v, sel, case["chunk_size"], case["block_size"], UNIT)
+        ek, ev = gen.paged_layers(case, zero=True)
+        ok.scatter(recs, ek, ev, b2, case["chunk_size"], case["block_size"], UNIT)
+        kh, vh = dst.host()
+        assert all(np.array_equal(a, b) for a, b in zip(kh, ek))
+        assert all(np.array_equal(a, b) for a, b in zip(vh, ev))
+        wd.unregister()
+        ws.unregister()
+    finally:
+        cc.exit()
