@@ -89,15 +89,17 @@ def kvcopy_path() -> str:
     return "lsu" if os.environ.get("CROSSCACHE_KVCOPY") == "lsu" else "bulk"
 
 
-def ncu_traffic() -> float | None:
-    """DRAM bytes per gather launch from the committed ncu summary of that kernel, if any."""
+def ncu_traffic(algorithmic_bytes: int) -> float | None:
+    """DRAM bytes of one gather launch moving `algorithmic_bytes`: the committed
+    ncu summary's DRAM bytes per algorithmic byte (a launch larger than L2, so
+    traffic grows in proportion), times this launch's algorithmic bytes."""
     f = ROOT / "profiles" / ("kv_copy_gather.md" if kvcopy_path() == "lsu" else "kv_copy_bulk.md")
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_full_launch:"):
+        if line.startswith("traffic_per_algorithmic_byte:"):
             try:
-                return float(line.split(":", 1)[1].strip())
+                return round(float(line.split(":", 1)[1].strip()) * algorithmic_bytes)
             except ValueError:
                 return None
     return None
@@ -1258,8 +1260,8 @@ def main() -> None:
                                     else "kv_copy_bulk_kernel gather (TMA cp.async.bulk via shared memory)"),
                          "achieved": round(achieved, 1),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                         "peak_kind": peak_kind, "traffic": ncu_traffic(),
-                         "algorithmic_bytes_per_launch": 2 * payload,
+                         "peak_kind": peak_kind, "traffic": ncu_traffic(2 * min(batch, nrec) * rec_bytes),
+                         "algorithmic_bytes_per_launch": 2 * min(batch, nrec) * rec_bytes,
                          "gather_ms": round(gather_ms, 4), "scatter_ms": round(scatter_ms, 4),
                          "scatter_frac": round(2 * payload / (scatter_ms / 1e3) / GB / hbm_peak, 4)},
             "e2e": e2e, "link": link, "p50_load_latency_ms": round(p50, 3) if p50 is not None else None,
