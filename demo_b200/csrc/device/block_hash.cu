@@ -211,7 +211,9 @@ struct HashArgs {
  * then the trailer and the SHA-256 padding -- and (3) after every write phase
  * compress each complete 64-byte block.  Control flow is uniform across the
  * warp, so every compression runs once per warp. */
-template <typename F>
+/* EXTRA: some block carries an extra-key segment (a separate instantiation,
+ * so the common case compiles without the per-block segment lookups) */
+template <typename F, bool EXTRA>
 __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const HashArgs a)
 {
     __shared__ __align__(16) uint8_t ring_all[kWarpsPerCta][kRing];
@@ -245,7 +247,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
     for (int i = 0; i < nblk; i++, tok += bs) {
         const uint8_t *x = nullptr;
         uint32_t xlen = 0;
-        if (a.extra) {
+        if (EXTRA) {
             const uint64_t gb = (uint64_t)a.out_offsets[r] + i;
             const int64_t x0 = a.extra_offsets[gb];
             x = a.extra + x0;
@@ -386,10 +388,19 @@ extern "C" int kv_block_hash_launch_ext(const int32_t *tokens, const int64_t *to
             a.none_hash[k] = ((uint32_t)none_hash[4 * k] << 24) | ((uint32_t)none_hash[4 * k + 1] << 16) |
                              ((uint32_t)none_hash[4 * k + 2] << 8) | (uint32_t)none_hash[4 * k + 3];
     unsigned grid = (num_req + kWarpsPerCta - 1) / kWarpsPerCta;
-    if (algo == KVHASH_SHA256_CBOR)
-        block_hash_kernel<CborFmt><<<grid, kWarpsPerCta * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
-    else
-        block_hash_kernel<PickleFmt><<<grid, kWarpsPerCta * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned threads = kWarpsPerCta * 32;
+    if (algo == KVHASH_SHA256_CBOR) {
+        if (extra)
+            block_hash_kernel<CborFmt, true><<<grid, threads, 0, s>>>(a);
+        else
+            block_hash_kernel<CborFmt, false><<<grid, threads, 0, s>>>(a);
+    } else {
+        if (extra)
+            block_hash_kernel<PickleFmt, true><<<grid, threads, 0, s>>>(a);
+        else
+            block_hash_kernel<PickleFmt, false><<<grid, threads, 0, s>>>(a);
+    }
     g_cc_kernel_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
 }
