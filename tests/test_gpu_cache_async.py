@@ -185,3 +185,46 @@ def test_layerwise_copies_on_a_fragmented_pool():
         ws.unregister()
     finally:
         cc.exit()
+
+
+@pytest.mark.parametrize("name", ["mla_bs64", "tp8_shard", "test_copy_defaults"])
+def test_layerwise_roundtrip_other_layouts(name):
+    """K-only MLA latent (block 64, 1152-byte unit), a one-head TP shard
+    (256-byte unit) and the reference test's defaults (block 2, 4-token
+    records): layer-by-layer store into the pool, then layer-by-layer load
+    into a zeroed cache at a second block table, bytes against the oracle"""
+    case = next(c for c in gen.KV_CASES if c["name"] == name)
+    unit = gen.unit_of(case)
+    bpc = case["chunk_size"] // case["block_size"]
+    cc.init(case["chunk_size"], (case["chunks"] + 1) * gen.record_bytes(case), None)
+    try:
+        src, dst = DeviceKV(case), DeviceKV(case, zero=True)
+        ws, wd = worker(src), worker(dst)
+        ws.register()
+        wd.register()
+        keys = keys_for(case["chunks"], seed=71)
+        bids, b2 = gen.block_ids(case), gen.block_ids(case, seed_offset=1)
+        s = torch.cuda.Stream()
+        h = ws.store_async(keys, bids)
+        for l in range(case["num_layers"]):
+            h.layers(l, l + 1, stream=s)
+        assert h.finish() == 0
+        h = wd.load_async(keys, b2)
+        assert h.records == case["chunks"]
+        for l in reversed(range(case["num_layers"])):        # any layer order
+            h.layers(l, l + 1, stream=s)
+        assert h.finish() == 0
+        torch.cuda.synchronize()
+        k, v = gen.paged_layers(case)
+        recs = ok.gather(k, v, bids, case["chunk_size"], case["block_size"], unit)
+        ek, ev = gen.paged_layers(case, zero=True)
+        ok.scatter(recs, ek, ev, b2, case["chunk_size"], case["block_size"], unit)
+        kh, vh = dst.host()
+        assert all(np.array_equal(a, b) for a, b in zip(kh, ek))
+        if vh is not None:
+            assert all(np.array_equal(a, b) for a, b in zip(vh, ev))
+        assert len(bids) == case["chunks"] * bpc
+        wd.unregister()
+        ws.unregister()
+    finally:
+        cc.exit()
