@@ -270,10 +270,19 @@ int launch_dir(const Params &p, int vec, cudaStream_t s)
  * kBulkSpinLimit polls the kernel sets KVCOPY_ERR_TIMEOUT, waits (bounded) for
  * its other loads in flight and for its stores, and returns.
  * ---------------------------------------------------------------------- */
-constexpr uint32_t kBulkTileBytes = 32768;
+#ifndef KVCOPY_BULK_TILE_BYTES
+#define KVCOPY_BULK_TILE_BYTES 32768
+#endif
+#ifndef KVCOPY_BULK_STAGES
+#define KVCOPY_BULK_STAGES 4
+#endif
+constexpr uint32_t kBulkTileBytes = KVCOPY_BULK_TILE_BYTES;
 constexpr uint32_t kBulkMinRunBytes = 8192;    /* shorter runs: the register path was faster
                                                 * (256-byte units: 6471 vs 6223 GB/s) */
-constexpr int kBulkStages = 4;
+constexpr int kBulkStages = KVCOPY_BULK_STAGES;
+static_assert(kBulkStages >= 2 && (uint64_t)kBulkStages * kBulkTileBytes <= 227u * 1024u - 256u,
+              "bulk ring must fit the 227 KiB of shared memory a CTA can have");
+static_assert(kBulkTileBytes % 16 == 0, "bulk copies move multiples of 16 bytes");
 constexpr uint32_t kBulkSpinLimit = 1u << 24;   /* polls of ~128 ns back-off: ~2 s */
 
 struct BulkParams {
