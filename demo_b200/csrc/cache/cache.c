@@ -77,6 +77,7 @@ struct rt_entry {
     pthread_mutex_t mu;
     pthread_cond_t cv;         /* signalled when a disk write completes */
 
+    uint32_t async_live;       /* async handles begun and not yet finished */
     int dfd;                   /* namespace directory, -1 without disk tier */
     uint32_t disk_pending;     /* write-behind jobs not yet finished */
     int disk_err;              /* first write error since the last flush */
@@ -156,8 +157,15 @@ static void destroy_entry(struct rt_entry *e)
     drain_writes(e, 1);
     kvmap_destroy(e->map);
     mempool_destroy(e->pool);
-    if (e->host_base)
+    if (e->host_base && e->async_live) {
+        /* copies of unfinished async handles may still reach the pool: keep
+         * it mapped (and leak it) rather than let the device touch freed
+         * memory */
+        log_error("[%s] %u async transfers were never finished; their pinned pool is kept",
+                  e->model_tag, e->async_live);
+    } else if (e->host_base) {
         free_pinned_ptr(g_mgr.adaptor, e->host_base, e->pool_bytes);
+    }
     if (e->dfd >= 0)
         close(e->dfd);
     pthread_cond_destroy(&e->cv);
@@ -1190,6 +1198,11 @@ static int async_begin(struct worker_context *wctx, uint8_t *keys, uint32_t key_
     h->x = ret ? NULL : transfer_async_begin(g_mgr.adaptor, &tb, &err);
     free(tbids);
     free(recs);
+    if (h->x) {
+        pthread_mutex_lock(&e->mu);
+        e->async_live++;
+        pthread_mutex_unlock(&e->mu);
+    }
     if (!h->x) {
         if (!ret)
             ret = err ? err : -EIO;
@@ -1276,7 +1289,8 @@ int cache_async_finish(cache_async_t *h)
     e = h->e;
     ret = transfer_async_end(g_mgr.adaptor, h->x);
     if (ret == -ETIMEDOUT) {
-        /* the device may still touch these records: keep them pinned / pending */
+        /* the device may still touch these records: keep them pinned /
+         * pending, and the handle counted so the pool is never freed */
         log_error("async %s of %u records timed out; records stay reserved",
                   h->store ? "store" : "load", h->n);
         async_free(h);
@@ -1295,6 +1309,7 @@ int cache_async_finish(cache_async_t *h)
         }
     }
     pthread_mutex_lock(&e->mu);
+    e->async_live--;
     for (i = 0; i < h->n; i++) {
         if (!h->store) {
             kvmap_unpin(e->map, h->idx[i]);

@@ -596,7 +596,8 @@ struct DeviceCtx {
         }
     }
 
-    ~DeviceCtx()
+    /* enqueue what is queued, then end the worker */
+    void stop_worker()
     {
         {
             std::lock_guard<std::mutex> lk(jmu);
@@ -606,6 +607,8 @@ struct DeviceCtx {
         if (worker.joinable())
             worker.join();
     }
+
+    ~DeviceCtx() { stop_worker(); }
 };
 
 struct IpcSet {
@@ -647,6 +650,13 @@ public:
     ~CudaAdaptor() override
     {
         std::lock_guard<std::mutex> g(reg_mu_);
+        /* copies of async transfers a caller never finished may still be
+         * queued: let them run out before the memory they touch goes away */
+        for (auto &kv : devs_) {
+            kv.second->stop_worker();
+            if (cudaSetDevice(kv.first) == cudaSuccess)
+                cudaDeviceSynchronize();
+        }
         for (auto &kv : devs_)
             drain(kv.second.get());
         for (auto &kv : ipc_) {

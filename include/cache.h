@@ -153,7 +153,11 @@ int cache_flush(struct worker_context *wctx);
  *                       tier writes them), else drops them.  0, -EINVAL
  *                       (bad block id, or a store missing layers),
  *                       -ETIMEDOUT (records stay reserved).
- *   cache_async_records number of records the handle moves. */
+ *   cache_async_records number of records the handle moves.
+ * Finish every handle before cache_unregister / cache_exit (a handle must
+ * not be used after them).  If one is left unfinished, teardown still keeps
+ * the device safe: the entry keeps its pinned pool mapped (leaked) and
+ * cache_exit waits for the device's queued copies before unmapping memory. */
 typedef struct cache_async cache_async_t;
 
 int cache_load_async(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,

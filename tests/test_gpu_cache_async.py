@@ -228,3 +228,40 @@ def test_layerwise_roundtrip_other_layouts(name):
         ws.unregister()
     finally:
         cc.exit()
+
+
+def test_teardown_with_an_unfinished_handle_is_safe():
+    """a handle enqueued and never finished: cache_exit lets its copies run
+    out before unmapping anything (the entry keeps its pool), and the
+    context stays usable for a new cache"""
+    case = CASE
+    cc.init(case["chunk_size"], (case["chunks"] + 1) * gen.record_bytes(case), None)
+    src = DeviceKV(case)
+    ws = worker(src)
+    ws.register()
+    keys = keys_for(case["chunks"], seed=81)
+    bids = gen.block_ids(case)
+    assert ws.store(keys, bids) == 0
+    dst = DeviceKV(case, zero=True)
+    wd = worker(dst)
+    wd.register()
+    s = torch.cuda.Stream()
+    h = wd.load_async(keys, gen.block_ids(case, seed_offset=1))
+    for l in range(case["num_layers"]):
+        h.layers(l, l + 1, stream=s)
+    abandoned = h                      # never finished (finishing after exit is not allowed)
+    wd.unregister()
+    ws.unregister()
+    cc.exit()
+    torch.cuda.synchronize()
+    # a fresh cache on the same device works
+    cc.init(case["chunk_size"], (case["chunks"] + 1) * gen.record_bytes(case), None)
+    try:
+        w2 = worker(src, name="m2")
+        w2.register()
+        assert w2.store(keys, bids) == 0
+        assert w2.lookup(keys) == 32 * case["chunks"]
+        w2.unregister()
+    finally:
+        cc.exit()
+    del abandoned
