@@ -45,6 +45,7 @@
 #include <cuda_runtime.h>
 
 #include <cerrno>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -71,13 +72,9 @@ __device__ __forceinline__ uint32_t bswap(uint32_t x) { return __byte_perm(x, 0,
 
 /* one compression of the 64 message bytes at `blk` (shared memory, message
  * byte order); every lane of the warp runs it on the same data */
-__device__ __forceinline__ void sha_compress(uint32_t st[8], const uint8_t *blk)
+/* the 64 rounds over message words m (big-endian values; m is consumed) */
+__device__ __forceinline__ void sha_rounds(uint32_t st[8], uint32_t m[16])
 {
-    const uint32_t *w32 = reinterpret_cast<const uint32_t *>(blk);
-    uint32_t m[16];
-#pragma unroll
-    for (int k = 0; k < 16; k++)
-        m[k] = bswap(w32[k]);
     uint32_t a = st[0], b = st[1], c = st[2], d = st[3];
     uint32_t e = st[4], f = st[5], g = st[6], h = st[7];
 #pragma unroll
@@ -103,6 +100,16 @@ __device__ __forceinline__ void sha_compress(uint32_t st[8], const uint8_t *blk)
     }
     st[0] += a; st[1] += b; st[2] += c; st[3] += d;
     st[4] += e; st[5] += f; st[6] += g; st[7] += h;
+}
+
+__device__ __forceinline__ void sha_compress(uint32_t st[8], const uint8_t *blk)
+{
+    const uint32_t *w32 = reinterpret_cast<const uint32_t *>(blk);
+    uint32_t m[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++)
+        m[k] = bswap(w32[k]);
+    sha_rounds(st, m);
 }
 
 /* The two serialisations of the (parent, tuple(tokens), None) triple that
@@ -149,6 +156,17 @@ struct PickleFmt {
         k -= 2 + xl;
         return k == 0 ? 0x87u : (k == 1 ? 0x94u : 0x2eu);
     }
+    /* put the parent digest h (8 big-endian words) into the first message
+     * block's words m: it occupies bytes 13..44, i.e. the low 3 bytes of
+     * word 3 through the top byte of word 11 */
+    static __device__ __forceinline__ void splice_parent(uint32_t m[16], const uint32_t h[8])
+    {
+        m[3] = (m[3] & 0xff000000u) | (h[0] >> 8);
+#pragma unroll
+        for (int k = 4; k <= 10; k++)
+            m[k] = (h[k - 4] << 24) | (h[k - 3] >> 8);
+        m[11] = (h[7] << 24) | (m[11] & 0x00ffffffu);
+    }
 };
 
 struct CborFmt {
@@ -187,6 +205,16 @@ struct CborFmt {
     static __device__ __forceinline__ uint32_t trailer_byte(uint32_t k, uint32_t, const uint8_t *x, uint32_t xlen)
     {
         return xlen ? x[k] : 0xf6u;
+    }
+    /* the parent occupies bytes 3..34: the low byte of word 0 through the
+     * top 3 bytes of word 8 */
+    static __device__ __forceinline__ void splice_parent(uint32_t m[16], const uint32_t h[8])
+    {
+        m[0] = (m[0] & 0xffffff00u) | (h[0] >> 24);
+#pragma unroll
+        for (int k = 1; k <= 7; k++)
+            m[k] = (h[k - 1] << 8) | (h[k] >> 24);
+        m[8] = (h[7] << 8) | (m[8] & 0xffu);
     }
 };
 
@@ -348,6 +376,161 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) block_hash_kernel(const Has
     }
 }
 
+/* ------------------------------------------------------------------------
+ * Pipelined form (blocks of up to 256 tokens, no extra keys): two warps per
+ * chain.  The producer warp builds block i+1's whole padded message -- all
+ * but the 32 parent bytes, which depend on block i's digest -- into one of
+ * two shared-memory slots while the consumer warp compresses block i from the
+ * other slot, splicing the parent words in from the digest it holds in
+ * registers.  One named barrier (the pair's 64 threads) per block swaps the
+ * slots; both warps pass it the same number of times, and nothing spins.
+ * The message building (a global token load, the width reduction and prefix
+ * scan, the byte writes) leaves the chain's critical path, which becomes the
+ * compressions alone.
+ * ---------------------------------------------------------------------- */
+constexpr int kPipeChains = 2;            /* chains per CTA, two warps each: every consumer
+                                          * warp gets an SM sub-partition of its own */
+constexpr uint32_t kPipeMaxBlock = 256;   /* tokens per block */
+
+/* padded message bound for a block of bs tokens (pickle: 47-byte header,
+ * at most 5 bytes a token, 6-byte trailer; CBOR is shorter) */
+__host__ __device__ constexpr uint32_t pipe_slot_bytes(uint32_t bs)
+{
+    return (47u + 5u * bs + 6u + 9u + 63u) & ~63u;
+}
+
+__device__ __forceinline__ void pair_sync(uint32_t id)
+{
+    asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+
+template <typename F>
+__global__ void __launch_bounds__(kPipeChains * 64) block_hash_pipe_kernel(const HashArgs a, uint32_t slot_bytes)
+{
+    extern __shared__ __align__(16) uint8_t pipe_smem[];
+    __shared__ uint32_t slot_total[kPipeChains][2];
+    __shared__ __align__(16) uint8_t zeros[32];
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t wid = threadIdx.x >> 5;
+    const uint32_t chain = wid >> 1;
+    const bool producer = (wid & 1) == 0;
+    const uint32_t r = blockIdx.x * kPipeChains + chain;
+    if (threadIdx.x < 32)
+        zeros[threadIdx.x] = 0;
+    __syncthreads();
+    if (r >= a.num_req)
+        return;                       /* both warps of the pair together */
+    uint8_t *slots = pipe_smem + (size_t)chain * 2 * slot_bytes;
+    const uint32_t bs = a.block_size;
+    const int nblk = a.num_blocks[r];
+    const uint32_t bar = 1 + chain;   /* barrier 0 is __syncthreads */
+
+    if (producer) {
+        const int32_t *tok0 = a.tokens + a.tok_offsets[r];
+        const uint32_t hdr_len = F::hdr_len(bs);
+        const uint32_t tl = F::trailer_len(0);
+        const uint32_t groups = (bs + 31) / 32;
+        for (int s = 0; s <= nblk; s++) {
+            if (s < nblk) {
+                const int32_t *tok = tok0 + (size_t)s * bs;
+                uint8_t *msg = slots + (s & 1) * slot_bytes;
+                uint32_t wsum = 0;
+                for (uint32_t j = lane; j < bs; j += 32)
+                    wsum += F::token_width(tok[j]);
+                const uint32_t len = hdr_len + tl + __reduce_add_sync(0xffffffffu, wsum);
+                const uint32_t total = (len + 9 + 63) & ~63u;
+                const uint64_t frame = len - 11;
+                for (uint32_t p = lane; p < hdr_len; p += 32)
+                    msg[p] = (uint8_t)F::header_byte(p, bs, frame, zeros);
+                uint32_t pos = hdr_len;
+                for (uint32_t g = 0; g < groups; g++) {
+                    const uint32_t j = g * 32 + lane;
+                    const int32_t v = j < bs ? tok[j] : 0;
+                    const uint32_t wdt = j < bs ? F::token_width(v) : 0u;
+                    uint32_t incl = wdt;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        uint32_t n = __shfl_up_sync(0xffffffffu, incl, o);
+                        if (lane >= (uint32_t)o)
+                            incl += n;
+                    }
+                    const uint32_t off = pos + incl - wdt;
+                    for (uint32_t k = 0; k < wdt; k++)
+                        msg[off + k] = (uint8_t)F::token_byte(v, k);
+                    pos += __shfl_sync(0xffffffffu, incl, 31);
+                }
+                const uint32_t tbase = len - tl;
+                const uint64_t bits = (uint64_t)len * 8;
+                for (uint32_t p = pos + lane; p < total; p += 32) {
+                    uint32_t v;
+                    if (p < len)
+                        v = F::trailer_byte(p - tbase, bs, nullptr, 0);
+                    else if (p == len)
+                        v = 0x80u;
+                    else if (p < total - 8)
+                        v = 0u;
+                    else
+                        v = (uint32_t)(bits >> (8 * (total - 1 - p))) & 0xffu;
+                    msg[p] = (uint8_t)v;
+                }
+                if (lane == 0)
+                    slot_total[chain][s & 1] = total;
+            }
+            pair_sync(bar);
+        }
+        return;
+    }
+
+    /* consumer */
+    uint32_t h[8];
+    if (a.parents) {
+        const uint8_t *pp = a.parents + (uint64_t)r * 32;
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            h[k] = ((uint32_t)pp[4 * k] << 24) | ((uint32_t)pp[4 * k + 1] << 16) |
+                   ((uint32_t)pp[4 * k + 2] << 8) | (uint32_t)pp[4 * k + 3];
+    } else {
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            h[k] = a.none_hash[k];
+    }
+    uint8_t *out = a.out + (uint64_t)a.out_offsets[r] * 32;
+    for (int s = 0; s <= nblk; s++) {
+        if (s >= 1) {
+            const int i = s - 1;
+            const uint32_t *w32 = reinterpret_cast<const uint32_t *>(slots + (i & 1) * slot_bytes);
+            const uint32_t nb = slot_total[chain][i & 1] / 64;
+            uint32_t st[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a,
+                              0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
+            for (uint32_t b = 0; b < nb; b++) {
+                uint32_t m[16];
+#pragma unroll
+                for (int k = 0; k < 16; k++)
+                    m[k] = bswap(w32[b * 16 + k]);
+                if (b == 0)
+                    F::splice_parent(m, h);
+                sha_rounds(st, m);
+            }
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                h[k] = st[k];
+            uint32_t dw = h[0];
+#pragma unroll
+            for (int k = 1; k < 8; k++)
+                if (lane == (uint32_t)k)
+                    dw = h[k];
+            if (lane < 8) {
+                uint8_t *o = out + (uint64_t)i * 32 + 4 * lane;
+                o[0] = (uint8_t)(dw >> 24);
+                o[1] = (uint8_t)(dw >> 16);
+                o[2] = (uint8_t)(dw >> 8);
+                o[3] = (uint8_t)dw;
+            }
+        }
+        pair_sync(bar);
+    }
+}
+
 struct HostWorkspace {
     std::mutex mu;
     void *dbuf = nullptr;
@@ -355,6 +538,17 @@ struct HostWorkspace {
 };
 
 HostWorkspace g_ws[64];
+
+/* CROSSCACHE_HASH_KERNEL=warp keeps the one-warp-per-chain kernel */
+bool pipe_allowed_by_env()
+{
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("CROSSCACHE_HASH_KERNEL");
+        v = (e && !strcmp(e, "warp")) ? 0 : 1;
+    }
+    return v == 1;
+}
 
 }  // namespace
 
@@ -390,6 +584,17 @@ extern "C" int kv_block_hash_launch_ext(const int32_t *tokens, const int64_t *to
     unsigned grid = (num_req + kWarpsPerCta - 1) / kWarpsPerCta;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const unsigned threads = kWarpsPerCta * 32;
+    if (!extra && block_size <= kPipeMaxBlock && pipe_allowed_by_env()) {
+        const uint32_t slot = pipe_slot_bytes(block_size);
+        const unsigned pgrid = (num_req + kPipeChains - 1) / kPipeChains;
+        const size_t smem = (size_t)kPipeChains * 2 * slot;
+        if (algo == KVHASH_SHA256_CBOR)
+            block_hash_pipe_kernel<CborFmt><<<pgrid, kPipeChains * 64, smem, s>>>(a, slot);
+        else
+            block_hash_pipe_kernel<PickleFmt><<<pgrid, kPipeChains * 64, smem, s>>>(a, slot);
+        g_cc_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+        return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
+    }
     if (algo == KVHASH_SHA256_CBOR) {
         if (extra)
             block_hash_kernel<CborFmt, true><<<grid, threads, 0, s>>>(a);
