@@ -95,8 +95,9 @@ struct cache_manager {
     threadpool_t *io_write;    /* write-behind of stored records */
     threadpool_t *io_read;     /* record reads of loads */
     adaptor_t *adaptor;
-    pthread_mutex_t mu;        /* guards the entry list */
+    pthread_mutex_t mu;        /* guards the entry list and dev_workers */
     struct rt_entry *entries;
+    uint32_t dev_workers[256]; /* registered workers per device (node_id) */
 };
 
 static struct cache_manager g_mgr = {.mu = PTHREAD_MUTEX_INITIALIZER,
@@ -229,6 +230,7 @@ int cache_init_backend(uint32_t chunk_size, uint64_t pool_size,
     }
     g_mgr.adaptor = ad;
     g_mgr.backend = backend;
+    memset(g_mgr.dev_workers, 0, sizeof(g_mgr.dev_workers));
     g_mgr.chunk_size = chunk_size;
     g_mgr.pool_size = pool_size;
     g_mgr.entries = NULL;
@@ -348,6 +350,7 @@ int cache_register(struct worker_context *wctx)
             goto unpin_v;
         }
         e->ref++;
+        g_mgr.dev_workers[wctx->node_id]++;
         pthread_mutex_unlock(&g_mgr.mu);
         return 0;
     }
@@ -411,6 +414,7 @@ int cache_register(struct worker_context *wctx)
     e->stats.records_total = m_count;
     e->next = g_mgr.entries;
     g_mgr.entries = e;
+    g_mgr.dev_workers[wctx->node_id]++;
     pthread_mutex_unlock(&g_mgr.mu);
     log_debug("register [%s,%u,%u] records:%lu x %lu B", e->model_tag,
               e->tp_size, e->tp_id, (unsigned long)m_count,
@@ -431,6 +435,7 @@ void cache_unregister(struct worker_context *wctx)
 {
     struct rt_entry *e, **pp;
     uint8_t nid;
+    int last;
 
     if (!g_mgr.initialised || !wctx || !wctx->model.model_name)
         return;
@@ -454,9 +459,15 @@ void cache_unregister(struct worker_context *wctx)
     if (wctx->v_ptrs)
         close_ipc_keys(g_mgr.adaptor, wctx->v_ptrs);
     wctx->k_ptrs = wctx->v_ptrs = NULL;
-    /* CUDA backend: drains and releases this process's streams and staging
-     * buffers on the device; it never resets a (shared) GPU. */
-    reset_device(g_mgr.adaptor, nid);
+    /* CUDA backend: releases this process's idle streams and staging
+     * buffers on the device once its last registered worker has left
+     * (another worker's transfers may be running); it never resets a
+     * (shared) GPU. */
+    pthread_mutex_lock(&g_mgr.mu);
+    last = g_mgr.dev_workers[nid] > 0 && --g_mgr.dev_workers[nid] == 0;
+    pthread_mutex_unlock(&g_mgr.mu);
+    if (last)
+        reset_device(g_mgr.adaptor, nid);
 }
 
 /* ------------------------------------------------------------------ */

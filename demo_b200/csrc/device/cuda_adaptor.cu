@@ -807,18 +807,32 @@ public:
     int AsyncQuery(struct transfer_async *h) override;
     int AsyncEnd(struct transfer_async *h) override;
 
+    /* Release this process's idle transfer resources on the device (lanes:
+     * streams, staging rings, metadata; finished async ops).  Lanes and ops
+     * in use by other threads stay, and so does the device context, which
+     * transfers in flight still point to; the GPU itself is never reset. */
     void Reset(uint8_t nid) override
     {
-        std::unique_ptr<DeviceCtx> ctx;
+        DeviceCtx *ctx;
         {
             std::lock_guard<std::mutex> g(reg_mu_);
             auto it = devs_.find(nid);
             if (it == devs_.end())
                 return;
-            ctx = std::move(it->second);
-            devs_.erase(it);
+            ctx = it->second.get();
         }
-        drain(ctx.get());
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        for (Lane *l : ctx->idle) {
+            ctx->all.erase(std::remove(ctx->all.begin(), ctx->all.end(), l), ctx->all.end());
+            l->release();
+            delete l;
+        }
+        ctx->idle.clear();
+        for (AsyncOp *op : ctx->async_idle) {
+            op->release();
+            delete op;
+        }
+        ctx->async_idle.clear();
     }
 
 private:
