@@ -78,6 +78,7 @@ struct rt_entry {
     pthread_cond_t cv;         /* signalled when a disk write completes */
 
     uint32_t async_live;       /* async handles begun and not yet finished */
+    int32_t busy;              /* API calls using the entry (g_mgr.mu) */
     int dfd;                   /* namespace directory, -1 without disk tier */
     uint32_t disk_pending;     /* write-behind jobs not yet finished */
     int disk_err;              /* first write error since the last flush */
@@ -95,12 +96,14 @@ struct cache_manager {
     threadpool_t *io_write;    /* write-behind of stored records */
     threadpool_t *io_read;     /* record reads of loads */
     adaptor_t *adaptor;
-    pthread_mutex_t mu;        /* guards the entry list and dev_workers */
+    pthread_mutex_t mu;        /* guards the entry list, dev_workers, busy */
+    pthread_cond_t idle_cv;    /* an entry's busy count reached 0 */
     struct rt_entry *entries;
     uint32_t dev_workers[256]; /* registered workers per device (node_id) */
 };
 
 static struct cache_manager g_mgr = {.mu = PTHREAD_MUTEX_INITIALIZER,
+                                     .idle_cv = PTHREAD_COND_INITIALIZER,
                                      .dirfd = -1};
 
 /* a store waits at most this long for write-behind to release pool records */
@@ -125,6 +128,10 @@ static struct rt_entry *find_entry_locked(const char *tag, uint8_t tp_size,
     return NULL;
 }
 
+/* The entry of wctx's (model, world size, rank), held busy until
+ * put_entry: the last cache_unregister unlinks an entry and waits for its
+ * busy calls before freeing it (a lookup needs no registration of its own,
+ * so it can race with the last worker leaving). */
 static struct rt_entry *get_entry(struct worker_context *wctx)
 {
     struct rt_entry *e;
@@ -133,8 +140,34 @@ static struct rt_entry *get_entry(struct worker_context *wctx)
     pthread_mutex_lock(&g_mgr.mu);
     e = find_entry_locked(wctx->model.model_name, wctx->world_size,
                           wctx->rank_id);
+    if (e)
+        e->busy++;
     pthread_mutex_unlock(&g_mgr.mu);
     return e;
+}
+
+static void put_entry(struct rt_entry *e)
+{
+    pthread_mutex_lock(&g_mgr.mu);
+    if (--e->busy == 0)
+        pthread_cond_broadcast(&g_mgr.idle_cv);
+    pthread_mutex_unlock(&g_mgr.mu);
+}
+
+/* whether wctx's entry is registered (for error codes only) */
+static int get_entry_exists(struct worker_context *wctx)
+{
+    struct rt_entry *e = get_entry(wctx);
+    if (e)
+        put_entry(e);
+    return e != NULL;
+}
+
+/* with g_mgr.mu held: wait until no API call uses e (they all end) */
+static void wait_idle_locked(struct rt_entry *e)
+{
+    while (e->busy)
+        pthread_cond_wait(&g_mgr.idle_cv, &g_mgr.mu);
 }
 
 /* wait until every write-behind job of e finished; returns the first write
@@ -279,6 +312,7 @@ void cache_exit()
     g_mgr.io_write = g_mgr.io_read = NULL;
     for (e = g_mgr.entries; e; e = n) {
         n = e->next;
+        wait_idle_locked(e);
         destroy_entry(e);
     }
     g_mgr.entries = NULL;
@@ -450,7 +484,8 @@ void cache_unregister(struct worker_context *wctx)
         return;
     }
     if (--e->ref <= 0) {
-        *pp = e->next;
+        *pp = e->next;          /* no new call finds it ... */
+        wait_idle_locked(e);    /* ... and the running ones end first */
         destroy_entry(e);
     }
     pthread_mutex_unlock(&g_mgr.mu);
@@ -874,21 +909,25 @@ static int cache_op(struct worker_context *wctx, uint8_t *keys,
 
     memset(&a, 0, sizeof(a));
     a.kstat = kstat;
+    if (!keys || key_len < KVMAP_KEY_LEN || (bnum && !bids))
+        return get_entry_exists(wctx) ? -EINVAL : -ENOENT;
     a.e = get_entry(wctx);
     if (!a.e)
         return -ENOENT;
-    if (!keys || key_len < KVMAP_KEY_LEN || (bnum && !bids))
+    if (!wctx->k_ptrs) {
+        put_entry(a.e);
         return -EINVAL;
-    if (!wctx->k_ptrs)
-        return -EINVAL;
+    }
     a.wctx = wctx;
     a.keys = keys;
     a.key_len = key_len;
     a.bids = bids;
     a.bpc = g_mgr.chunk_size / wctx->block_size;
     a.key_num = bnum / a.bpc;
-    if (!a.key_num)
+    if (!a.key_num) {
+        put_entry(a.e);
         return 0;
+    }
     a.idx = malloc(a.key_num * sizeof(int64_t));
     a.kpos = malloc(a.key_num * sizeof(uint32_t));
     a.from_disk = malloc(a.key_num);
@@ -901,6 +940,7 @@ static int cache_op(struct worker_context *wctx, uint8_t *keys,
     free(a.kpos);
     free(a.from_disk);
     free(a.tbids);
+    put_entry(a.e);
     return ret;
 }
 
@@ -928,7 +968,7 @@ static int batch_op(struct worker_context *wctx, uint8_t *keys, uint32_t key_len
 
     if (!req_status || (num_req && !key_nums))
         return -EINVAL;
-    if (!get_entry(wctx)) {
+    if (!get_entry_exists(wctx)) {
         for (r = 0; r < num_req; r++)
             req_status[r] = -ENOENT;
         return -ENOENT;
@@ -1013,65 +1053,82 @@ static uint32_t prefix_hits(struct rt_entry *e, const uint8_t *keys,
 int cache_lookup(struct worker_context *wctx, uint8_t *keys, uint32_t key_num,
                  uint32_t key_len)
 {
-    struct rt_entry *e = get_entry(wctx);
+    struct rt_entry *e;
+    int ret;
 
-    if (!e || !keys || key_len < KVMAP_KEY_LEN)
+    if (!keys || key_len < KVMAP_KEY_LEN)
         return 0;
-    return (int)(prefix_hits(e, keys, key_num, key_len) * key_len);
+    e = get_entry(wctx);
+    if (!e)
+        return 0;
+    ret = (int)(prefix_hits(e, keys, key_num, key_len) * key_len);
+    put_entry(e);
+    return ret;
 }
 
 int cache_lookup_batch(struct worker_context *wctx, const uint8_t *keys,
                        const uint32_t *key_nums, uint32_t num_req,
                        uint32_t key_len, uint32_t *hit_keys)
 {
-    struct rt_entry *e = get_entry(wctx);
+    struct rt_entry *e;
     uint64_t off = 0;
     uint32_t r;
 
     if (!hit_keys || (num_req && !key_nums))
         return -EINVAL;
+    e = get_entry(wctx);
     if (!e) {
         for (r = 0; r < num_req; r++)
             hit_keys[r] = 0;
         return -ENOENT;
     }
-    if (key_len < KVMAP_KEY_LEN || (num_req && !keys))
+    if (key_len < KVMAP_KEY_LEN || (num_req && !keys)) {
+        put_entry(e);
         return -EINVAL;
+    }
     if (e->dfd >= 0) {
         for (r = 0; r < num_req; r++) {
             hit_keys[r] = prefix_hits(e, keys + off, key_nums[r], key_len);
             off += (uint64_t)key_nums[r] * key_len;
         }
-        return 0;
+    } else {
+        /* memory only: one lock acquisition for the whole batch */
+        pthread_mutex_lock(&e->mu);
+        for (r = 0; r < num_req; r++) {
+            hit_keys[r] = prefix_hits_locked(e, keys + off, key_nums[r], key_len);
+            off += (uint64_t)key_nums[r] * key_len;
+        }
+        pthread_mutex_unlock(&e->mu);
     }
-    /* memory only: one lock acquisition for the whole batch */
-    pthread_mutex_lock(&e->mu);
-    for (r = 0; r < num_req; r++) {
-        hit_keys[r] = prefix_hits_locked(e, keys + off, key_nums[r], key_len);
-        off += (uint64_t)key_nums[r] * key_len;
-    }
-    pthread_mutex_unlock(&e->mu);
+    put_entry(e);
     return 0;
 }
 
 int cache_flush(struct worker_context *wctx)
 {
     struct rt_entry *e = get_entry(wctx);
+    int ret;
 
     if (!e)
         return -ENOENT;
-    return drain_writes(e, 1);
+    ret = drain_writes(e, 1);
+    put_entry(e);
+    return ret;
 }
 
 int cache_get_stats(struct worker_context *wctx, struct cache_stats *out)
 {
-    struct rt_entry *e = get_entry(wctx);
-    if (!e || !out)
+    struct rt_entry *e;
+    if (!out)
+        return -ENOENT;
+    e = get_entry(wctx);
+    if (!e)
         return -ENOENT;
     pthread_mutex_lock(&e->mu);
     *out = e->stats;
     out->records_used = kvmap_size(e->map);
     pthread_mutex_unlock(&e->mu);
+    put_entry(e);
     return 0;
 }
 
@@ -1092,6 +1149,7 @@ int cache_clear(struct worker_context *wctx)
         }
     }
     pthread_mutex_unlock(&e->mu);
+    put_entry(e);
     return 0;
 }
 
@@ -1117,10 +1175,36 @@ static void async_free(struct cache_async *h)
     free(h);
 }
 
+static int async_begin_entry(struct rt_entry *e, struct worker_context *wctx, uint8_t *keys,
+                             uint32_t key_len, uint64_t *bids, uint32_t bnum, int store,
+                             cache_async_t **out);
+
 static int async_begin(struct worker_context *wctx, uint8_t *keys, uint32_t key_len,
                        uint64_t *bids, uint32_t bnum, int store, cache_async_t **out)
 {
     struct rt_entry *e;
+    int ret;
+
+    if (!out)
+        return -EINVAL;
+    *out = NULL;
+    if (!wctx)
+        return -ENOENT;
+    if (!keys || key_len < KVMAP_KEY_LEN || (bnum && !bids) || !wctx->k_ptrs)
+        return get_entry_exists(wctx) ? -EINVAL : -ENOENT;
+    e = get_entry(wctx);
+    if (!e)
+        return -ENOENT;
+    ret = async_begin_entry(e, wctx, keys, key_len, bids, bnum, store, out);
+    put_entry(e);
+    return ret;
+}
+
+/* async_begin with e held busy by the caller */
+static int async_begin_entry(struct rt_entry *e, struct worker_context *wctx, uint8_t *keys,
+                             uint32_t key_len, uint64_t *bids, uint32_t bnum, int store,
+                             cache_async_t **out)
+{
     struct cache_async *h;
     struct transfer_batch tb;
     uint64_t *tbids = NULL;
@@ -1128,14 +1212,6 @@ static int async_begin(struct worker_context *wctx, uint8_t *keys, uint32_t key_
     uint32_t bpc, key_num, i, misses = 0;
     int ret = 0, err = 0, waited;
 
-    if (!out)
-        return -EINVAL;
-    *out = NULL;
-    e = get_entry(wctx);
-    if (!e)
-        return -ENOENT;
-    if (!keys || key_len < KVMAP_KEY_LEN || (bnum && !bids) || !wctx->k_ptrs)
-        return -EINVAL;
     bpc = g_mgr.chunk_size / wctx->block_size;
     key_num = bnum / bpc;
     h = calloc(1, sizeof(*h));

@@ -94,3 +94,57 @@ def test_mixed_operations_keep_every_loaded_byte_right(tmp_path):
     print(last)
     # the run went through eviction, write-behind and the file fallback
     assert last["evictions"] > 0 and last["disk_writes"] > 0 and last["disk_reads"] > 0
+
+
+def test_lookups_racing_with_the_last_unregister():
+    """a lookup needs no registration of its own (the server answers them for
+    rank 0 of a model): lookups in one thread while another registers and
+    unregisters the entry's only worker must see either the entry or none,
+    never a freed one"""
+    import ctypes as C
+
+    from demo_b200._lib import CacheStats, ModelInfo, WorkerContext, lib
+
+    cc.init(CASE["chunk_size"], 2 * gen.record_bytes(CASE), None, CACHE_BACKEND_MEM)
+    stop = threading.Event()
+    errors = []
+    try:
+        keys = keys_for(4, seed=5)
+        kb = b"".join(keys)
+        name = b"m"
+
+        def lookups():
+            try:
+                ctx = WorkerContext()
+                ctx.model = ModelInfo(name, 0, 0, 0)
+                ctx.world_size = 1
+                ctx.rank_id = 0
+                st = CacheStats()
+                n = 0
+                while not stop.is_set() or n < 1000:
+                    r = lib.cache_lookup(C.byref(ctx), kb, 4, 32)
+                    if r not in (0, 32, 64, 96, 128):
+                        errors.append(r)
+                    if lib.cache_get_stats(C.byref(ctx), C.byref(st)) not in (0, -errno.ENOENT):
+                        errors.append("stats")
+                    n += 1
+                lookups.count = n
+            except Exception as e:  # noqa: BLE001 - reported below
+                errors.append(repr(e))
+
+        th = threading.Thread(target=lookups)
+        th.start()
+        src = HostKV(CASE)
+        for i in range(200):
+            w = src.worker()
+            w.register()
+            if i % 2:
+                assert w.store(keys[:1], np.arange(BPC, dtype=np.uint64)) == 0
+            w.unregister()
+        stop.set()
+        th.join()
+    finally:
+        stop.set()
+        cc.exit()
+    assert not errors, errors[:5]
+    assert lookups.count >= 1000
