@@ -88,6 +88,8 @@ class TransferBatch(C.Structure):
         ("caches_element_size", C.c_uint8),
         ("record_on_device", C.c_uint8),
         ("direction", C.c_bool),
+        ("block_stride", C.c_uint64),
+        ("head_bytes", C.c_uint32),
     ]
 
 
@@ -112,6 +114,8 @@ class KvCopyDesc(C.Structure):
         ("layer_begin", C.c_uint32),
         ("record_layers", C.c_uint32),
         ("max_ctas", C.c_uint32),
+        ("block_stride", C.c_uint64),
+        ("head_bytes", C.c_uint32),
     ]
 
 
@@ -135,6 +139,7 @@ SIGNATURES: dict[str, tuple] = {
     "cache_init_backend": (C.c_int, [C.c_uint32, C.c_uint64, C.c_char_p, C.c_int]),
     "cache_exit": (None, []),
     "cache_register": (C.c_int, [C.POINTER(WorkerContext)]),
+    "cache_register_paged": (C.c_int, [C.POINTER(WorkerContext), C.c_uint64, C.c_uint32]),
     "cache_unregister": (None, [C.POINTER(WorkerContext)]),
     "cache_lookup": (C.c_int, [C.POINTER(WorkerContext), C.c_void_p, C.c_uint32, C.c_uint32]),
     "cache_store": (C.c_int, [C.POINTER(WorkerContext), C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32]),

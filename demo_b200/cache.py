@@ -59,6 +59,10 @@ class KVLayout:
     hidden_dim_size: int     # heads * head_dim of this rank
     element_size: int
     kv: int                  # 2 = K and V, 1 = K only (MLA)
+    # paged geometry of the planes (cache_register_paged, include/cache.h):
+    # 0 / 0 = dense token-major, the reference's FlashAttention layout
+    block_stride: int = 0    # bytes from one block of a plane to the next
+    head_bytes: int = 0      # > 0: head-major blocks [heads][block_size][head_bytes]
 
     @property
     def unit(self) -> int:
@@ -120,7 +124,11 @@ class Worker:
 
     # -- reference API ------------------------------------------------------
     def register(self) -> None:
-        ret = lib.cache_register(C.byref(self.ctx))
+        lay = self.layout
+        if lay.block_stride or lay.head_bytes:
+            ret = lib.cache_register_paged(C.byref(self.ctx), lay.block_stride, lay.head_bytes)
+        else:
+            ret = lib.cache_register(C.byref(self.ctx))
         if ret:
             raise CacheError("cache_register", ret)
         self.registered = True
@@ -269,36 +277,87 @@ class AsyncTransfer:
         return lib.cache_async_finish(h)
 
 
-def layout_from_kv_tensors(kv_caches, tp_heads: int | None = None) -> tuple[KVLayout, list[int], list[int] | None]:
+def _plane_geometry(nb: int, bs: int, h: int, d: int, strides, esz: int) -> tuple[int, int]:
+    """(block_stride, head_bytes) of a plane indexed [block][token][head][dim]
+    with element strides `strides`; ValueError for a geometry the kernels
+    cannot address"""
+    sb, st, sh, sd = strides
+    if d > 1 and sd != 1:
+        raise ValueError("head_dim must be the innermost, contiguous dimension")
+    unit = h * d
+    if (h == 1 or sh == d) and st == unit:               # token-major block
+        head_bytes = 0
+    elif st == d and sh == bs * d:                        # head-major block (HND)
+        head_bytes = d * esz
+    else:
+        raise ValueError(f"unsupported KV block strides {tuple(strides)}")
+    if nb > 1 and sb < bs * unit:
+        raise ValueError("KV blocks overlap")
+    block_stride = sb * esz if nb > 1 else bs * unit * esz
+    if block_stride == bs * unit * esz and not head_bytes:
+        block_stride = 0                                  # dense: the reference layout
+    return block_stride, head_bytes
+
+
+def layout_from_kv_tensors(kv_caches, kv_layout: str | None = None
+                           ) -> tuple[KVLayout, list[int], list[int] | None]:
     """Layout and per-layer K/V plane pointers of vLLM paged caches.
 
-    kv_caches: iterable of per-layer tensors shaped [2, num_blocks, block_size,
-    heads, head_dim] (FlashAttention NHD layout, K plane then V plane) or
-    [num_blocks, block_size, width] for a K-only MLA latent cache.
+    kv_caches: iterable of per-layer tensors, all of one shape, strides and
+    dtype, each either
+      [2, num_blocks, block_size, heads, head_dim]  FlashAttention: K plane
+          then V plane (the reference's layout, src python connector)
+      [num_blocks, 2, block_size, heads, head_dim]  FlashInfer: K and V of a
+          block side by side; on sm_100 vLLM stores the block head-major
+          (the tensor is a permuted view of [num_blocks, 2, heads,
+          block_size, head_dim])
+      [num_blocks, block_size, width]               K-only MLA latent cache
+    The two 5-d forms are told apart by which leading dimension is 2;
+    `kv_layout` ("flash_attn" / "flashinfer") settles a cache of 2 blocks.
+    Strided or head-major blocks come back as a non-zero
+    KVLayout.block_stride / head_bytes (cache_register_paged).
     """
     layers = list(kv_caches)
+    if not layers:
+        raise ValueError("no KV layer tensors")
     t0 = layers[0]
+    esz = t0.element_size()
+    for t in layers:
+        if t.shape != t0.shape or t.stride() != t0.stride() or t.dtype != t0.dtype:
+            raise ValueError("KV layer tensors must share one shape, strides and dtype")
     if t0.dim() == 5:
-        _, nb, bs, h, d = t0.shape
+        if kv_layout is None:
+            if t0.shape[0] == 2 and t0.shape[1] != 2:
+                kv_layout = "flash_attn"
+            elif t0.shape[1] == 2 and t0.shape[0] != 2:
+                kv_layout = "flashinfer"
+            else:
+                raise ValueError(f"ambiguous KV tensor shape {tuple(t0.shape)}: pass kv_layout")
+        if kv_layout == "flash_attn":
+            _, nb, bs, h, d = t0.shape
+            skv, sb, st, sh, sd = t0.stride()
+        elif kv_layout == "flashinfer":
+            nb, _, bs, h, d = t0.shape
+            sb, skv, st, sh, sd = t0.stride()
+        else:
+            raise ValueError(f"unknown kv_layout {kv_layout!r}")
         kv = 2
         hidden = h * d
+        block_stride, head_bytes = _plane_geometry(nb, bs, h, d, (sb, st, sh, sd), esz)
+        k = [t.data_ptr() for t in layers]
+        v = [t.data_ptr() + skv * esz for t in layers]
     elif t0.dim() == 3:
         nb, bs, hidden = t0.shape
+        sb, st, sd = t0.stride()
         kv = 1
+        block_stride, head_bytes = _plane_geometry(nb, bs, 1, hidden, (sb, st, hidden, sd), esz)
+        k, v = [t.data_ptr() for t in layers], None
     else:
         raise ValueError(f"unsupported KV tensor shape {tuple(t0.shape)}")
-    k, v = [], []
-    for t in layers:
-        if not t.is_contiguous() or t.shape != t0.shape or t.dtype != t0.dtype:
-            raise ValueError("KV layer tensors must be contiguous and identically shaped")
-        if kv == 2:
-            k.append(t[0].data_ptr())
-            v.append(t[1].data_ptr())
-        else:
-            k.append(t.data_ptr())
     lay = KVLayout(num_layers=len(layers), num_blocks=int(nb), block_size=int(bs),
-                   hidden_dim_size=int(hidden), element_size=t0.element_size(), kv=kv)
-    return lay, k, (v if kv == 2 else None)
+                   hidden_dim_size=int(hidden), element_size=esz, kv=kv,
+                   block_stride=int(block_stride), head_bytes=int(head_bytes))
+    return lay, k, v
 
 
 __all__ = ["init", "exit", "Worker", "KVLayout", "layout_from_kv_tensors", "CacheError",

@@ -305,8 +305,17 @@ class CrossCacheConnector(KVConnectorBase_V1):
         tracker.num_vllm_hit_blocks = num_vllm_blocks
         tracker.num_cache_hit_blocks = num_cache_blocks
         need_to_load = max(0, ret - num_computed_tokens)
-        # layer-wise: loaded inside the step that computes the request
-        return need_to_load, need_to_load > 0 and not self._layerwise
+        if not self._layerwise:
+            return need_to_load, need_to_load > 0
+        # layer-wise: loaded inside the step that computes the request.  That
+        # step must compute at least one token (vLLM trims a full hit itself
+        # only for asynchronous loads), so a hit covering the whole prompt
+        # leaves its last token to the forward; the load still moves whole
+        # records, and the forward rewrites that token's slot with its own
+        # K/V.
+        if num_computed_tokens + need_to_load >= request.num_tokens:
+            need_to_load = max(0, request.num_tokens - 1 - num_computed_tokens)
+        return need_to_load, False
 
     def update_state_after_alloc(self, request: "Request", blocks: "KVCacheBlocks", num_external_tokens: int):
         tracker = self._get_request_tracker(request.request_id)

@@ -86,6 +86,15 @@ struct rt_entry {
     struct rt_entry *next;
 };
 
+/* paged geometry of a worker registered with cache_register_paged (workers
+ * of plain cache_register have none: dense token-major planes) */
+struct paged_geom {
+    const void *k_ptrs;        /* the worker's imported K layer table */
+    uint64_t block_stride;
+    uint32_t head_bytes;
+    struct paged_geom *next;
+};
+
 struct cache_manager {
     int initialised;
     uint32_t chunk_size;
@@ -100,11 +109,45 @@ struct cache_manager {
     pthread_cond_t idle_cv;    /* an entry's busy count reached 0 */
     struct rt_entry *entries;
     uint32_t dev_workers[256]; /* registered workers per device (node_id) */
+    pthread_mutex_t geom_mu;   /* leaf lock of geoms */
+    struct paged_geom *geoms;
 };
 
 static struct cache_manager g_mgr = {.mu = PTHREAD_MUTEX_INITIALIZER,
                                      .idle_cv = PTHREAD_COND_INITIALIZER,
-                                     .dirfd = -1};
+                                     .dirfd = -1,
+                                     .geom_mu = PTHREAD_MUTEX_INITIALIZER};
+
+/* the paged geometry of the worker whose K layer table is k_ptrs */
+static void geom_of(const void *k_ptrs, uint64_t *block_stride, uint32_t *head_bytes)
+{
+    struct paged_geom *g;
+
+    *block_stride = 0;
+    *head_bytes = 0;
+    pthread_mutex_lock(&g_mgr.geom_mu);
+    for (g = g_mgr.geoms; g; g = g->next)
+        if (g->k_ptrs == k_ptrs) {
+            *block_stride = g->block_stride;
+            *head_bytes = g->head_bytes;
+            break;
+        }
+    pthread_mutex_unlock(&g_mgr.geom_mu);
+}
+
+static void geom_drop(const void *k_ptrs)
+{
+    struct paged_geom *g, **pp;
+
+    pthread_mutex_lock(&g_mgr.geom_mu);
+    for (pp = &g_mgr.geoms; (g = *pp); pp = &g->next)
+        if (g->k_ptrs == k_ptrs) {
+            *pp = g->next;
+            free(g);
+            break;
+        }
+    pthread_mutex_unlock(&g_mgr.geom_mu);
+}
 
 /* a store waits at most this long for write-behind to release pool records */
 #define DISK_WAIT_SEC 30
@@ -316,6 +359,13 @@ void cache_exit()
         destroy_entry(e);
     }
     g_mgr.entries = NULL;
+    pthread_mutex_lock(&g_mgr.geom_mu);
+    while (g_mgr.geoms) {
+        struct paged_geom *g = g_mgr.geoms;
+        g_mgr.geoms = g->next;
+        free(g);
+    }
+    pthread_mutex_unlock(&g_mgr.geom_mu);
     if (g_mgr.backend == CACHE_BACKEND_CUDA)
         cuda_adaptor_destroy(g_mgr.adaptor);
     else
@@ -331,6 +381,46 @@ void cache_exit()
 }
 
 int cache_register(struct worker_context *wctx)
+{
+    return cache_register_paged(wctx, 0, 0);
+}
+
+static int register_worker(struct worker_context *wctx);
+
+int cache_register_paged(struct worker_context *wctx, uint64_t block_stride,
+                         uint32_t head_bytes)
+{
+    struct paged_geom *g = NULL;
+    uint64_t unit;
+    int ret;
+
+    if (!wctx || !wctx->block_size)
+        return -EINVAL;
+    unit = (uint64_t)wctx->model.hidden_dim_size * wctx->model.element_size;
+    if ((block_stride && block_stride < (uint64_t)wctx->block_size * unit) ||
+        (head_bytes && (!unit || unit % head_bytes)))
+        return -EINVAL;
+    if (block_stride || head_bytes) {
+        g = calloc(1, sizeof(*g));
+        if (!g)
+            return -ENOMEM;
+    }
+    ret = register_worker(wctx);
+    if (ret || !g) {
+        free(g);
+        return ret;
+    }
+    g->k_ptrs = wctx->k_ptrs;
+    g->block_stride = block_stride;
+    g->head_bytes = head_bytes;
+    pthread_mutex_lock(&g_mgr.geom_mu);
+    g->next = g_mgr.geoms;
+    g_mgr.geoms = g;
+    pthread_mutex_unlock(&g_mgr.geom_mu);
+    return 0;
+}
+
+static int register_worker(struct worker_context *wctx)
 {
     struct rt_entry *e;
     void *dptrs, *haddr = NULL, *daddr = NULL;
@@ -489,8 +579,10 @@ void cache_unregister(struct worker_context *wctx)
         destroy_entry(e);
     }
     pthread_mutex_unlock(&g_mgr.mu);
-    if (wctx->k_ptrs)
+    if (wctx->k_ptrs) {
+        geom_drop(wctx->k_ptrs);
         close_ipc_keys(g_mgr.adaptor, wctx->k_ptrs);
+    }
     if (wctx->v_ptrs)
         close_ipc_keys(g_mgr.adaptor, wctx->v_ptrs);
     wctx->k_ptrs = wctx->v_ptrs = NULL;
@@ -538,6 +630,7 @@ static int run_transfer(struct rt_entry *e, struct worker_context *wctx,
     tb.caches_element_size = wctx->model.element_size;
     tb.record_on_device = 0;
     tb.direction = direction;
+    geom_of(wctx->k_ptrs, &tb.block_stride, &tb.head_bytes);
     ret = transfer_kvcache_batch(g_mgr.adaptor, &tb);
     free(recs);
     return ret;
@@ -1282,6 +1375,7 @@ static int async_begin_entry(struct rt_entry *e, struct worker_context *wctx, ui
     tb.devid = wctx->node_id;
     tb.caches_element_size = wctx->model.element_size;
     tb.direction = store ? KV_D_TO_H : KV_H_TO_D;
+    geom_of(wctx->k_ptrs, &tb.block_stride, &tb.head_bytes);
     h->x = ret ? NULL : transfer_async_begin(g_mgr.adaptor, &tb, &err);
     free(tbids);
     free(recs);

@@ -1025,6 +1025,8 @@ int CudaAdaptor::run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch 
     d.block_size = b->block_size;
     d.num_layers = b->num_layers;
     d.direction = save ? 1 : 0;
+    d.block_stride = b->block_stride;
+    d.head_bytes = b->head_bytes;
     /* TMA bulk copies need HBM records (staging or device records) and
      * 16-byte aligned bases; mapped host records keep the register path */
     bool recs_aligned = true;
@@ -1096,13 +1098,22 @@ int CudaAdaptor::run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch 
     return finish(l, l->ks, 0);
 }
 
+/* paged geometry a kernel can address: blocks that do not overlap, heads
+ * that tile the token's unit */
+static bool geometry_ok(const struct transfer_batch *b)
+{
+    const uint64_t unit = (uint64_t)b->hidden_dim_size * b->caches_element_size;
+    return (!b->block_stride || b->block_stride >= (uint64_t)b->block_size * unit) &&
+           (!b->head_bytes || unit % b->head_bytes == 0);
+}
+
 int CudaAdaptor::TransferKVCacheBatch(struct transfer_batch *b)
 {
     if (!b->num_records)
         return 0;
     if (!b->keys_ptrs || !b->records || !b->block_ids || !b->block_size || !b->num_layers ||
         !b->num_tokens || b->num_tokens % b->block_size || !b->hidden_dim_size ||
-        !b->caches_element_size || b->devid >= num_devices_)
+        !b->caches_element_size || b->devid >= num_devices_ || !geometry_ok(b))
         return -EINVAL;
     if (!CU_OK(cudaSetDevice(b->devid)))
         return -EIO;
@@ -1131,7 +1142,7 @@ struct transfer_async *CudaAdaptor::AsyncBegin(const struct transfer_batch *b, i
     };
     if (!b->keys_ptrs || (b->num_records && (!b->records || !b->block_ids)) || !b->block_size ||
         !b->num_layers || !b->num_tokens || b->num_tokens % b->block_size || !b->hidden_dim_size ||
-        !b->caches_element_size || b->devid >= num_devices_)
+        !b->caches_element_size || b->devid >= num_devices_ || !geometry_ok(b))
         return fail(-EINVAL);
     if (!CU_OK(cudaSetDevice(b->devid)))
         return fail(-EIO);
@@ -1236,6 +1247,8 @@ struct transfer_async *CudaAdaptor::AsyncBegin(const struct transfer_batch *b, i
     d.block_size = b->block_size;
     d.num_records = R;
     d.direction = b->direction ? 1 : 0;
+    d.block_stride = b->block_stride;
+    d.head_bytes = b->head_bytes;
     d.block_ids = op->d_meta;
     d.records = op->d_meta + (uint64_t)R * bpr;
     d.record_layers = b->num_layers;

@@ -20,6 +20,12 @@
  * (slot = block_id * block_size + t % block_size, the reference's slot map
  * src/cache/cache.c:345-398).  A slot outside [0, page_buffer_size) or a null
  * layer pointer sets an error bit and the vector is skipped.
+ *
+ * The paged side may also be strided or head-major (kv_copy_desc
+ * block_stride / head_bytes: vLLM FlashInfer's [blocks][2][heads][bs][dim]
+ * on sm_100); the record side is token-major in every case.  Head-major
+ * blocks take the register path with the head split folded into the paged
+ * address; dense and strided token-major blocks may take the bulk path.
  */
 #include "kvcopy.h"
 #include "adaptor.h"
@@ -79,6 +85,11 @@ struct Params {
     int32_t *error;
     uint64_t page_buffer_size;
     uint64_t unit;
+    uint64_t block_stride;   /* bytes between consecutive blocks of a plane */
+    uint64_t head_stride;    /* head-major: block_size * head_bytes */
+    uint64_t nblk;           /* ceil(page_buffer_size / block_size) */
+    uint32_t head_bytes;     /* head-major: bytes of one head of one token */
+    uint32_t dense;          /* slot s at s * unit (block_stride == block_size * unit, token-major) */
     uint32_t vpu;            /* vectors per token unit */
     uint32_t num_tokens;
     uint32_t block_size;
@@ -90,7 +101,7 @@ struct Params {
     uint32_t layer0;         /* first record layer this launch copies */
     uint32_t rec_layers;     /* layers a record holds */
     uint32_t max_grid;       /* CTA cap, 0 = none */
-    FastDiv div_vpu, div_bs, div_tpl, div_layers, div_kv;
+    FastDiv div_vpu, div_bs, div_tpl, div_layers, div_kv, div_hb;
 };
 
 template <int V> struct VecOf;
@@ -104,33 +115,58 @@ template <typename T> __device__ __forceinline__ T load_stream(const T *p) { ret
 template <> __device__ __forceinline__ uint16_t load_stream<uint16_t>(const uint16_t *p) { return *p; }
 template <> __device__ __forceinline__ uint8_t load_stream<uint8_t>(const uint8_t *p) { return *p; }
 
-__device__ __forceinline__ int64_t slot_of(const Params &p, uint32_t r, uint32_t t)
+/* paged byte offset (from the layer plane's base) of byte o < unit of token
+ * t of record r; false when the slot is outside the paged cache */
+template <bool HND>
+__device__ __forceinline__ bool paged_offset(const Params &p, uint32_t r, uint32_t t, uint32_t o, uint64_t &off)
 {
-    if (p.slots)
-        return p.slots[(uint64_t)r * p.num_tokens + t];
-    uint32_t b = fdiv(t, p.div_bs);
-    uint32_t j = t - b * p.block_size;
-    uint64_t bid = p.block_ids[(uint64_t)r * p.bpr + b];
-    return (int64_t)(bid * p.block_size + j);
+    uint64_t blk;
+    uint32_t j;
+    if (p.slots) {
+        int64_t s = p.slots[(uint64_t)r * p.num_tokens + t];
+        if (s < 0 || (uint64_t)s >= p.page_buffer_size)
+            return false;
+        if (!HND && p.dense) {
+            off = (uint64_t)s * p.unit + o;
+            return true;
+        }
+        uint32_t s32 = (uint32_t)s;           /* page_buffer_size < 2^32 when not dense */
+        uint32_t b = fdiv(s32, p.div_bs);
+        blk = b;
+        j = s32 - b * p.block_size;
+    } else {
+        uint32_t b = fdiv(t, p.div_bs);
+        j = t - b * p.block_size;
+        blk = p.block_ids[(uint64_t)r * p.bpr + b];
+        if (blk >= p.nblk || blk * p.block_size + j >= p.page_buffer_size)
+            return false;
+    }
+    if (!HND) {
+        off = blk * p.block_stride + (uint64_t)j * p.unit + o;
+        return true;
+    }
+    uint32_t h = fdiv(o, p.div_hb);
+    off = blk * p.block_stride + (uint64_t)h * p.head_stride + (uint64_t)j * p.head_bytes + (o - h * p.head_bytes);
+    return true;
 }
 
 /* one tile copied byte by byte: used only when a base address is not aligned
  * to the vector width chosen from the unit size */
-template <bool TO_RECORD>
+template <bool TO_RECORD, bool HND>
 __device__ void copy_tile_bytes(const Params &p, uint32_t r, uint8_t *layer, uint8_t *rec,
                                 uint32_t t0, uint32_t n)
 {
     uint64_t bytes = (uint64_t)n * p.unit;
     for (uint64_t i = threadIdx.x; i < bytes; i += blockDim.x) {
         uint32_t tok = (uint32_t)(i / p.unit);
-        uint64_t off = i - (uint64_t)tok * p.unit;
-        int64_t slot = slot_of(p, r, t0 + tok);
-        if (slot < 0 || (uint64_t)slot >= p.page_buffer_size) {
+        uint32_t o = (uint32_t)(i - (uint64_t)tok * p.unit);
+        uint64_t off;
+        if (!paged_offset<HND>(p, r, t0 + tok, o, off)) {
             if (p.error)
                 atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
             continue;
         }
-        uint8_t *pg = layer + (uint64_t)slot * p.unit + off;
+        uint8_t *pg = layer + off;
         if (TO_RECORD)
             rec[i] = *pg;
         else
@@ -138,7 +174,7 @@ __device__ void copy_tile_bytes(const Params &p, uint32_t r, uint8_t *layer, uin
     }
 }
 
-template <int VEC, bool TO_RECORD, typename Shape>
+template <int VEC, bool TO_RECORD, bool HND, typename Shape>
 __global__ void __launch_bounds__(Shape::threads, Shape::min_blocks) kv_copy_kernel(const Params p)
 {
     using T = typename VecOf<VEC>::T;
@@ -166,7 +202,7 @@ __global__ void __launch_bounds__(Shape::threads, Shape::min_blocks) kv_copy_ker
             continue;
         }
         if ((reinterpret_cast<uintptr_t>(layer) | reinterpret_cast<uintptr_t>(rec)) % VEC) {
-            copy_tile_bytes<TO_RECORD>(p, r, layer, rec, t0, n);
+            copy_tile_bytes<TO_RECORD, HND>(p, r, layer, rec, t0, n);
             continue;
         }
 
@@ -182,9 +218,9 @@ __global__ void __launch_bounds__(Shape::threads, Shape::min_blocks) kv_copy_ker
                 if (i < items) {
                     uint32_t tok = fdiv(i, p.div_vpu);
                     uint32_t vec = i - tok * p.vpu;
-                    int64_t slot = slot_of(p, r, t0 + tok);
-                    if (slot >= 0 && (uint64_t)slot < p.page_buffer_size)
-                        pg[u] = reinterpret_cast<T *>(layer + (uint64_t)slot * p.unit) + vec;
+                    uint64_t off;
+                    if (paged_offset<HND>(p, r, t0 + tok, vec * (uint32_t)VEC, off))
+                        pg[u] = reinterpret_cast<T *>(layer + off);
                     else if (p.error)
                         atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
                 }
@@ -209,7 +245,7 @@ __global__ void __launch_bounds__(Shape::threads, Shape::min_blocks) kv_copy_ker
     }
 }
 
-template <int VEC, bool TO_RECORD, typename Shape>
+template <int VEC, bool TO_RECORD, bool HND, typename Shape>
 int launch_variant(const Params &p, cudaStream_t stream)
 {
     constexpr int kThreads = Shape::threads;
@@ -221,7 +257,7 @@ int launch_variant(const Params &p, cudaStream_t stream)
         return -EIO;
     std::call_once(once[dev], [&] {
         int bps = 0, sms = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, kv_copy_kernel<VEC, TO_RECORD, Shape>, kThreads, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, kv_copy_kernel<VEC, TO_RECORD, HND, Shape>, kThreads, 0);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         blocks_per_sm[dev] = bps > 0 ? bps : 1;
         sm_count[dev] = sms > 0 ? sms : 1;
@@ -231,29 +267,35 @@ int launch_variant(const Params &p, cudaStream_t stream)
         grid = p.max_grid;
     if (grid > p.num_tiles)
         grid = p.num_tiles;
-    kv_copy_kernel<VEC, TO_RECORD, Shape><<<(unsigned)grid, kThreads, 0, stream>>>(p);
+    kv_copy_kernel<VEC, TO_RECORD, HND, Shape><<<(unsigned)grid, kThreads, 0, stream>>>(p);
     g_cc_kernel_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
 }
 
-template <bool TO_RECORD, typename Shape>
+template <bool TO_RECORD, bool HND, typename Shape>
 int launch_vec(const Params &p, int vec, cudaStream_t s)
 {
     switch (vec) {
-    case 16: return launch_variant<16, TO_RECORD, Shape>(p, s);
-    case 8: return launch_variant<8, TO_RECORD, Shape>(p, s);
-    case 4: return launch_variant<4, TO_RECORD, Shape>(p, s);
-    case 2: return launch_variant<2, TO_RECORD, Shape>(p, s);
-    default: return launch_variant<1, TO_RECORD, Shape>(p, s);
+    case 16: return launch_variant<16, TO_RECORD, HND, Shape>(p, s);
+    case 8: return launch_variant<8, TO_RECORD, HND, Shape>(p, s);
+    case 4: return launch_variant<4, TO_RECORD, HND, Shape>(p, s);
+    case 2: return launch_variant<2, TO_RECORD, HND, Shape>(p, s);
+    default: return launch_variant<1, TO_RECORD, HND, Shape>(p, s);
     }
+}
+
+template <bool TO_RECORD, bool HND>
+int launch_shape(const Params &p, int vec, cudaStream_t s)
+{
+    if (p.unit < kNarrowUnitBytes)
+        return launch_vec<TO_RECORD, HND, NarrowShape>(p, vec, s);
+    return launch_vec<TO_RECORD, HND, WideShape>(p, vec, s);
 }
 
 template <bool TO_RECORD>
 int launch_dir(const Params &p, int vec, cudaStream_t s)
 {
-    if (p.unit < kNarrowUnitBytes)
-        return launch_vec<TO_RECORD, NarrowShape>(p, vec, s);
-    return launch_vec<TO_RECORD, WideShape>(p, vec, s);
+    return p.head_bytes ? launch_shape<TO_RECORD, true>(p, vec, s) : launch_shape<TO_RECORD, false>(p, vec, s);
 }
 
 /* ------------------------------------------------------------------------
@@ -293,6 +335,7 @@ struct BulkParams {
     int32_t *error;
     uint64_t num_blocks;        /* paged blocks per layer */
     uint64_t run_bytes;         /* block_size * unit */
+    uint64_t block_stride;      /* bytes between consecutive blocks of a plane */
     uint64_t layer_rec_bytes;   /* num_tokens * unit: one layer of one record part */
     uint32_t bpr;               /* blocks per record */
     uint32_t gpt;               /* blocks per tile */
@@ -423,7 +466,7 @@ __global__ void __launch_bounds__(32, 1) kv_copy_bulk_kernel(const BulkParams p)
             for (uint32_t j = 0; j < t.nb; j++) {
                 uint64_t bid = t.bids[j];
                 if (bid < p.num_blocks)
-                    bulk_g2s(stage + j * run, t.layer + bid * p.run_bytes, run, &bars[s]);
+                    bulk_g2s(stage + j * run, t.layer + bid * p.block_stride, run, &bars[s]);
                 else if (p.error)
                     atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
             }
@@ -444,7 +487,7 @@ __global__ void __launch_bounds__(32, 1) kv_copy_bulk_kernel(const BulkParams p)
                 for (uint32_t j = 0; j < t.nb; j++) {
                     uint64_t bid = t.bids[j];
                     if (bid < p.num_blocks)
-                        bulk_s2g(t.layer + bid * p.run_bytes, stage + j * run, run);
+                        bulk_s2g(t.layer + bid * p.block_stride, stage + j * run, run);
                     else if (p.error)
                         atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
                 }
@@ -546,8 +589,14 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
     const uint64_t *lv = d->layer_v ? d->layer_v + d->layer_begin : nullptr;
 
     const uint64_t run_bytes = (uint64_t)d->block_size * d->unit_bytes;
-    if ((d->flags & KVCOPY_FLAG_BULK) && !d->slots && d->unit_bytes % 16 == 0 &&
-        run_bytes >= kBulkMinRunBytes && run_bytes <= kBulkTileBytes &&
+    const uint64_t block_stride = d->block_stride ? d->block_stride : run_bytes;
+    const bool dense = block_stride == run_bytes && !d->head_bytes;
+    if (block_stride < run_bytes || (d->head_bytes && d->unit_bytes % d->head_bytes))
+        return -EINVAL;
+    if (!dense && d->slots && d->page_buffer_size >= (1ull << 32))
+        return -EINVAL;
+    if ((d->flags & KVCOPY_FLAG_BULK) && !d->slots && !d->head_bytes && d->unit_bytes % 16 == 0 &&
+        block_stride % 16 == 0 && run_bytes >= kBulkMinRunBytes && run_bytes <= kBulkTileBytes &&
         d->page_buffer_size % d->block_size == 0 && bulk_allowed_by_env()) {
         BulkParams bp{};
         bp.layer_k = lk;
@@ -560,6 +609,7 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
         bp.error = d->error;
         bp.num_blocks = d->page_buffer_size / d->block_size;
         bp.run_bytes = run_bytes;
+        bp.block_stride = block_stride;
         bp.layer_rec_bytes = (uint64_t)d->num_tokens * d->unit_bytes;
         bp.bpr = d->num_tokens / d->block_size;
         bp.gpt = (uint32_t)(kBulkTileBytes / run_bytes);
@@ -590,14 +640,20 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
     p.error = d->error;
     p.page_buffer_size = d->page_buffer_size;
     p.unit = d->unit_bytes;
+    p.block_stride = block_stride;
+    p.head_bytes = d->head_bytes;
+    p.head_stride = (uint64_t)d->block_size * d->head_bytes;
+    p.nblk = (d->page_buffer_size + d->block_size - 1) / d->block_size;
+    p.dense = dense ? 1 : 0;
     p.num_tokens = d->num_tokens;
     p.block_size = d->block_size;
     p.bpr = d->num_tokens / d->block_size;
     p.num_layers = d->num_layers;
     p.num_kv = d->layer_v ? 2 : 1;
 
+    /* a vector never straddles a token, a head or a block boundary */
     int vec = 16;
-    while (d->unit_bytes % vec)
+    while (d->unit_bytes % vec || block_stride % vec || (d->head_bytes && d->head_bytes % vec))
         vec >>= 1;
     p.vpu = d->unit_bytes / vec;
     /* tile = about kTileVectors vectors, whole tokens, at most one record layer */
@@ -619,6 +675,7 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
     p.div_tpl = make_fastdiv(tpl);
     p.div_layers = make_fastdiv(p.num_layers);
     p.div_kv = make_fastdiv(p.num_kv);
+    p.div_hb = make_fastdiv(d->head_bytes ? d->head_bytes : 1);
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     return d->direction ? launch_dir<true>(p, vec, s) : launch_dir<false>(p, vec, s);

@@ -33,14 +33,43 @@ struct RecordJob {
     cc_latch_t *latch;
 };
 
+/* paged geometry of kvcopy.h (kv_copy_desc block_stride / head_bytes) */
+struct Geom {
+    uint64_t block_stride = 0;   /* 0: block_size * unit */
+    uint32_t head_bytes = 0;     /* 0: token-major block */
+};
+
+/* token t of the record at paged slot s, geometry g: copy its unit between
+ * the plane at base and the record bytes c */
+void copy_token_strided(uint8_t *base, uint8_t *c, uint64_t s, uint32_t bs, uint64_t unit,
+                        const Geom &g, bool to_record)
+{
+    const uint64_t blk = s / bs, j = s % bs;
+    const uint64_t stride = g.block_stride ? g.block_stride : bs * unit;
+    if (!g.head_bytes) {
+        uint8_t *p = base + blk * stride + j * unit;
+        to_record ? memcpy(c, p, unit) : memcpy(p, c, unit);
+        return;
+    }
+    for (uint64_t h = 0; h < unit / g.head_bytes; h++) {
+        uint8_t *p = base + blk * stride + (h * bs + j) * g.head_bytes;
+        uint8_t *q = c + h * g.head_bytes;
+        to_record ? memcpy(q, p, g.head_bytes) : memcpy(p, q, g.head_bytes);
+    }
+}
+
 /* copy record layers [l0, l1) of one record holding L layers; slot(t) from
  * per-token slots or from block ids */
 int copy_record(uint8_t *rec, const uint64_t *kl, const uint64_t *vl,
                 const int64_t *slots, const uint64_t *bids, uint32_t bs,
                 uint64_t page_buffer_size, uint32_t L, uint32_t C,
-                uint64_t unit, bool to_record, uint32_t l0 = 0, uint32_t l1 = UINT32_MAX)
+                uint64_t unit, bool to_record, uint32_t l0 = 0, uint32_t l1 = UINT32_MAX,
+                const Geom &g = Geom{})
 {
     const int nkv = vl ? 2 : 1;
+    const bool dense = !g.head_bytes && (!g.block_stride || g.block_stride == (uint64_t)bs * unit);
+    if ((g.block_stride && g.block_stride < (uint64_t)bs * unit) || (g.head_bytes && unit % g.head_bytes))
+        return -EINVAL;
     if (l1 > L)
         l1 = L;
     for (int kv = 0; kv < nkv; kv++) {
@@ -53,9 +82,11 @@ int copy_record(uint8_t *rec, const uint64_t *kl, const uint64_t *vl,
             uint32_t t = 0;
             while (t < C) {
                 int64_t s0 = slots ? slots[t] : (int64_t)(bids[t / bs] * bs + t % bs);
+                if (!slots && bids[t / bs] >= (page_buffer_size + bs - 1) / bs)
+                    return -EINVAL;
                 uint32_t n = 1;
                 for (;;) {
-                    if (t + n >= C)
+                    if (!dense || t + n >= C)
                         break;
                     int64_t sn = slots ? slots[t + n]
                                        : (int64_t)(bids[(t + n) / bs] * bs + (t + n) % bs);
@@ -65,17 +96,29 @@ int copy_record(uint8_t *rec, const uint64_t *kl, const uint64_t *vl,
                 }
                 if (s0 < 0 || (uint64_t)s0 + n > page_buffer_size)
                     return -EINVAL;
-                uint8_t *p = base + (uint64_t)s0 * unit;
                 uint8_t *c = rl + (uint64_t)t * unit;
-                if (to_record)
-                    memcpy(c, p, n * unit);
-                else
-                    memcpy(p, c, n * unit);
+                if (!dense) {
+                    copy_token_strided(base, c, (uint64_t)s0, bs, unit, g, to_record);
+                } else {
+                    uint8_t *p = base + (uint64_t)s0 * unit;
+                    if (to_record)
+                        memcpy(c, p, n * unit);
+                    else
+                        memcpy(p, c, n * unit);
+                }
                 t += n;
             }
         }
     }
     return 0;
+}
+
+Geom geom_of(const struct transfer_batch *tb)
+{
+    Geom g;
+    g.block_stride = tb->block_stride;
+    g.head_bytes = tb->head_bytes;
+    return g;
 }
 
 void record_job(void *arg)
@@ -89,7 +132,7 @@ void record_job(void *arg)
                           tb->block_ids + (uint64_t)j->r * bpr, tb->block_size,
                           tb->page_buffer_size, tb->num_layers, tb->num_tokens,
                           (uint64_t)tb->hidden_dim_size * tb->caches_element_size,
-                          tb->direction);
+                          tb->direction, 0, UINT32_MAX, geom_of(tb));
     cc_latch_done(j->latch, ret);
 }
 
@@ -219,7 +262,7 @@ public:
                                   static_cast<const uint64_t *>(tb->value_ptrs), nullptr,
                                   tb->block_ids + (uint64_t)r * bpr, tb->block_size,
                                   tb->page_buffer_size, tb->num_layers, tb->num_tokens, unit,
-                                  tb->direction, l0, l1);
+                                  tb->direction, l0, l1, geom_of(tb));
             if (ret) {
                 h->err = ret;
                 return 0;       /* reported by AsyncEnd, as the device backend does */

@@ -16,34 +16,39 @@ IPC_HANDLE_BYTES = 64
 KEY_BYTES = IPC_HANDLE_BYTES + 8
 
 
-def ipckey_from_tensor(t: torch.Tensor) -> bytes:
-    """72-byte key of the tensor's first element (include/device.h
-    ipc_export_key): handle of the enclosing cudaMalloc block + byte offset."""
+def ipckey_from_ptr(ptr: int) -> bytes:
+    """72-byte key of a device address (include/device.h ipc_export_key):
+    handle of the enclosing cudaMalloc block + byte offset of `ptr`."""
     import ctypes as C
 
     from ._lib import lib
 
-    if not t.is_cuda:
-        raise ValueError("tensor must be on a CUDA device")
-    if not t.is_contiguous():
-        raise ValueError("tensor must be contiguous")
     buf = (C.c_uint8 * KEY_BYTES)()
-    ret = lib.ipc_export_key(C.c_void_p(t.data_ptr()), buf)
+    ret = lib.ipc_export_key(C.c_void_p(ptr), buf)
     if ret:
         raise RuntimeError(f"ipc_export_key failed: {ret}")
     return bytes(buf)
 
 
+def ipckey_from_tensor(t: torch.Tensor) -> bytes:
+    """72-byte key of the tensor's first element (ipckey_from_ptr)."""
+    if not t.is_cuda:
+        raise ValueError("tensor must be on a CUDA device")
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    return ipckey_from_ptr(t.data_ptr())
+
+
 def layer_keys(kv_caches) -> tuple[bytes, bytes | None]:
     """Concatenated K keys and V keys (None for a K-only cache) of per-layer
-    tensors shaped [2, num_blocks, block_size, heads, head_dim] or
-    [num_blocks, block_size, width] -- the k_raw_ptrs / v_raw_ptrs of a
-    worker_context registered with per_len 72."""
-    ks, vs = [], []
-    for t in kv_caches:
-        if t.dim() == 5:
-            ks.append(ipckey_from_tensor(t[0]))
-            vs.append(ipckey_from_tensor(t[1]))
-        else:
-            ks.append(ipckey_from_tensor(t))
-    return b"".join(ks), (b"".join(vs) if vs else None)
+    vLLM KV tensors (the forms demo_b200.cache.layout_from_kv_tensors
+    takes): the key of each layer's K plane and V plane base -- the
+    k_raw_ptrs / v_raw_ptrs of a worker_context registered with per_len 72."""
+    from . import cache as cc
+
+    layers = list(kv_caches)
+    if any(not t.is_cuda for t in layers):
+        raise ValueError("KV tensors must be on a CUDA device")
+    _, kp, vp = cc.layout_from_kv_tensors(layers)
+    ks = b"".join(ipckey_from_ptr(p) for p in kp)
+    return ks, (b"".join(ipckey_from_ptr(p) for p in vp) if vp is not None else None)

@@ -20,7 +20,10 @@ version field (1 on REGISTER, left 0 on the others; the server checks it on
 REGISTER only, main.c:257-261, as decode_request does here).  Differences:
 UNREGISTER encodes (the reference encoder returns None for it, so its
 unregister cannot be sent); decode_request checks every length against the
-frame instead of trusting them.
+frame instead of trusting them; a REGISTER of a worker whose planes are not
+dense token-major (vLLM FlashInfer) ends with a 16-byte paged-geometry
+trailer after the keys (b"PGEO", uint64 block_stride, uint32 head_bytes),
+sent only for such workers, so a dense worker's REGISTER is the reference's.
 """
 from __future__ import annotations
 
@@ -51,6 +54,8 @@ REGISTER = struct.Struct("<BBBBIIII")   # msg_register
 COMMON = struct.Struct("<II")           # msg_common
 LOOKUP_TAIL = struct.Struct("<B")       # msg_lookup
 RESPONSE = struct.Struct("<II")         # msg_response
+GEOMETRY = struct.Struct("<4sQI")       # REGISTER trailer of a non-dense worker
+GEOMETRY_MAGIC = b"PGEO"
 
 
 class ProtocolError(ValueError):
@@ -89,6 +94,8 @@ class Register:
     k_keys: bytes                 # num_layers * key_len
     v_keys: bytes | None          # same, or None for a K-only cache
     version: int = CACHE_VERSION
+    block_stride: int = 0         # paged geometry trailer (0 / 0: dense)
+    head_bytes: int = 0
 
     @property
     def num_layers(self) -> int:
@@ -147,9 +154,11 @@ def _keys(keys) -> tuple[bytes, int, int]:
 
 def encode_register(node_id: int, uid: int, world_size: int, rank_id: int, num_blocks: int,
                     block_size: int, element_size: int, hidden_dim_size: int, key_len: int,
-                    model_name: str, layer_keys: list[tuple[bytes, ...]]) -> bytes:
+                    model_name: str, layer_keys: list[tuple[bytes, ...]], block_stride: int = 0,
+                    head_bytes: int = 0) -> bytes:
     """layer_keys: per layer (k_key,) or (k_key, v_key), each key_len bytes
-    (python/utils/protocol.py:125-180: K keys of every layer, then V keys)."""
+    (python/utils/protocol.py:125-180: K keys of every layer, then V keys).
+    A non-zero block_stride / head_bytes appends the geometry trailer."""
     if not layer_keys:
         raise ProtocolError("no layers")
     has_v = len(layer_keys[0]) > 1
@@ -163,6 +172,8 @@ def encode_register(node_id: int, uid: int, world_size: int, rank_id: int, num_b
     body += _name(model_name) + b"".join(lk[0] for lk in layer_keys)
     if has_v:
         body += b"".join(lk[1] for lk in layer_keys)
+    if block_stride or head_bytes:
+        body += GEOMETRY.pack(GEOMETRY_MAGIC, block_stride, head_bytes)
     return _header(Op.REGISTER, node_id, uid, len(body)) + body
 
 
@@ -232,12 +243,16 @@ def decode_request(frame: bytes):
         ws, rank, nl, flags, nb, bs, hid, klen = REGISTER.unpack_from(body)
         name, pos = _cstr(body, REGISTER.size)
         nk = 2 if flags & K_V_MASK else 1
-        if not nl or not klen or len(body) - pos != nk * nl * klen:
+        kend = pos + nk * nl * klen
+        stride = hb = 0
+        if nl and klen and len(body) == kend + GEOMETRY.size and body[kend:kend + 4] == GEOMETRY_MAGIC:
+            _, stride, hb = GEOMETRY.unpack_from(body, kend)
+        elif not nl or not klen or len(body) != kend:
             raise fail("register keys do not match num_layers * first_key_in_bytes")
         kk = body[pos:pos + nl * klen]
-        vk = body[pos + nl * klen:] if nk == 2 else None
+        vk = body[pos + nl * klen:kend] if nk == 2 else None
         return Register(node_id, uid, ws, rank, nb, bs, element_size_of(flags), hid, klen, name, kk, vk,
-                        version)
+                        version, stride, hb)
     if op == Op.UNREGISTER:
         return Unregister(node_id, uid)
     if op in (Op.LOOKUP, Op.STORE, Op.LOAD):

@@ -104,7 +104,8 @@ class RemoteWorkerAdapter(WorkerAdapter):
             for i in range(layout.num_layers)]
         ret = self.mq_client.request(lambda uid: P.encode_register(
             self.instance_id, uid, self.world_size, self.worker_id, layout.num_blocks, layout.block_size,
-            layout.element_size, layout.hidden_dim_size, KEY_BYTES, self.model_name, per_layer),
+            layout.element_size, layout.hidden_dim_size, KEY_BYTES, self.model_name, per_layer,
+            layout.block_stride, layout.head_bytes),
             timeout=self.timeout)
         if ret != 0:
             raise cc.CacheError("remote register", ret)

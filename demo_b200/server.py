@@ -198,7 +198,7 @@ class CacheServer:
         if m.node_id >= MAX_NODE_NUM:
             return -errno.ERANGE
         layout = cc.KVLayout(m.num_layers, m.num_blocks, m.block_size, m.hidden_dim_size, m.element_size,
-                             2 if m.v_keys is not None else 1)
+                             2 if m.v_keys is not None else 1, m.block_stride, m.head_bytes)
         w = cc.Worker.from_keys(m.model_name, layout, m.k_keys, m.v_keys, m.key_len, node_id=m.node_id,
                                 world_size=m.world_size, rank=m.rank_id)
         with self._slot_lock:

@@ -63,6 +63,21 @@ void cache_exit();
 int cache_init_backend(uint32_t chunk_size, uint64_t pool_size,
                        const char *root_dir, int backend);
 
+/* cache_register for a worker whose layer planes are not dense token-major
+ * (the reference supports only vLLM FlashAttention's
+ * [2][num_blocks][block_size][heads][head_dim]).  block_stride = bytes
+ * between consecutive blocks of a plane (0: block_size * unit); head_bytes
+ * > 0 marks head-major blocks [unit / head_bytes][block_size][head_bytes]
+ * (kv_copy_desc in kvcopy.h).  vLLM FlashInfer on sm_100 registers K
+ * planes at each layer tensor, V planes half a block later, block_stride =
+ * 2 * block_size * unit and head_bytes = head_dim * element size.  Records
+ * stay token-major, so workers of different geometries share records.
+ * cache_register(w) is cache_register_paged(w, 0, 0).  -EINVAL for a
+ * block_stride below block_size * unit or a head_bytes not dividing the
+ * unit; otherwise as cache_register. */
+int cache_register_paged(struct worker_context *wctx, uint64_t block_stride,
+                         uint32_t head_bytes);
+
 /* Batched prefix lookup over num_req requests.  Request r owns key_nums[r]
  * consecutive keys of key_len bytes (requests are packed back to back in
  * keys).  hit_keys[r] receives the number of leading keys of request r that

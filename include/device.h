@@ -104,6 +104,10 @@ struct transfer_batch {
     uint8_t caches_element_size;
     uint8_t record_on_device;
     bool direction;
+    /* paged geometry of the layer planes (kv_copy_desc block_stride /
+     * head_bytes in kvcopy.h); both 0 = dense token-major */
+    uint64_t block_stride;
+    uint32_t head_bytes;
 };
 
 int transfer_kvcache_batch(adaptor_t *adaptor, struct transfer_batch *batch);

@@ -66,11 +66,32 @@ struct kv_copy_desc {
     uint32_t layer_begin;
     uint32_t record_layers;
     uint32_t max_ctas;           /* cap on the launch's CTAs, 0 = fill the GPU */
+    /* paged geometry (new): where a slot lives inside a layer plane.  With
+     * both fields 0 the plane is dense and token-major, slot s at byte
+     * s * unit (the reference's only layout: vLLM FlashAttention,
+     * [2][num_blocks][block_size][heads][head_dim]).  Otherwise slot s sits
+     * in block b = s / block_size at token j = s % block_size, block b
+     * starting at byte b * block_stride of the plane (0: block_size * unit);
+     *   head_bytes == 0: token j at + j * unit                        (NHD)
+     *   head_bytes  > 0: the block holds unit / head_bytes heads, each
+     *                    [block_size][head_bytes]; byte o of token j's
+     *                    unit at + (o / head_bytes) * block_size *
+     *                    head_bytes + j * head_bytes + o % head_bytes (HND)
+     * vLLM FlashInfer keeps K and V of a block side by side
+     * ([num_blocks][2][...]): its K plane starts at the layer tensor, its V
+     * plane one half-block later, block_stride = 2 * block_size * unit, and
+     * on sm_100 the block is HND.  Records stay token-major whatever the
+     * paged geometry, so every geometry reads and writes the same record
+     * bytes. */
+    uint64_t block_stride;
+    uint32_t head_bytes;
 };
 
 /* Launch the gather/scatter on `stream` (a cudaStream_t, NULL = legacy
  * default stream).  Asynchronous; returns 0, or -EINVAL for a malformed
- * descriptor, or -EIO when the launch failed. */
+ * descriptor (including a block_stride below block_size * unit, a unit
+ * that head_bytes does not divide, or a non-dense geometry with
+ * page_buffer_size >= 2^32 in slot mode), or -EIO when the launch failed. */
 int kv_copy_launch(const struct kv_copy_desc *desc, void *stream);
 
 /* Algorithmic payload of one launch: kv * num_layers * num_tokens * unit_bytes

@@ -62,8 +62,10 @@ int main(void) {
   F(transfer_params, num_layers); F(transfer_params, hidden_dim_size); F(transfer_params, direction);
   S(transfer_batch); F(transfer_batch, records); F(transfer_batch, num_records);
   F(transfer_batch, num_layers); F(transfer_batch, direction);
+  F(transfer_batch, block_stride); F(transfer_batch, head_bytes);
   S(kv_copy_desc); F(kv_copy_desc, page_buffer_size); F(kv_copy_desc, direction); F(kv_copy_desc, flags);
   F(kv_copy_desc, layer_begin); F(kv_copy_desc, record_layers); F(kv_copy_desc, max_ctas);
+  F(kv_copy_desc, block_stride); F(kv_copy_desc, head_bytes);
   S(cache_stats);
   return 0;
 }

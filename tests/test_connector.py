@@ -34,7 +34,7 @@ def _cfg():
 
 def _request(rid, ntok, seed):
     toks = np.random.default_rng(seed).integers(0, 128256, ntok).tolist()
-    return SimpleNamespace(request_id=rid, all_token_ids=toks,
+    return SimpleNamespace(request_id=rid, all_token_ids=toks, num_tokens=ntok,
                            block_hashes=bh.block_hashes(toks, BS, bh.none_hash("0")))
 
 
@@ -190,6 +190,29 @@ def test_layerwise_scheduler_loads_inside_the_step(sched):
     lw.update_state_after_alloc(req, _Blocks(range(64)), 512)
     meta = lw.build_connector_meta(_sched_out(new=[("LW", 1024)]))
     assert [m.direction for m in meta.requests] == ["RETRIEVE", "STORE"]
+
+
+def test_layerwise_full_prompt_hit_leaves_the_last_token_to_compute(sched):
+    """every chunk of a 1024-token prompt cached: the in-step load may not
+    cover the whole prompt (vLLM's scheduler needs a token to compute), so
+    layer-wise answers 1023; the asynchronous mode answers 1024 and vLLM
+    trims it itself.  The load still covers all four records."""
+    conn, w = sched
+    cfg = _cfg()
+    cfg.kv_transfer_config.kv_connector_extra_config["cache.layerwise"] = True
+    lw = CrossCacheConnector(cfg, vllm_base.KVConnectorRole.SCHEDULER)
+    lw.scheduler_adapter.bind_worker(w)
+    req = _request("FULL", 1024, 11)
+    keys = bh.chunk_keys(req.block_hashes, 256 // BS)
+    assert w.store(keys, np.arange(64)) == 0
+    assert lw.get_num_new_matched_tokens(req, 0) == (1023, False)
+    lw.update_state_after_alloc(req, _Blocks(range(100, 164)), 1023)
+    meta = lw.build_connector_meta(_sched_out(new=[("FULL", 1024)]))
+    ret = [m for m in meta.requests if m.direction == "RETRIEVE"]
+    assert len(ret) == 1 and ret[0].op.block_ids == list(range(100, 164))
+    req2 = _request("FULL", 1024, 11)
+    req2.request_id = "FULL-async"
+    assert conn.get_num_new_matched_tokens(req2, 0) == (1024, True)
 
 
 def test_xxhash_block_hashes_become_32_byte_keys(sched):
