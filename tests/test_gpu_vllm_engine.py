@@ -1,0 +1,39 @@
+"""The connector inside a real vLLM engine (vLLM 0.22, single process): the
+first pass stores every whole 256-token chunk of four prompts, the second
+pass loads them and must produce the same greedy tokens.  Covers the
+FlashInfer backend vLLM picks on sm_100 (head-major blocks, registered
+with a block stride and head split), FlashAttention (the reference's dense
+layout) and the layer-wise mode, where a fully cached prompt must still
+leave vLLM's scheduler a token to compute."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+RECORDS = 16          # 4 prompts of 1024-1135 tokens: 4 whole chunks each
+
+
+def _run(mode: str, backend: str) -> dict:
+    pytest.importorskip("vllm")
+    p = subprocess.run([sys.executable, os.path.join(HERE, "vllm_engine_run.py"), mode, backend],
+                       capture_output=True, text=True, timeout=900, cwd=os.path.dirname(HERE))
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("ENGINE_RESULT ")]
+    assert p.returncode == 0 and lines, p.stderr[-4000:]
+    return json.loads(lines[-1].split(" ", 1)[1])
+
+
+@pytest.mark.parametrize("mode,backend", [("plain", "auto"), ("layerwise", "auto"), ("plain", "FLASH_ATTN")])
+def test_second_pass_is_served_from_the_cache(mode, backend):
+    r = _run(mode, backend)
+    assert r["stored"] == RECORDS and r["loaded_first"] == 0
+    assert r["loaded_second"] == RECORDS and r["lookup_hits"] >= RECORDS
+    assert r["same_tokens"]
+    if backend == "FLASH_ATTN":
+        assert (r["block_stride"], r["head_bytes"]) == (0, 0)
+    else:                                   # FlashInfer, head-major on sm_100
+        assert r["block_stride"] == 2 * 16 * 256 and r["head_bytes"] == 128

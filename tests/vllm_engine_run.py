@@ -1,0 +1,70 @@
+"""One real vLLM engine run with the CrossCache connector, for
+tests/test_gpu_vllm_engine.py (run as a child process: vLLM sets up
+process-wide state).
+
+A small random-weight Llama (4 layers, hidden 512, 8 query heads, 2 KV heads
+of 64, bf16; load_format="dummy", no tokenizer) answers four prompts of
+1024-1135 token ids twice with greedy sampling and prefix caching off, so
+the second pass can only reuse KV through the connector.  Prints one JSON
+line: the registered paged geometry, the worker's stats after each pass and
+whether both passes produced the same tokens.
+
+argv: plain|layerwise  auto|FLASH_ATTN|FLASHINFER
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+import tempfile
+
+
+def main() -> None:
+    mode, backend = sys.argv[1], sys.argv[2]
+    os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")   # engine in this process
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from transformers import LlamaConfig
+
+    model_dir = tempfile.mkdtemp(prefix="crosscache-llama-")
+    LlamaConfig(vocab_size=32000, hidden_size=512, intermediate_size=1024, num_hidden_layers=4,
+                num_attention_heads=8, num_key_value_heads=2, head_dim=64, max_position_embeddings=4096,
+                torch_dtype="bfloat16").save_pretrained(model_dir)
+
+    from vllm import LLM, SamplingParams
+    from vllm.config import KVTransferConfig
+
+    extra = {"cache.pool_size": 1 << 30}
+    if mode == "layerwise":
+        extra["cache.layerwise"] = True
+    kw = {} if backend == "auto" else {"attention_config": {"backend": backend}}
+    llm = LLM(model=model_dir, load_format="dummy", skip_tokenizer_init=True, enforce_eager=True,
+              enable_prefix_caching=False, gpu_memory_utilization=0.2, max_model_len=2048, block_size=16,
+              dtype="bfloat16", disable_hybrid_kv_cache_manager=True, seed=0,
+              kv_transfer_config=KVTransferConfig(kv_connector="CrossCacheConnector",
+                                                  kv_connector_module_path="demo_b200.connector",
+                                                  kv_role="kv_both", kv_connector_extra_config=extra),
+              **kw)
+    prompts = [{"prompt_token_ids": [(7 * i + 13 * j) % 31000 + 100 for j in range(1024 + 37 * i)]}
+               for i in range(4)]
+    sp = SamplingParams(max_tokens=16, temperature=0, detokenize=False)
+    first = llm.generate(prompts, sp, use_tqdm=False)
+
+    from demo_b200 import connector
+
+    adapter = next(iter(connector._LOCAL_WORKERS.values()))
+    st1 = adapter.worker.stats()
+    second = llm.generate(prompts, sp, use_tqdm=False)
+    st2 = adapter.worker.stats()
+    lay = adapter.worker.layout
+    print("ENGINE_RESULT " + json.dumps({
+        "mode": mode, "backend": backend,
+        "block_stride": lay.block_stride, "head_bytes": lay.head_bytes,
+        "stored": st2["stored"], "loaded_first": st1["loaded"], "loaded_second": st2["loaded"],
+        "lookup_hits": st2["lookup_hits"],
+        "same_tokens": all(a.outputs[0].token_ids == b.outputs[0].token_ids for a, b in zip(first, second)),
+        "tokens": [list(o.outputs[0].token_ids) for o in second],
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()
