@@ -700,6 +700,86 @@ def _layerwise_probe(args, cc, layers, layout, kp, vp, hashes, bt_save, bt_load,
                     "contiguous records) into an HBM ring and a <= 32-CTA scatter, on a side stream"}
 
 
+def _paged_layout_probe(args, layers, b_save, b_load, s) -> dict:
+    """The value step's kernels on vLLM FlashInfer paged layouts: the same KV
+    re-laid per layer as [num_blocks][2][heads][block_size][head_dim] (HND,
+    what vLLM uses on sm_100) and [num_blocks][2][block_size][heads][head_dim]
+    (NHD), registered with block_stride = 2 * block_size * unit (and
+    head_bytes for HND).  Per geometry: one gather of every record at the
+    save table and one scatter at the load table per step, CUDA events on
+    the launch stream; the records must equal the dense layout's gather byte
+    for byte and the scatter must reproduce the saved blocks."""
+    import torch
+
+    from demo_b200._lib import KVCOPY_FLAG_BULK, KvCopyDesc, lib
+
+    dev, nrec, rec_bytes, bpc = s["dev"], s["nrec"], s["rec_bytes"], s["bpc"]
+    n_blocks, unit, n_layers = s["n_blocks"], s["unit"], len(layers)
+    hbm_peak, _ = peaks()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ref = torch.empty(nrec * rec_bytes, dtype=torch.uint8, device=dev)
+    out = torch.empty_like(ref)
+    ptrs = {id(ref): torch.arange(nrec, dtype=torch.int64, device=dev) * rec_bytes + ref.data_ptr(),
+            id(out): torch.arange(nrec, dtype=torch.int64, device=dev) * rec_bytes + out.data_ptr()}
+    stream = torch.cuda.Stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+
+    def desc(kp_d, vp_d, recs, bids, direction, stride=0, head_bytes=0):
+        return KvCopyDesc(layer_k=kp_d.data_ptr(), layer_v=vp_d.data_ptr(), records=ptrs[id(recs)].data_ptr(),
+                          slots=None, block_ids=bids.data_ptr(), error=err.data_ptr(),
+                          page_buffer_size=n_blocks * BS, unit_bytes=unit, num_tokens=CHUNK, block_size=BS,
+                          num_layers=n_layers, num_records=nrec, direction=direction, flags=KVCOPY_FLAG_BULK,
+                          block_stride=stride, head_bytes=head_bytes)
+
+    dense_k = torch.tensor([t[0].data_ptr() for t in layers], dtype=torch.int64, device=dev)
+    dense_v = torch.tensor([t[1].data_ptr() for t in layers], dtype=torch.int64, device=dev)
+    with torch.cuda.stream(stream):
+        assert lib.kv_copy_launch(C.byref(desc(dense_k, dense_v, ref, b_save, 1)), sptr) == 0
+    torch.cuda.synchronize()
+    res = {}
+    for name, hnd in (("flashinfer_hnd", True), ("flashinfer_nhd", False)):
+        fi = [(t.permute(1, 0, 3, 2, 4) if hnd else t.permute(1, 0, 2, 3, 4)).contiguous() for t in layers]
+        kp_d = torch.tensor([t.data_ptr() for t in fi], dtype=torch.int64, device=dev)
+        vp_d = kp_d + BS * unit
+        stride, hb = 2 * BS * unit, (HEAD_DIM * ELT if hnd else 0)
+        dg = desc(kp_d, vp_d, out, b_save, 1, stride, hb)
+        ds = desc(kp_d, vp_d, out, b_load, 0, stride, hb)
+        g_ms, s_ms = [], []
+        for it in range(args.warmup + args.steps):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record(stream)
+            assert lib.kv_copy_launch(C.byref(dg), sptr) == 0
+            ev[1].record(stream)
+            assert lib.kv_copy_launch(C.byref(ds), sptr) == 0
+            ev[2].record(stream)
+            torch.cuda.synchronize()
+            if it == 0:
+                same_records = bool(torch.equal(out, ref))
+            if it >= args.warmup:
+                g_ms.append(ev[0].elapsed_time(ev[1]))
+                s_ms.append(ev[1].elapsed_time(ev[2]))
+        assert int(err.item()) == 0, "kv copy reported an error"
+        # with overlapping tables the scatter may overwrite saved blocks: records only
+        same_blocks = not s["disjoint"] or all(torch.equal(t[b_save], t[b_load]) for t in fi)
+        moved = 2 * nrec * rec_bytes               # read + write bytes of one launch
+        gms, sms = statistics.median(g_ms), statistics.median(s_ms)
+        res[name] = {"gather_gbs": round(moved / (gms / 1e3) / GB, 1),
+                     "scatter_gbs": round(moved / (sms / 1e3) / GB, 1),
+                     "gather_frac": round(moved / (gms / 1e3) / GB / hbm_peak, 4),
+                     "scatter_frac": round(moved / (sms / 1e3) / GB / hbm_peak, 4),
+                     "gather_ms": round(gms, 4), "scatter_ms": round(sms, 4),
+                     "path": "register (head split folded into the address)" if hnd else
+                             "bulk (cp.async.bulk, strided blocks)",
+                     "verified_bytes": bool(same_records and same_blocks)}
+        del fi, kp_d, vp_d
+        torch.cuda.empty_cache()
+    del ref, out
+    torch.cuda.empty_cache()
+    res["note"] = ("frac of the measured HBM copy peak; same records, block tables and grid as the value step, "
+                   "per-layer tensors re-laid in the FlashInfer geometry; records equal the dense layout's")
+    return res
+
+
 def _serve_for_bench(q, stop, pool_bytes):
     import torch
 
@@ -1043,6 +1123,7 @@ def main() -> None:
     disk = None
     server = None
     layerwise = None
+    paged_layouts = None
     if not args.skip_e2e:
         # host-link peaks measured in this run: pinned 256 MiB cudaMemcpyAsync,
         # 16 per direction (4 GiB), every rank at once after a barrier -- the
@@ -1233,6 +1314,10 @@ def main() -> None:
                 "load_frac": round(payload / load_s / GB / link_peak["h2d"], 4),
                 "note": "per GPU; pinned cudaMemcpyAsync, 4 GiB per direction, all ranks at once, this run"}
 
+    if world == 1:
+        paged_layouts = _paged_layout_probe(args, layers, b_save, b_load,
+                                            dict(dev=dev, nrec=nrec, rec_bytes=rec_bytes, bpc=bpc,
+                                                 n_blocks=n_blocks, unit=unit, disjoint=disjoint))
     clocks.__exit__(None, None, None)
     cpu = None
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
@@ -1266,6 +1351,7 @@ def main() -> None:
                          "scatter_frac": round(2 * payload / (scatter_ms / 1e3) / GB / hbm_peak, 4)},
             "e2e": e2e, "link": link, "p50_load_latency_ms": round(p50, 3) if p50 is not None else None,
             "block_hash": hash_info, "disk_tier": disk, "via_server": server, "layerwise": layerwise,
+            "paged_layouts": paged_layouts,
             "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": clocks.summary(),
             "verified_bytes": bool(ok_value),
         }

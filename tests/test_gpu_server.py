@@ -31,7 +31,26 @@ def _serve(q, stop):
     srv.stop()
 
 
-def test_remote_adapters_store_lookup_load():
+def _kv_layers(layout: str, g):
+    """per-layer vLLM KV tensors: FlashAttention [2, NB, BS, H, D], or the
+    FlashInfer view [NB, 2, BS, H, D] of head-major blocks (sm_100)"""
+    import torch
+
+    if layout == "flash_attn":
+        return {f"layer.{i}": torch.randn(2, NB, BS, H, D, generator=g, device="cuda").to(torch.bfloat16)
+                for i in range(L)}
+    return {f"layer.{i}": torch.randn(NB, 2, H, BS, D, generator=g, device="cuda").to(torch.bfloat16)
+            .permute(0, 1, 3, 2, 4) for i in range(L)}
+
+
+def _blocks(t, layout: str, sl: slice):
+    return t[:, sl] if layout == "flash_attn" else t[sl]
+
+
+@pytest.mark.parametrize("layout", ["flash_attn", "flashinfer_hnd"])
+def test_remote_adapters_store_lookup_load(layout):
+    """FlashInfer: the REGISTER carries IPC keys of the K and V plane bases
+    (V half a block into each layer) and the paged-geometry trailer"""
     import torch
 
     from demo_b200.adaptor import LoadStoreOp
@@ -47,8 +66,7 @@ def test_remote_adapters_store_lookup_load():
         assert status == "ok", endpoint
         torch.cuda.set_device(0)
         g = torch.Generator(device="cuda").manual_seed(3)
-        layers = {f"layer.{i}": torch.randn(2, NB, BS, H, D, generator=g, device="cuda").to(torch.bfloat16)
-                  for i in range(L)}
+        layers = _kv_layers(layout, g)
         orig = {k: t.clone() for k, t in layers.items()}
         zctx = zmq.Context.instance()
         wa = RemoteWorkerAdapter(endpoint, zctx, "remote-model", 1, 0, BS, device=0)
@@ -65,7 +83,7 @@ def test_remote_adapters_store_lookup_load():
         assert hit == 512
 
         for t in layers.values():
-            t[:, 64:96].zero_()
+            _blocks(t, layout, slice(64, 96)).zero_()
         torch.cuda.synchronize()
         wa.load_requests(["r2"], [LoadStoreOp(hashes, list(range(64, 96)))])
         assert wa.wait_all(timeout=120) == [0, 0]
@@ -73,8 +91,10 @@ def test_remote_adapters_store_lookup_load():
         assert loads == {"r2"}
         torch.cuda.synchronize()
         for k, t in layers.items():
-            assert torch.equal(t[:, 64:96].view(torch.int16), orig[k][:, :32].view(torch.int16)), k
-            assert torch.equal(t[:, :64].view(torch.int16), orig[k][:, :64].view(torch.int16)), k
+            assert torch.equal(_blocks(t, layout, slice(64, 96)).view(torch.int16),
+                               _blocks(orig[k], layout, slice(0, 32)).view(torch.int16)), k
+            assert torch.equal(_blocks(t, layout, slice(0, 64)).view(torch.int16),
+                               _blocks(orig[k], layout, slice(0, 64)).view(torch.int16)), k
     finally:
         if sa is not None:
             sa.close()

@@ -9,7 +9,7 @@ the second pass can only reuse KV through the connector.  Prints one JSON
 line: the registered paged geometry, the worker's stats after each pass and
 whether both passes produced the same tokens.
 
-argv: plain|layerwise  auto|FLASH_ATTN|FLASHINFER
+argv: plain|layerwise  auto|FLASH_ATTN|FLASHINFER  [auto|fp8 (kv_cache_dtype)]
 """
 from __future__ import annotations
 
@@ -21,6 +21,7 @@ import tempfile
 
 def main() -> None:
     mode, backend = sys.argv[1], sys.argv[2]
+    kv_dtype = sys.argv[3] if len(sys.argv) > 3 else "auto"
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")   # engine in this process
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from transformers import LlamaConfig
@@ -39,7 +40,7 @@ def main() -> None:
     kw = {} if backend == "auto" else {"attention_config": {"backend": backend}}
     llm = LLM(model=model_dir, load_format="dummy", skip_tokenizer_init=True, enforce_eager=True,
               enable_prefix_caching=False, gpu_memory_utilization=0.2, max_model_len=2048, block_size=16,
-              dtype="bfloat16", disable_hybrid_kv_cache_manager=True, seed=0,
+              dtype="bfloat16", disable_hybrid_kv_cache_manager=True, seed=0, kv_cache_dtype=kv_dtype,
               kv_transfer_config=KVTransferConfig(kv_connector="CrossCacheConnector",
                                                   kv_connector_module_path="demo_b200.connector",
                                                   kv_role="kv_both", kv_connector_extra_config=extra),
@@ -57,7 +58,7 @@ def main() -> None:
     st2 = adapter.worker.stats()
     lay = adapter.worker.layout
     print("ENGINE_RESULT " + json.dumps({
-        "mode": mode, "backend": backend,
+        "mode": mode, "backend": backend, "kv_cache_dtype": kv_dtype, "element_size": lay.element_size,
         "block_stride": lay.block_stride, "head_bytes": lay.head_bytes,
         "stored": st2["stored"], "loaded_first": st1["loaded"], "loaded_second": st2["loaded"],
         "lookup_hits": st2["lookup_hits"],
