@@ -768,8 +768,9 @@ def _paged_layout_probe(args, layers, b_save, b_load, s) -> dict:
                      "gather_frac": round(moved / (gms / 1e3) / GB / hbm_peak, 4),
                      "scatter_frac": round(moved / (sms / 1e3) / GB / hbm_peak, 4),
                      "gather_ms": round(gms, 4), "scatter_ms": round(sms, 4),
-                     "path": "register (head split folded into the address)" if hnd else
-                             "bulk (cp.async.bulk, strided blocks)",
+                     "path": ("register (head split folded into the address)" if kvcopy_path() == "lsu" else
+                              "bulk, blocks transposed in shared memory (kv_copy_bulk_hnd_kernel)") if hnd else
+                             ("register" if kvcopy_path() == "lsu" else "bulk (cp.async.bulk, strided blocks)"),
                      "verified_bytes": bool(same_records and same_blocks)}
         del fi, kp_d, vp_d
         torch.cuda.empty_cache()

@@ -23,9 +23,10 @@
  *
  * The paged side may also be strided or head-major (kv_copy_desc
  * block_stride / head_bytes: vLLM FlashInfer's [blocks][2][heads][bs][dim]
- * on sm_100); the record side is token-major in every case.  Head-major
- * blocks take the register path with the head split folded into the paged
- * address; dense and strided token-major blocks may take the bulk path.
+ * on sm_100); the record side is token-major in every case.  On the bulk
+ * path head-major blocks are transposed in shared memory between the bulk
+ * load and the bulk store (kv_copy_bulk_hnd_kernel); on the register path
+ * the head split is folded into the paged address.
  */
 #include "kvcopy.h"
 #include "adaptor.h"
@@ -346,6 +347,10 @@ struct BulkParams {
     uint32_t rec_layers;        /* layers a record holds */
     uint32_t max_grid;          /* CTA cap, 0 = none */
     FastDiv div_tpl, div_layers, div_kv;
+    /* head-major blocks, in 16-byte vectors: hv per head piece of a token,
+     * tv = block_size * hv per head, vpb = heads * tv per block */
+    uint32_t heads, hv, tv, vpb, bs;
+    FastDiv div_hv, div_tv, div_vpb, div_bs;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p)
@@ -432,6 +437,60 @@ __device__ __forceinline__ BulkTile bulk_decode(const BulkParams &p, uint32_t w)
     return t;
 }
 
+/* start the loads of tile t into `stage`, completion counted in bytes on
+ * `bar`; a tile whose base is null or misaligned loads nothing and flags it */
+template <bool TO_RECORD>
+__device__ void bulk_issue_load(const BulkParams &p, const BulkTile &t, uint8_t *stage, uint64_t *bar)
+{
+    const uint32_t run = (uint32_t)p.run_bytes;
+    bool bad_base = !t.layer || ((reinterpret_cast<uintptr_t>(t.layer) | reinterpret_cast<uintptr_t>(t.rec)) & 15);
+    if (bad_base) {
+        if (p.error)
+            atomicOr(p.error, t.layer ? KVCOPY_ERR_ALIGN : KVCOPY_ERR_NULL_LAYER);
+        mbar_expect_tx(bar, 0);
+        return;
+    }
+    if (TO_RECORD) {
+        uint32_t bytes = 0;
+        for (uint32_t j = 0; j < t.nb; j++)
+            if (t.bids[j] < p.num_blocks)
+                bytes += run;
+        mbar_expect_tx(bar, bytes);
+        for (uint32_t j = 0; j < t.nb; j++) {
+            uint64_t bid = t.bids[j];
+            if (bid < p.num_blocks)
+                bulk_g2s(stage + j * run, t.layer + bid * p.block_stride, run, bar);
+            else if (p.error)
+                atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
+        }
+    } else {
+        mbar_expect_tx(bar, t.nb * run);
+        bulk_g2s(stage, t.rec, t.nb * run, bar);
+    }
+}
+
+/* store tile t from shared memory at `src` (one bulk group) */
+template <bool TO_RECORD>
+__device__ void bulk_issue_store(const BulkParams &p, const BulkTile &t, const uint8_t *src)
+{
+    const uint32_t run = (uint32_t)p.run_bytes;
+    bool bad_base = !t.layer || ((reinterpret_cast<uintptr_t>(t.layer) | reinterpret_cast<uintptr_t>(t.rec)) & 15);
+    if (!bad_base) {
+        if (TO_RECORD) {
+            bulk_s2g(t.rec, src, t.nb * run);
+        } else {
+            for (uint32_t j = 0; j < t.nb; j++) {
+                uint64_t bid = t.bids[j];
+                if (bid < p.num_blocks)
+                    bulk_s2g(t.layer + bid * p.block_stride, src + j * run, run);
+                else if (p.error)
+                    atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
+            }
+        }
+    }
+    bulk_commit();
+}
+
 template <bool TO_RECORD>
 __global__ void __launch_bounds__(32, 1) kv_copy_bulk_kernel(const BulkParams p)
 {
@@ -444,56 +503,14 @@ __global__ void __launch_bounds__(32, 1) kv_copy_bulk_kernel(const BulkParams p)
     mbar_fence_init();
 
     const uint32_t n_my = p.num_tiles > blockIdx.x ? (p.num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-    const uint32_t run = (uint32_t)p.run_bytes;
 
-    /* start the loads of my k-th tile into stage s; false when a base is unusable */
     auto issue_load = [&](uint32_t k, int s) {
-        BulkTile t = bulk_decode(p, blockIdx.x + k * gridDim.x);
-        uint8_t *stage = bulk_smem + (uint32_t)s * kBulkTileBytes;
-        bool bad_base = !t.layer || ((reinterpret_cast<uintptr_t>(t.layer) | reinterpret_cast<uintptr_t>(t.rec)) & 15);
-        if (bad_base) {
-            if (p.error)
-                atomicOr(p.error, t.layer ? KVCOPY_ERR_ALIGN : KVCOPY_ERR_NULL_LAYER);
-            mbar_expect_tx(&bars[s], 0);
-            return;
-        }
-        if (TO_RECORD) {
-            uint32_t bytes = 0;
-            for (uint32_t j = 0; j < t.nb; j++)
-                if (t.bids[j] < p.num_blocks)
-                    bytes += run;
-            mbar_expect_tx(&bars[s], bytes);
-            for (uint32_t j = 0; j < t.nb; j++) {
-                uint64_t bid = t.bids[j];
-                if (bid < p.num_blocks)
-                    bulk_g2s(stage + j * run, t.layer + bid * p.block_stride, run, &bars[s]);
-                else if (p.error)
-                    atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
-            }
-        } else {
-            mbar_expect_tx(&bars[s], t.nb * run);
-            bulk_g2s(stage, t.rec, t.nb * run, &bars[s]);
-        }
+        bulk_issue_load<TO_RECORD>(p, bulk_decode(p, blockIdx.x + k * gridDim.x),
+                                   bulk_smem + (uint32_t)s * kBulkTileBytes, &bars[s]);
     };
-    /* store my k-th tile from stage s (one bulk group) */
     auto issue_store = [&](uint32_t k, int s) {
-        BulkTile t = bulk_decode(p, blockIdx.x + k * gridDim.x);
-        uint8_t *stage = bulk_smem + (uint32_t)s * kBulkTileBytes;
-        bool bad_base = !t.layer || ((reinterpret_cast<uintptr_t>(t.layer) | reinterpret_cast<uintptr_t>(t.rec)) & 15);
-        if (!bad_base) {
-            if (TO_RECORD) {
-                bulk_s2g(t.rec, stage, t.nb * run);
-            } else {
-                for (uint32_t j = 0; j < t.nb; j++) {
-                    uint64_t bid = t.bids[j];
-                    if (bid < p.num_blocks)
-                        bulk_s2g(t.layer + bid * p.block_stride, stage + j * run, run);
-                    else if (p.error)
-                        atomicOr(p.error, KVCOPY_ERR_SLOT_RANGE);
-                }
-            }
-        }
-        bulk_commit();
+        bulk_issue_store<TO_RECORD>(p, bulk_decode(p, blockIdx.x + k * gridDim.x),
+                                    bulk_smem + (uint32_t)s * kBulkTileBytes);
     };
 
     uint32_t issued = 0;
@@ -551,6 +568,165 @@ int launch_bulk(const BulkParams &bp, bool to_record, cudaStream_t stream)
     return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
 }
 
+/* ------------------------------------------------------------------------
+ * TMA bulk path for head-major blocks (vLLM FlashInfer HND on sm_100).
+ *
+ * A paged block is one contiguous run of [heads][block_size][head_bytes];
+ * the record wants the same bytes token-major, [block_size][heads]
+ * [head_bytes].  Tiles, loads and stores are those of the bulk path; in
+ * between, the CTA's 16 warps transpose each block of the stage into one
+ * of two shared buffers (16-byte vectors: head pieces of a token stay whole),
+ * and the bulk store reads that buffer.  When a token's vectors divide the
+ * CTA, each thread keeps one (head, vector) position for the whole kernel
+ * and walks tokens, so a vector costs one division and a few adds.  Thread 0 drives the copies and the
+ * bounded mbarrier waits; two CTA barriers per tile hand the stage and the
+ * buffer between the copies and the warps:
+ *   - before a buffer is rewritten, the store that last read it has read it
+ *     (cp.async.bulk.wait_group.read with one group left: the previous tile's)
+ *   - after the transpose, fence.proxy.async makes the warps' shared-memory
+ *     writes visible to the bulk store and orders their stage reads before
+ *     the refill of that stage.
+ * ---------------------------------------------------------------------- */
+constexpr int kHndThreads = 512;
+constexpr int kHndStages = 4;
+static_assert((uint64_t)(kHndStages + 2) * kBulkTileBytes <= 227u * 1024u - 256u,
+              "head-major bulk stages and transpose buffers must fit in shared memory");
+
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+/* vector w of a block in head-major order -> its index in token-major order */
+__device__ __forceinline__ uint32_t hnd_to_token_major(const BulkParams &p, uint32_t w)
+{
+    uint32_t h = fdiv(w, p.div_tv);
+    uint32_t r = w - h * p.tv;
+    uint32_t t = fdiv(r, p.div_hv);
+    uint32_t x = r - t * p.hv;
+    return (t * p.heads + h) * p.hv + x;
+}
+
+template <bool TO_RECORD>
+__global__ void __launch_bounds__(kHndThreads, 1) kv_copy_bulk_hnd_kernel(const BulkParams p)
+{
+    extern __shared__ __align__(128) uint8_t bulk_smem[];
+    __shared__ __align__(8) uint64_t bars[kHndStages];
+    __shared__ int go;
+    uint8_t *const tbuf = bulk_smem + (uint32_t)kHndStages * kBulkTileBytes;
+    const bool leader = threadIdx.x == 0;
+    const uint32_t n_my = p.num_tiles > blockIdx.x ? (p.num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    /* this thread's fixed position inside a token: vector pos of P, head h */
+    const uint32_t P = p.heads * p.hv;
+    const bool fixed_pos = kHndThreads % P == 0;
+    const uint32_t pos = threadIdx.x % P, row0 = threadIdx.x / P, drow = kHndThreads / P;
+    const uint32_t h0 = fdiv(pos, p.div_hv);
+    const uint32_t hm0 = h0 * p.tv + (pos - h0 * p.hv);
+
+    uint32_t issued = 0;
+    if (leader) {
+        for (int s = 0; s < kHndStages; s++)
+            mbar_init(&bars[s], 1);
+        mbar_fence_init();
+        for (; issued < n_my && issued < (uint32_t)kHndStages; issued++)
+            bulk_issue_load<TO_RECORD>(p, bulk_decode(p, blockIdx.x + issued * gridDim.x),
+                                       bulk_smem + issued * kBulkTileBytes, &bars[issued]);
+    }
+    for (uint32_t k = 0; k < n_my; k++) {
+        const uint32_t s = k % kHndStages;
+        uint8_t *const stage = bulk_smem + s * kBulkTileBytes;
+        uint8_t *const buf = tbuf + (k & 1) * kBulkTileBytes;
+        if (leader) {
+            bool ok = mbar_wait_bounded(&bars[s], (k / kHndStages) & 1);
+            if (!ok) {
+                if (p.error)
+                    atomicOr(p.error, KVCOPY_ERR_TIMEOUT);
+                for (uint32_t j = k + 1; j < issued; j++)   /* loads still in flight */
+                    mbar_wait_bounded(&bars[j % kHndStages], (j / kHndStages) & 1);
+            }
+            if (k >= 2)
+                bulk_wait_read1();      /* tile k-2's store has read buf */
+            go = ok;
+        }
+        __syncthreads();
+        if (!go)
+            break;
+        const BulkTile t = bulk_decode(p, blockIdx.x + k * gridDim.x);
+        const uint4 *src = reinterpret_cast<const uint4 *>(stage);
+        uint4 *dst = reinterpret_cast<uint4 *>(buf);
+        if (fixed_pos) {
+            /* token-major vector row * P + pos <-> head-major jb * vpb + hm0 + t * hv */
+            const uint32_t rows = t.nb * p.bs;
+#pragma unroll 4
+            for (uint32_t row = row0; row < rows; row += drow) {
+                uint32_t jb = fdiv(row, p.div_bs);
+                uint32_t hm = jb * p.vpb + hm0 + (row - jb * p.bs) * p.hv;
+                uint32_t tm = row * P + pos;
+                if (TO_RECORD)
+                    dst[tm] = src[hm];  /* head-major block -> token-major record */
+                else
+                    dst[hm] = src[tm];  /* token-major record -> head-major block */
+            }
+        } else {
+            const uint32_t nvec = t.nb * p.vpb;
+            for (uint32_t v = threadIdx.x; v < nvec; v += kHndThreads) {
+                uint32_t jb = fdiv(v, p.div_vpb);
+                uint32_t w = v - jb * p.vpb;
+                uint32_t tm = jb * p.vpb + hnd_to_token_major(p, w);
+                if (TO_RECORD)
+                    dst[tm] = src[v];
+                else
+                    dst[v] = src[tm];
+            }
+        }
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (leader) {
+            bulk_issue_store<TO_RECORD>(p, t, buf);
+            if (issued < n_my) {        /* the stage of tile k is free: refill it */
+                bulk_issue_load<TO_RECORD>(p, bulk_decode(p, blockIdx.x + issued * gridDim.x), stage, &bars[s]);
+                issued++;
+            }
+        }
+    }
+    if (leader)
+        bulk_wait_all();
+}
+
+int launch_bulk_hnd(const BulkParams &bp, bool to_record, cudaStream_t stream)
+{
+    static int sm_count[64];
+    static std::once_flag once[64];
+    static cudaError_t attr_err[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return -EIO;
+    const int smem = (kHndStages + 2) * (int)kBulkTileBytes;
+    std::call_once(once[dev], [&] {
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        sm_count[dev] = sms > 0 ? sms : 1;
+        attr_err[dev] = cudaFuncSetAttribute(kv_copy_bulk_hnd_kernel<true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (attr_err[dev] == cudaSuccess)
+            attr_err[dev] = cudaFuncSetAttribute(kv_copy_bulk_hnd_kernel<false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
+    if (attr_err[dev] != cudaSuccess)
+        return -EIO;
+    uint32_t grid = (uint32_t)sm_count[dev];
+    if (bp.max_grid && grid > bp.max_grid)
+        grid = bp.max_grid;
+    if (grid > bp.num_tiles)
+        grid = bp.num_tiles;
+    if (to_record)
+        kv_copy_bulk_hnd_kernel<true><<<grid, kHndThreads, smem, stream>>>(bp);
+    else
+        kv_copy_bulk_hnd_kernel<false><<<grid, kHndThreads, smem, stream>>>(bp);
+    g_cc_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -EIO;
+}
+
 /* CROSSCACHE_KVCOPY=lsu forces the register path even when the bulk path is allowed */
 bool bulk_allowed_by_env()
 {
@@ -595,7 +771,7 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
         return -EINVAL;
     if (!dense && d->slots && d->page_buffer_size >= (1ull << 32))
         return -EINVAL;
-    if ((d->flags & KVCOPY_FLAG_BULK) && !d->slots && !d->head_bytes && d->unit_bytes % 16 == 0 &&
+    if ((d->flags & KVCOPY_FLAG_BULK) && !d->slots && d->head_bytes % 16 == 0 && d->unit_bytes % 16 == 0 &&
         block_stride % 16 == 0 && run_bytes >= kBulkMinRunBytes && run_bytes <= kBulkTileBytes &&
         d->page_buffer_size % d->block_size == 0 && bulk_allowed_by_env()) {
         BulkParams bp{};
@@ -625,6 +801,18 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
         bp.div_tpl = make_fastdiv(tpl);
         bp.div_layers = make_fastdiv(bp.num_layers);
         bp.div_kv = make_fastdiv(bp.num_kv);
+        if (d->head_bytes) {
+            bp.hv = d->head_bytes / 16;
+            bp.heads = d->unit_bytes / d->head_bytes;
+            bp.tv = d->block_size * bp.hv;
+            bp.vpb = (uint32_t)(run_bytes / 16);
+            bp.div_hv = make_fastdiv(bp.hv);
+            bp.div_tv = make_fastdiv(bp.tv);
+            bp.div_vpb = make_fastdiv(bp.vpb);
+            bp.bs = d->block_size;
+            bp.div_bs = make_fastdiv(d->block_size);
+            return launch_bulk_hnd(bp, d->direction != 0, static_cast<cudaStream_t>(stream));
+        }
         return launch_bulk(bp, d->direction != 0, static_cast<cudaStream_t>(stream));
     }
 

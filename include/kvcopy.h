@@ -43,7 +43,9 @@ extern "C" {
                                        * whose block run (block_size * unit) is a
                                        * multiple of 16 bytes from 8 to 32 KiB
                                        * then use TMA bulk copies
-                                       * (cp.async.bulk) staged in shared memory */
+                                       * (cp.async.bulk) staged in shared memory
+                                       * (head-major blocks with head_bytes a
+                                       * multiple of 16: transposed there too) */
 
 struct kv_copy_desc {
     const uint64_t *layer_k;     /* [num_layers] K layer base addresses      */
