@@ -2,14 +2,17 @@
 tests/test_gpu_vllm_engine.py (run as a child process: vLLM sets up
 process-wide state).
 
-A small random-weight Llama (4 layers, hidden 512, 8 query heads, 2 KV heads
-of 64, bf16; load_format="dummy", no tokenizer) answers four prompts of
-1024-1135 token ids twice with greedy sampling and prefix caching off, so
-the second pass can only reuse KV through the connector.  Prints one JSON
-line: the registered paged geometry, the worker's stats after each pass and
-whether both passes produced the same tokens.
+A small random-weight model (load_format="dummy", no tokenizer, bf16)
+answers four prompts of 1024-1135 token ids twice with greedy sampling and
+prefix caching off, so the second pass can only reuse KV through the
+connector:
+  llama  4 layers, hidden 512, 8 query heads, 2 KV heads of 64, block 16
+  mla    DeepSeek-V2 attention, 4 dense layers, hidden 512, 8 heads,
+         kv_lora_rank 512 + rope 64 (a 576-wide K-only latent cache), block 64
+Prints one JSON line: the registered paged geometry, the worker's stats
+after each pass and whether both passes produced the same tokens.
 
-argv: plain|layerwise  auto|FLASH_ATTN|FLASHINFER  [auto|fp8 (kv_cache_dtype)]
+argv: plain|layerwise  auto|<attention backend>  [auto|fp8 (kv_cache_dtype)]  [llama|mla]
 """
 from __future__ import annotations
 
@@ -22,14 +25,27 @@ import tempfile
 def main() -> None:
     mode, backend = sys.argv[1], sys.argv[2]
     kv_dtype = sys.argv[3] if len(sys.argv) > 3 else "auto"
+    model = sys.argv[4] if len(sys.argv) > 4 else "llama"
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")   # engine in this process
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
-    from transformers import LlamaConfig
 
-    model_dir = tempfile.mkdtemp(prefix="crosscache-llama-")
-    LlamaConfig(vocab_size=32000, hidden_size=512, intermediate_size=1024, num_hidden_layers=4,
-                num_attention_heads=8, num_key_value_heads=2, head_dim=64, max_position_embeddings=4096,
-                torch_dtype="bfloat16").save_pretrained(model_dir)
+    model_dir = tempfile.mkdtemp(prefix=f"crosscache-{model}-")
+    if model == "mla":
+        from transformers import DeepseekV2Config
+
+        DeepseekV2Config(vocab_size=32000, hidden_size=512, intermediate_size=1024, moe_intermediate_size=256,
+                         num_hidden_layers=4, num_attention_heads=8, n_shared_experts=1, n_routed_experts=8,
+                         num_experts_per_tok=2, first_k_dense_replace=4, kv_lora_rank=512, q_lora_rank=None,
+                         qk_rope_head_dim=64, v_head_dim=128, qk_nope_head_dim=128, max_position_embeddings=4096,
+                         architectures=["DeepseekV2ForCausalLM"], torch_dtype="bfloat16").save_pretrained(model_dir)
+        block_size = 64
+    else:
+        from transformers import LlamaConfig
+
+        LlamaConfig(vocab_size=32000, hidden_size=512, intermediate_size=1024, num_hidden_layers=4,
+                    num_attention_heads=8, num_key_value_heads=2, head_dim=64, max_position_embeddings=4096,
+                    architectures=["LlamaForCausalLM"], torch_dtype="bfloat16").save_pretrained(model_dir)
+        block_size = 16
 
     from vllm import LLM, SamplingParams
     from vllm.config import KVTransferConfig
@@ -39,7 +55,7 @@ def main() -> None:
         extra["cache.layerwise"] = True
     kw = {} if backend == "auto" else {"attention_config": {"backend": backend}}
     llm = LLM(model=model_dir, load_format="dummy", skip_tokenizer_init=True, enforce_eager=True,
-              enable_prefix_caching=False, gpu_memory_utilization=0.2, max_model_len=2048, block_size=16,
+              enable_prefix_caching=False, gpu_memory_utilization=0.2, max_model_len=2048, block_size=block_size,
               dtype="bfloat16", disable_hybrid_kv_cache_manager=True, seed=0, kv_cache_dtype=kv_dtype,
               kv_transfer_config=KVTransferConfig(kv_connector="CrossCacheConnector",
                                                   kv_connector_module_path="demo_b200.connector",
@@ -58,7 +74,9 @@ def main() -> None:
     st2 = adapter.worker.stats()
     lay = adapter.worker.layout
     print("ENGINE_RESULT " + json.dumps({
-        "mode": mode, "backend": backend, "kv_cache_dtype": kv_dtype, "element_size": lay.element_size,
+        "mode": mode, "backend": backend, "kv_cache_dtype": kv_dtype, "model": model,
+        "element_size": lay.element_size, "kv": lay.kv, "block_size": lay.block_size,
+        "hidden_dim_size": lay.hidden_dim_size,
         "block_stride": lay.block_stride, "head_bytes": lay.head_bytes,
         "stored": st2["stored"], "loaded_first": st1["loaded"], "loaded_second": st2["loaded"],
         "lookup_hits": st2["lookup_hits"],
