@@ -183,7 +183,8 @@ class CrossCacheConnector(KVConnectorBase_V1):
 
             from .remote import RemoteSchedulerAdapter, RemoteWorkerAdapter
             port = vllm_config.kv_transfer_config.get_from_extra_config("cache.server.port", 5555)
-            url, ctx = f"{host}:{port}", zmq.Context.instance()
+            # the reference's host carries the scheme ("tcp://localhost"); a bare host means TCP
+            url, ctx = f"{host if '://' in host else 'tcp://' + host}:{port}", zmq.Context.instance()
         if role == KVConnectorRole.SCHEDULER:
             if self._remote:
                 self.scheduler_adapter = RemoteSchedulerAdapter(url, ctx, model, world_size, rank,

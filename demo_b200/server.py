@@ -27,6 +27,7 @@ from __future__ import annotations
 import argparse
 import ctypes as C
 import errno
+import json
 import logging
 import os
 import queue
@@ -107,6 +108,7 @@ class CacheServer:
         with self._slot_lock:
             for i, w in enumerate(self._slots):
                 if w is not None:
+                    _log_worker_stats(i, w, "server stopped")
                     w.unregister()
                     self._slots[i] = None
         self._sock.close()
@@ -223,6 +225,7 @@ class CacheServer:
         if w is None:
             logger.warning("worker:%u has not registered", nid)
             return 0
+        _log_worker_stats(nid, w, "unregistered")
         w.unregister()
         return 0
 
@@ -251,6 +254,17 @@ class CacheServer:
         bids = np.ascontiguousarray(m.block_ids, dtype=np.uint64)
         fn = lib.cache_store if m.op == P.Op.STORE else lib.cache_load
         return fn(C.byref(w.ctx), m.keys, m.key_len, bids.ctypes.data, len(bids))
+
+
+def _log_worker_stats(nid: int, w: cc.Worker, why: str) -> None:
+    """one INFO line per departing worker: its entry's counters as JSON"""
+    try:
+        st = w.stats()
+    except cc.CacheError:
+        return
+    ctx = w.ctx
+    logger.info("worker:%u %s: model=%s tp=%u rank=%u stats=%s", nid, why, ctx.model.model_name.decode(),
+                ctx.world_size, ctx.rank_id, json.dumps(st, sort_keys=True))
 
 
 def main(argv: list[str] | None = None) -> None:

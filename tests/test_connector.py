@@ -158,6 +158,7 @@ def test_remote_scheduler_asks_the_server():
                            timeout=30) == 0
         cfg = _cfg()
         host, port = srv.endpoint.rsplit(":", 1)
+        host = host.split("://", 1)[1]       # a bare host: the connector adds tcp://
         cfg.kv_transfer_config.kv_connector_extra_config.update({"cache.server.host": host,
                                                                  "cache.server.port": int(port)})
         conn = CrossCacheConnector(cfg, vllm_base.KVConnectorRole.SCHEDULER)

@@ -8,6 +8,7 @@ socket on the CPU (MEM) backend, with the record bytes checked against the
 oracle and the reference's error answers."""
 import errno
 import json
+import logging
 import struct
 from pathlib import Path
 
@@ -126,7 +127,8 @@ def _register(cli, kv: HostKV, node=0, world=1, rank=0, name="m"):
                        timeout=30)
 
 
-def test_server_store_lookup_load_roundtrip(server):
+def test_server_store_lookup_load_roundtrip(server, caplog):
+    caplog.set_level(logging.INFO, logger="demo_b200.server")
     srv, cli = server
     src, dst = HostKV(CASE), HostKV(CASE, zero=True)
     assert _register(cli, src, node=0) == 0
@@ -146,6 +148,11 @@ def test_server_store_lookup_load_roundtrip(server):
     assert all(np.array_equal(a, b) for a, b in zip(dst.v, ev))
     assert cli.request(lambda u: P.encode_unregister(1, u), timeout=30) == 0
     assert cli.request(lambda u: P.encode_unregister(0, u), timeout=30) == 0
+    # a departing worker's counters are logged (both slots share one entry)
+    left = [r.getMessage() for r in caplog.records if "unregistered" in r.getMessage()]
+    assert len(left) == 2 and all("model=m tp=1 rank=0" in m for m in left)
+    st = json.loads(left[-1].split("stats=", 1)[1])
+    assert st["stored"] == CASE["chunks"] and st["loaded"] == CASE["chunks"]
 
 
 def test_server_error_answers(server):

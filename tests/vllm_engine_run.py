@@ -12,10 +12,13 @@ connector:
 Prints one JSON line: the registered paged geometry, the worker's stats
 after each pass and whether both passes produced the same tokens.
 
-argv: plain|layerwise  auto|<attention backend>  [auto|fp8 (kv_cache_dtype)]  [llama|mla]
+With --server-port the connector talks to a CrossCache server (one process
+for all TP ranks, CUDA IPC registration); the counters then live in the
+server, which logs them per worker when the worker leaves.
 """
 from __future__ import annotations
 
+import argparse
 import json
 import os
 import sys
@@ -23,9 +26,15 @@ import tempfile
 
 
 def main() -> None:
-    mode, backend = sys.argv[1], sys.argv[2]
-    kv_dtype = sys.argv[3] if len(sys.argv) > 3 else "auto"
-    model = sys.argv[4] if len(sys.argv) > 4 else "llama"
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--mode", choices=["plain", "layerwise"], default="plain")
+    ap.add_argument("--backend", default="auto", help="vLLM attention backend, or auto")
+    ap.add_argument("--kv-dtype", default="auto", help="kv_cache_dtype (auto or fp8)")
+    ap.add_argument("--model", choices=["llama", "mla"], default="llama")
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--server-port", type=int, default=0, help="CrossCache server on 127.0.0.1 (0: in-process)")
+    a = ap.parse_args()
+    mode, backend, kv_dtype, model = a.mode, a.backend, a.kv_dtype, a.model
     os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")   # engine in this process
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
@@ -53,10 +62,13 @@ def main() -> None:
     extra = {"cache.pool_size": 1 << 30}
     if mode == "layerwise":
         extra["cache.layerwise"] = True
+    if a.server_port:
+        extra.update({"cache.server.host": "tcp://127.0.0.1", "cache.server.port": a.server_port})
     kw = {} if backend == "auto" else {"attention_config": {"backend": backend}}
     llm = LLM(model=model_dir, load_format="dummy", skip_tokenizer_init=True, enforce_eager=True,
               enable_prefix_caching=False, gpu_memory_utilization=0.2, max_model_len=2048, block_size=block_size,
               dtype="bfloat16", disable_hybrid_kv_cache_manager=True, seed=0, kv_cache_dtype=kv_dtype,
+              tensor_parallel_size=a.tp,
               kv_transfer_config=KVTransferConfig(kv_connector="CrossCacheConnector",
                                                   kv_connector_module_path="demo_b200.connector",
                                                   kv_role="kv_both", kv_connector_extra_config=extra),
@@ -65,6 +77,14 @@ def main() -> None:
                for i in range(4)]
     sp = SamplingParams(max_tokens=16, temperature=0, detokenize=False)
     first = llm.generate(prompts, sp, use_tqdm=False)
+    if a.server_port:
+        second = llm.generate(prompts, sp, use_tqdm=False)
+        print("ENGINE_RESULT " + json.dumps({
+            "mode": mode, "backend": backend, "model": model, "tp": a.tp, "server": True,
+            "same_tokens": all(x.outputs[0].token_ids == y.outputs[0].token_ids for x, y in zip(first, second)),
+            "tokens": [list(o.outputs[0].token_ids) for o in second],
+        }), flush=True)
+        return
 
     from demo_b200 import connector
 
