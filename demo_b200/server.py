@@ -33,6 +33,7 @@ import os
 import queue
 import signal
 import threading
+import time
 from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
@@ -181,6 +182,7 @@ class CacheServer:
             self._reply(ident, msg.uid, -errno.ESHUTDOWN)
 
     def _handle(self, ident: bytes, msg) -> None:
+        t0 = time.perf_counter()
         try:
             if isinstance(msg, P.Register):
                 ret = self._register(msg)
@@ -193,6 +195,10 @@ class CacheServer:
         except Exception:                 # answered, never left hanging
             logger.exception("request uid %d failed", msg.uid)
             ret = -errno.EIO
+        if logger.isEnabledFor(logging.DEBUG):
+            logger.debug("%s worker:%u uid:%u keys:%d -> %d (%.2f ms)", type(msg).__name__ if not isinstance(
+                msg, P.Transfer) else msg.op.name, msg.node_id, msg.uid, getattr(msg, "keys_num", 0), ret,
+                (time.perf_counter() - t0) * 1e3)
         self._reply(ident, msg.uid, ret)
 
     # ---- operations (main.c:58-190) ------------------------------------

@@ -90,7 +90,7 @@ def test_engine_through_the_server(tp):
     srv = subprocess.Popen([sys.executable, "-m", "demo_b200.server", "-P", str(port), "--host", "127.0.0.1",
                             "--cachedir", "", "--poolsize", str(1 << 30)],
                            stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, cwd=ROOT,
-                           env=dict(os.environ, CROSSCACHE_PYLOG="INFO"))
+                           env=dict(os.environ, CROSSCACHE_PYLOG="DEBUG"))
     lines: list[str] = []
     listening = threading.Event()
 
@@ -122,6 +122,8 @@ def test_engine_through_the_server(tp):
         if m:
             per_rank[int(m.group(2))] = (int(m.group(1)), json.loads(m.group(3)))
     assert sorted(per_rank) == list(range(tp)), "".join(lines)[-4000:]
+    requests = [ln.split("server:", 1)[-1].strip() for ln in lines
+                if re.search(r"(LOOKUP|Lookup|STORE|LOAD) worker", ln)]
     for rank, (world, st) in per_rank.items():
         assert world == tp
-        assert st["stored"] == RECORDS and st["loaded"] == RECORDS, (rank, st)
+        assert st["stored"] == RECORDS and st["loaded"] == RECORDS, (rank, json.dumps(st), requests[-60:])

@@ -23,6 +23,7 @@ import json
 import os
 import sys
 import tempfile
+import time
 
 
 def main() -> None:
@@ -77,7 +78,13 @@ def main() -> None:
                for i in range(4)]
     sp = SamplingParams(max_tokens=16, temperature=0, detokenize=False)
     first = llm.generate(prompts, sp, use_tqdm=False)
+    # generate() returns once every request has its tokens; the connector's
+    # stores of those requests may still be in flight (vLLM only holds their
+    # blocks until the connector reports them done), and a second pass that
+    # starts first finds nothing and recomputes.  Let them land.
+    chunks = sum(len(p["prompt_token_ids"]) // 256 for p in prompts)
     if a.server_port:
+        time.sleep(5.0)           # the counters live in the server process
         second = llm.generate(prompts, sp, use_tqdm=False)
         print("ENGINE_RESULT " + json.dumps({
             "mode": mode, "backend": backend, "model": model, "tp": a.tp, "server": True,
@@ -89,6 +96,9 @@ def main() -> None:
     from demo_b200 import connector
 
     adapter = next(iter(connector._LOCAL_WORKERS.values()))
+    deadline = time.time() + 60
+    while adapter.worker.stats()["stored"] < chunks and time.time() < deadline:
+        time.sleep(0.05)
     st1 = adapter.worker.stats()
     second = llm.generate(prompts, sp, use_tqdm=False)
     st2 = adapter.worker.stats()
