@@ -5,23 +5,31 @@ x 128, bf16, block 16, 16384 blocks per layer; 64 requests x 2048 tokens).
 
 One process per GPU (torchrun for N > 1).  At N GPUs the KV heads are split
 tensor-parallel (8/N heads per rank); every rank saves and loads its own head
-shard (no data exchange) and one NCCL all-reduce(min) agrees the per-request
-hit length before loading.
+shard (no data exchange) and one NCCL all-reduce(min) per lookup agrees the
+per-request hit length before loading.
 
 Printed JSON line (rank 0):
-  value      save+load payload GB/s of all ranks with the records in HBM:
-             one gather launch (paged -> records) and one scatter launch
-             (records -> a fresh block table) per step, CUDA-event timed
-  e2e        the same metric through the public C API with the pinned host
-             record pool: device block hashing of the tokens, cache_store,
-             cache_lookup_batch, all-reduce(min), one cache_load per request
-             (host clock, H2D/D2H inside); p50 per-request load latency
-  roofline   gather kernel vs the measured HBM copy peak
-  link       e2e save/load vs the host link measured in the same run
+  value      save + load payload GB/s of all ranks through the public C API
+             (cache_store / cache_lookup_batch / cache_load) between the paged
+             KV cache in HBM and the pinned host record pool, host copies
+             inside: each step hashes the token ids on the device, stores
+             every request and loads it back, with request r's load (H2D)
+             overlapping request r+1's store (D2H) -- the cache serving both
+             directions at once.  e2e is the same measurement (with the bytes
+             it moves across the host link); `sequential` is the store-all-
+             then-load-all step
+  link       a synchronised host-link probe (every rank copying at once for
+             2 s per direction and both directions together; rank 0 alone at
+             N > 1) and the e2e rates as fractions of it
+  device     gather + scatter kernels with the records in HBM (CUDA events)
+  roofline   the gather kernel that ran (kv_copy_path) vs the measured HBM copy peak
+  tp70b / prefix_reuse / mla_evict   the other configurations (Llama-3-70B
+             TP at every N; prefix reuse and MLA eviction pressure at N = 1)
   cpu_baseline  the oracle's C restatement of CrossCache's CPU memcpy path
              on the host cores, on a bounded sample of the workload
 --impl reference times CrossCache's own CPU transfer path (its mem.cpp
-compiled from the reference sources, oracle/_ref) on the host cores.
+compiled from the reference sources, oracle/_ref) on the host cores, on this
+world size's head shard.
 """
 from __future__ import annotations
 
@@ -50,13 +58,17 @@ GB = 1e9
 
 PRESETS = {
     # the headline config: Llama-3-8B GQA, 64 requests x 2048 tokens
-    "llama3-8b": dict(layers=32, requests=64, tokens=2048, blocks=16384,
+    "llama3-8b": dict(layers=32, requests=64, tokens=2048, blocks=16384, model="llama-3-8b",
                       name="llama3-8b-gqa-kv-offload: 32 layers x 8 KV heads x 128 bf16, block 16, "
                            "16384 blocks/layer; 64 requests x 2048 tokens; 256-token records"),
-    # the TP config: Llama-3-70B, 80 layers, heads re-split per world size
-    "tp70b": dict(layers=80, requests=32, tokens=8192, blocks=16384,
+    # the TP config: Llama-3-70B, 80 layers, heads re-split per world size.
+    # 32 x 8192 tokens fill 16384 blocks; 512 more per layer hold request 0's
+    # reload while the other requests' blocks are still being saved (the
+    # duplex step reloads request r into the blocks request r - 1 was saved
+    # from)
+    "tp70b": dict(layers=80, requests=32, tokens=8192, blocks=16896, model="llama-3-70b",
                   name="llama3-70b-tp-kv-offload: 80 layers x 8 KV heads x 128 bf16 split over TP ranks, "
-                       "block 16, 16384 blocks/layer; 32 requests x 8192 tokens; 256-token records"),
+                       "block 16, 16896 blocks/layer; 32 requests x 8192 tokens; 256-token records"),
 }
 
 
@@ -84,25 +96,32 @@ def peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-def kvcopy_path() -> str:
-    """which gather/scatter kernel the value path runs (CROSSCACHE_KVCOPY=lsu forces registers)"""
-    return "lsu" if os.environ.get("CROSSCACHE_KVCOPY") == "lsu" else "bulk"
+PATH_NAMES = {1: "kv_copy_kernel (16-byte register copies)",
+              2: "kv_copy_bulk_kernel (TMA cp.async.bulk via shared memory)",
+              3: "kv_copy_bulk_hnd_kernel (TMA bulk + head-major transpose in shared memory)"}
 
 
-def ncu_traffic(algorithmic_bytes: int) -> float | None:
-    """DRAM bytes of one gather launch moving `algorithmic_bytes`: the committed
-    ncu summary's DRAM bytes per algorithmic byte (a launch larger than L2, so
+def profile_for(path: int, unit: int) -> Path:
+    """the committed ncu summary of the kernel a launch ran"""
+    if path == 1:
+        return ROOT / "profiles" / ("kv_copy_register_256b_unit.md" if unit < 1024 else "kv_copy_gather.md")
+    return ROOT / "profiles" / ("kv_copy_bulk.md" if path == 2 else "kv_copy_flashinfer_hnd.md")
+
+
+def ncu_traffic(path: int, unit: int, algorithmic_bytes: int) -> tuple[float | None, str | None]:
+    """DRAM bytes of one launch moving `algorithmic_bytes`: the matching ncu
+    summary's DRAM bytes per algorithmic byte (a capture larger than L2, so
     traffic grows in proportion), times this launch's algorithmic bytes."""
-    f = ROOT / "profiles" / ("kv_copy_gather.md" if kvcopy_path() == "lsu" else "kv_copy_bulk.md")
+    f = profile_for(path, unit)
     if not f.exists():
-        return None
+        return None, None
     for line in f.read_text().splitlines():
         if line.startswith("traffic_per_algorithmic_byte:"):
             try:
-                return round(float(line.split(":", 1)[1].strip()) * algorithmic_bytes)
+                return round(float(line.split(":", 1)[1].strip()) * algorithmic_bytes), f"profiles/{f.name}"
             except ValueError:
-                return None
-    return None
+                return None, None
+    return None, None
 
 
 class ClockSampler:
@@ -159,18 +178,48 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(mhz)}
 
 
+def host_info() -> dict:
+    """read-only facts about the box the numbers come from"""
+    info = {"cpus": os.cpu_count(), "cpu_model": _cpu_model(), "mem_available_gib": round(_mem_available() / 2**30, 1)}
+    try:
+        q = subprocess.run(["nvidia-smi", "--query-gpu=index,pci.bus_id,pcie.link.gen.current,"
+                            "pcie.link.width.current,pcie.link.gen.max,pcie.link.width.max",
+                            "--format=csv,noheader"], capture_output=True, text=True, timeout=30)
+        info["pcie"] = [ln.strip() for ln in q.stdout.splitlines() if ln.strip()]
+        t = subprocess.run(["nvidia-smi", "topo", "-m"], capture_output=True, text=True, timeout=30)
+        # the GPU rows: link type to each peer, CPU and NUMA affinity
+        info["topo"] = [" ".join(ln.split()) for ln in t.stdout.splitlines() if ln.startswith("GPU")]
+    except Exception as e:
+        info["nvidia_smi"] = repr(e)
+    return info
+
+
+def _mem_available() -> int:
+    try:
+        with open("/proc/meminfo") as f:
+            for ln in f:
+                if ln.startswith("MemAvailable:"):
+                    return int(ln.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
 # ---------------------------------------------------------------------------
 # CPU legs (oracle port / compiled reference), host memory only
 
-def cpu_sample_run(impl: str, seconds: float | None, iters: int | None, threads: int) -> dict:
-    """Save then load a bounded sample (64 of the 512 records, 1024 blocks) of
-    the workload shapes through a CPU implementation of CrossCache's path.
-    Returns GB/s of save+load payload."""
+def cpu_sample_run(impl: str, seconds: float | None, iters: int | None, threads: int, shards: int = 1) -> dict:
+    """Save then load a bounded sample of the workload through a CPU
+    implementation of CrossCache's path: 64 of the 512 full-width records
+    (2 GiB per direction), or under a TP split into `shards` the same bytes as
+    64 * shards records of one rank's head shard (unit 8/shards heads x 128
+    bf16), paged cache in host memory.  Returns GB/s of save+load payload."""
     sys.path.insert(0, str(ROOT))
     from oracle import kvcopy as ok
 
-    nb, chunks = 1024, 64
-    unit = KV_HEADS * HEAD_DIM * ELT
+    chunks = 64 * shards
+    nb = chunks * (CHUNK // BS)
+    unit = (KV_HEADS // shards) * HEAD_DIM * ELT
     layer_bytes = nb * BS * unit
     k = [np.full(layer_bytes, l, np.uint8) for l in range(L)]
     v = [np.full(layer_bytes, 100 + l, np.uint8) for l in range(L)]
@@ -189,10 +238,10 @@ def cpu_sample_run(impl: str, seconds: float | None, iters: int | None, threads:
         pool = ThreadPoolExecutor(threads)
 
         def one_step():
-            list(pool.map(lambda c: ref.lib.transfer_kvcache(ref.ad, C.byref(_params(ref, recs[c], k, v, slots1[c], True))),
-                          range(chunks)))
-            list(pool.map(lambda c: ref.lib.transfer_kvcache(ref.ad, C.byref(_params(ref, recs[c], k, v, slots2[c], False))),
-                          range(chunks)))
+            list(pool.map(lambda c: ref.lib.transfer_kvcache(
+                ref.ad, C.byref(_params(ref, recs[c], k, v, slots1[c], True, unit))), range(chunks)))
+            list(pool.map(lambda c: ref.lib.transfer_kvcache(
+                ref.ad, C.byref(_params(ref, recs[c], k, v, slots2[c], False, unit))), range(chunks)))
         # the reference prints a log line per token to stdout: send it to /dev/null
         sys.stdout.flush()
         saved, devnull = os.dup(1), os.open(os.devnull, os.O_WRONLY)
@@ -212,11 +261,13 @@ def cpu_sample_run(impl: str, seconds: float | None, iters: int | None, threads:
         times = _time_steps(one_step, seconds, iters)
         kind, sample = "port", "oracle/kvcopy_oracle.c restatement of mem.cpp:114-173 + cache.c:513-593"
     gbs = [payload / t / GB for t in times]
+    shard = (f"{chunks} records of one TP={shards} rank's head shard ({KV_HEADS // shards} heads, {unit}-byte "
+             f"units, {rec_bytes >> 20} MiB records; the same bytes as 64 full-width records)"
+             if shards > 1 else f"64 of 512 records (1024 blocks, {rec_bytes >> 20} MiB records)")
     return {"value": statistics.median(gbs), "unit": "GB/s", "cores": threads, "kind": kind,
-            "sample": f"{sample}; 64 of 512 records (1024 blocks, {rec_bytes >> 20} MiB records), "
-                      f"save then load into a second block table, paged cache in host memory; "
-                      f"median of {len(times)} passes",
-            "times_s": [round(t, 4) for t in times]}
+            "sample": f"{sample}; {shard}, save then load into a second block table, paged cache in host "
+                      f"memory; median of {len(times)} passes",
+            "times_s": [round(t, 4) for t in times], "shards": shards, "unit_bytes": unit}
 
 
 def _cpu_model() -> str:
@@ -230,14 +281,14 @@ def _cpu_model() -> str:
     return "unknown"
 
 
-def _params(ref, rec, k, v, slots, direction):
+def _params(ref, rec, k, v, slots, direction, unit):
     from oracle.kvcopy import _RefParams
     kp = np.array([a.ctypes.data for a in k], np.uint64)
     vp = np.array([a.ctypes.data for a in v], np.uint64)
     p = _RefParams(caches=rec.ctypes.data, caches_h=rec.ctypes.data, keys_ptrs=kp.ctypes.data,
                    value_ptrs=vp.ctypes.data, page_buffer_size=0, slot_mapping=slots.ctypes.data,
                    devid=0, caches_element_size=1, num_layers=len(kp), num_tokens=CHUNK,
-                   hidden_dim_size=KV_HEADS * HEAD_DIM * ELT, direction=direction)
+                   hidden_dim_size=unit, direction=direction)
     p._keep = (kp, vp)
     return p
 
@@ -257,14 +308,19 @@ def _time_steps(fn, seconds, iters):
 
 
 def run_reference_arm(args) -> None:
+    """CrossCache's own CPU path on the host cores, on this world size's work:
+    at N GPUs under TP the host serves N head shards, so the sample is made of
+    one rank's shard records (unit 8/N heads) holding the same bytes as the
+    N = 1 sample, all host threads, one process (rank 0; the others exit)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
+    shards = max(1, args.gpus)
     have_ref = (ROOT / "oracle" / "_ref" / "libref_mem.so").exists()
     impl = "reference" if have_ref else "port"
-    cpu_sample_run(impl, None, args.warmup, threads)      # warm-up passes
-    res = cpu_sample_run(impl, None, args.steps, threads)
+    cpu_sample_run(impl, None, args.warmup, threads, shards)      # warm-up passes
+    res = cpu_sample_run(impl, None, args.steps, threads, shards)
     v = res["value"]
     line = {"metric": METRIC, "value": round(v, 3), "unit": "GB/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -272,6 +328,9 @@ def run_reference_arm(args) -> None:
             "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
             "config": workload_config(args.gpus),
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "shard": {"tp": shards, "kv_heads_per_shard": KV_HEADS // shards, "unit_bytes": res["unit_bytes"],
+                      "processes": 1, "threads": threads,
+                      "note": "the host serves every rank's shard; one process times them on all host threads"},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -308,13 +367,13 @@ def run_cache_workload(args) -> None:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     if args.workload == "prefix-reuse":
-        res = _prefix_reuse(args, dev, cc, lib)
+        res = _prefix_reuse(dev, cc, lib, args.steps, args.warmup)
     else:
-        res = _mla_evict(args, dev, cc, lib, LRUPool)
+        res = _mla_evict(dev, cc, lib, LRUPool, args.steps, args.warmup)
     print(json.dumps(res), flush=True)
 
 
-def _prefix_reuse(args, dev, cc, lib) -> dict:
+def _prefix_reuse(dev, cc, lib, steps: int, warmup: int, layers=None) -> dict:
     """256 requests = one shared 1024-token prefix + a unique 512-token suffix
     (token ids U[0,128256), seed 1); Llama-3-8B KV shapes (32 layers x 8 KV
     heads x 128 bf16, block 16, 16384 blocks/layer, N(0,1) seed 0).  Per step:
@@ -324,9 +383,10 @@ def _prefix_reuse(args, dev, cc, lib) -> dict:
     import torch
     nreq, pre, suf = 256, 1024, 512
     ntok = pre + suf
-    g = torch.Generator(device=dev).manual_seed(0)
-    layers = [torch.randn(2, NUM_BLOCKS, BS, KV_HEADS, HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
-              for _ in range(L)]
+    if layers is None:
+        g = torch.Generator(device=dev).manual_seed(0)
+        layers = [torch.randn(2, NUM_BLOCKS, BS, KV_HEADS, HEAD_DIM, generator=g, device=dev).to(torch.bfloat16)
+                  for _ in range(L)]
     layout, kp, vp = cc.layout_from_kv_tensors(layers)
     rb = layout.per_token_size * CHUNK
     gt = torch.Generator().manual_seed(1)
@@ -381,11 +441,11 @@ def _prefix_reuse(args, dev, cc, lib) -> dict:
         return t1 - t0, t2 - t1, t3 - t2, int(hits.sum()), ok
 
     _, _, _, _, ok = step(None, check=True)          # pristine first pass: verified
-    for _ in range(max(0, args.warmup - 1)):
+    for _ in range(max(0, warmup - 1)):
         step(None)
     lat, parts = [], []
     ta = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         parts.append(step(lat))
     te = time.perf_counter() - ta
     st = w.stats()
@@ -396,11 +456,11 @@ def _prefix_reuse(args, dev, cc, lib) -> dict:
     loaded_b = hit_chunks * rb
     save_s = statistics.median(p[1] for p in parts)
     load_s = statistics.median(p[2] for p in parts)
-    return {"metric": METRIC, "value": round((stored_b + loaded_b) * args.steps / te / GB, 3), "unit": "GB/s",
+    return {"metric": METRIC, "value": round((stored_b + loaded_b) * steps / te / GB, 3), "unit": "GB/s",
             "workload": "prefix-reuse: Llama-3-8B KV, 256 requests = shared 1024-token prefix + unique "
                         "512-token suffix; save 128, look up + load the other 128",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(te / args.steps * 1e3, 3), "higher_is_better": True,
+            "n_gpus": 1, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(te / steps * 1e3, 3), "higher_is_better": True,
             "data": "synthetic", "dtype": "u8",
             "hit_blocks_per_request": hit_chunks * bpc // 128, "hit_rate_chunks": round(hit_chunks / (128 * kpr), 4),
             "records_stored_per_step": uniq, "store_keys_deduplicated_per_step": 128 * kpr - uniq,
@@ -410,7 +470,7 @@ def _prefix_reuse(args, dev, cc, lib) -> dict:
             "verified_bytes": bool(ok), "stats": st}
 
 
-def _mla_evict(args, dev, cc, lib, LRUPool) -> dict:
+def _mla_evict(dev, cc, lib, LRUPool, steps: int, warmup: int) -> dict:
     """DeepSeek-V2-Lite MLA latent cache: 27 layers, K-only width 576 bf16,
     block 64.  512 requests x 4096 tokens = a 2048-token base prefix (one of 64
     seeded bases, chosen Zipf(1.1), seed 4) + a unique 2048-token suffix
@@ -503,11 +563,11 @@ def _mla_evict(args, dev, cc, lib, LRUPool) -> dict:
     ev0 = w.stats()["evictions"]
     hit_tot, mism, *_ = one_pass(True)
     ev1 = w.stats()["evictions"]
-    for _ in range(max(0, args.warmup - 1)):
+    for _ in range(max(0, warmup - 1)):
         one_pass(False)
     res = []
     ta = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(steps):
         e0 = w.stats()["evictions"]
         res.append(one_pass(False) + (w.stats()["evictions"] - e0,))
     te = time.perf_counter() - ta
@@ -518,8 +578,8 @@ def _mla_evict(args, dev, cc, lib, LRUPool) -> dict:
     return {"metric": METRIC, "value": round(moved / te / GB, 3), "unit": "GB/s",
             "workload": "mla-evict: DeepSeek-V2-Lite MLA latent (27 layers, 576 bf16, block 64), 512 requests x "
                         "4096 tokens, Zipf(1.1) reuse of 64 base prefixes, host pool 25 % of the working set",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(te / args.steps * 1e3, 3), "higher_is_better": True,
+            "n_gpus": 1, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(te / steps * 1e3, 3), "higher_is_better": True,
             "data": "synthetic", "dtype": "u8",
             "pool_records": pool_records, "working_set_records": total_records,
             "hit_rate_chunks": round(hit_tot / total_records, 4),
@@ -533,7 +593,7 @@ def _mla_evict(args, dev, cc, lib, LRUPool) -> dict:
 
 
 # ---------------------------------------------------------------------------
-# GPU arm
+# optional probes of the headline workload (disk tier, layer-wise, server, paged layouts)
 
 def _fs_type(path: str) -> str:
     best, kind = "", "unknown"
@@ -768,9 +828,7 @@ def _paged_layout_probe(args, layers, b_save, b_load, s) -> dict:
                      "gather_frac": round(moved / (gms / 1e3) / GB / hbm_peak, 4),
                      "scatter_frac": round(moved / (sms / 1e3) / GB / hbm_peak, 4),
                      "gather_ms": round(gms, 4), "scatter_ms": round(sms, 4),
-                     "path": ("register (head split folded into the address)" if kvcopy_path() == "lsu" else
-                              "bulk, blocks transposed in shared memory (kv_copy_bulk_hnd_kernel)") if hnd else
-                             ("register" if kvcopy_path() == "lsu" else "bulk (cp.async.bulk, strided blocks)"),
+                     "path": PATH_NAMES.get(lib.kv_copy_path(C.byref(dg)), "?"),
                      "verified_bytes": bool(same_records and same_blocks)}
         del fi, kp_d, vp_d
         torch.cuda.empty_cache()
@@ -890,6 +948,613 @@ def _server_probe(args, layers, hashes, bt_save, bt_load, disjoint, s) -> dict:
             p.kill()
 
 
+# ---------------------------------------------------------------------------
+# GPU arm
+
+class Ranks:
+    """This process's place in the job, and the few collectives the bench
+    takes (every rank takes them in the same order)."""
+
+    def __init__(self, world: int, rank: int, local: int, dev, shards: int, shard_index: int):
+        self.world, self.rank, self.local, self.dev = world, rank, local, dev
+        self.shards, self.shard_index = shards, shard_index
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def _reduce(self, x: float, op) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    def max(self, x: float) -> float:
+        import torch.distributed as dist
+        return self._reduce(x, dist.ReduceOp.MAX if self.world > 1 else None)
+
+    def min(self, x: float) -> float:
+        import torch.distributed as dist
+        return self._reduce(x, dist.ReduceOp.MIN if self.world > 1 else None)
+
+    def sum(self, x: float) -> float:
+        import torch.distributed as dist
+        return self._reduce(x, dist.ReduceOp.SUM if self.world > 1 else None)
+
+    def gather(self, x: float) -> list[float]:
+        if self.world == 1:
+            return [x]
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        out = [torch.zeros_like(t) for _ in range(self.world)]
+        dist.all_gather(out, t)
+        return [float(o.item()) for o in out]
+
+
+def link_probe(rk: Ranks, seconds: float) -> dict:
+    """The host link as the e2e steps see it.  After a barrier every rank
+    copies 256 MiB pinned <-> device buffers on its own stream for `seconds`
+    (four copies in flight): D2H alone, H2D alone, and both directions at
+    once on two streams; at N > 1 also rank 0 alone (the others idle), which
+    separates a per-GPU link limit from the box's shared one.  Per GPU: bytes
+    / CUDA-event time on the copy stream; aggregate: all ranks' bytes / the
+    slowest rank's time."""
+    import torch
+
+    mb = 256 << 20
+    hd = torch.empty(mb, dtype=torch.uint8, pin_memory=True)      # D2H destination
+    hh = torch.empty(mb, dtype=torch.uint8, pin_memory=True)      # H2D source
+    dd = torch.zeros(mb, dtype=torch.uint8, device=rk.dev)
+    dh = torch.empty(mb, dtype=torch.uint8, device=rk.dev)
+    streams = {"d2h": torch.cuda.Stream(rk.dev), "h2d": torch.cuda.Stream(rk.dev)}
+    ops = {"d2h": lambda: hd.copy_(dd, non_blocking=True), "h2d": lambda: dh.copy_(hh, non_blocking=True)}
+
+    def run(kinds, secs, active=True):
+        torch.cuda.synchronize()
+        rk.barrier()
+        out = {k: (0.0, 1.0) for k in kinds}
+        if active:
+            e0 = {k: torch.cuda.Event(enable_timing=True) for k in kinds}
+            e1 = {k: torch.cuda.Event(enable_timing=True) for k in kinds}
+            ring = {k: [torch.cuda.Event() for _ in range(4)] for k in kinds}
+            n = dict.fromkeys(kinds, 0)
+            for k in kinds:
+                e0[k].record(streams[k])
+            t0 = time.perf_counter()
+            while time.perf_counter() - t0 < secs:
+                for k in kinds:
+                    if n[k] >= 4:
+                        ring[k][n[k] % 4].synchronize()
+                    with torch.cuda.stream(streams[k]):
+                        ops[k]()
+                    ring[k][n[k] % 4].record(streams[k])
+                    n[k] += 1
+            for k in kinds:
+                e1[k].record(streams[k])
+            torch.cuda.synchronize()
+            out = {k: (float(n[k] * mb), e0[k].elapsed_time(e1[k]) / 1e3) for k in kinds}
+        rk.barrier()
+        return out
+
+    def summarise(r, k):
+        b, t = rk.gather(r[k][0]), rk.gather(r[k][1])
+        rates = sorted(x / y / GB for x, y in zip(b, t))
+        return {"per_gpu_min": round(rates[0], 2), "per_gpu_median": round(statistics.median(rates), 2),
+                "per_gpu_max": round(rates[-1], 2), "aggregate": round(sum(b) / max(t) / GB, 2)}
+
+    run(["d2h", "h2d"], 0.3)                         # warm the copy paths
+    res = {"seconds_per_probe": seconds, "buffer_mib": 256}
+    for k in ("d2h", "h2d"):
+        res[k] = summarise(run([k], seconds), k)
+    r = run(["d2h", "h2d"], seconds)
+    res["both"] = {k: summarise(r, k) for k in ("d2h", "h2d")}
+    res["both"]["aggregate"] = round(res["both"]["d2h"]["aggregate"] + res["both"]["h2d"]["aggregate"], 2)
+    if rk.world > 1:
+        solo = {}
+        for k in ("d2h", "h2d"):
+            r = run([k], seconds / 2, active=rk.rank == 0)
+            solo[k] = round(r[k][0] / r[k][1] / GB, 2) if rk.rank == 0 else None
+        res["solo_rank0"] = solo
+    del hd, hh, dd, dh
+    torch.cuda.empty_cache()
+    return res
+
+
+def _block_sums(layers, idx, dev) -> list:
+    """per (layer, K/V, block) position-weighted int64 checksums of the given blocks"""
+    import torch
+    out = []
+    for t in layers:
+        per = []
+        for kv in range(2):
+            x = t[kv, idx].view(torch.int16).reshape(idx.numel(), -1).to(torch.int64)
+            wgt = (torch.arange(x.shape[1], device=dev, dtype=torch.int64) % 251) + 1
+            per.append(torch.stack([x.sum(1), (x * wgt).sum(1)]))
+            del x
+        out.append(torch.stack(per))
+    return out
+
+
+def _sums_equal(a: list, b: list) -> bool:
+    import torch
+    return all(torch.equal(x, y) for x, y in zip(a, b))
+
+
+class Offload:
+    """One KV-offload workload on this rank's head shard: the seeded paged
+    cache (this rank's heads of N(0,1) bf16 values, seed 0), the block tables
+    (save: seeded permutation, seed 2; reload: seed 3 over the blocks the save
+    did not use when the cache holds both, else over all blocks), the token
+    ids (uniform, seed 1) and the keys (vLLM's chained sha256 block hashes,
+    one per 256-token record)."""
+
+    def __init__(self, rk: Ranks, preset: str, over: dict | None = None):
+        import torch
+
+        from demo_b200 import cache as cc
+
+        pr = dict(PRESETS[preset], **(over or {}))
+        self.rk, self.preset, self.model = rk, preset, pr["model"]
+        self.n_layers, self.n_req, self.n_blocks, self.n_tok = pr["layers"], pr["requests"], pr["blocks"], pr["tokens"]
+        self.full_size = not over
+        self.heads = KV_HEADS // rk.shards
+        self.unit = self.heads * HEAD_DIM * ELT
+        self.bpc = CHUNK // BS
+        self.prb = self.n_tok // BS                 # blocks per request
+        self.kpr = self.n_tok // CHUNK              # records (keys) per request
+        self.nblk = self.n_req * self.prb
+        self.nrec = self.nblk // self.bpc
+        self.rec_bytes = 2 * self.n_layers * CHUNK * self.unit
+        self.payload = self.nrec * self.rec_bytes   # one direction, this rank
+        self.group = 1                              # requests per lookup + hit agreement (duplex)
+        if self.nblk > self.n_blocks:
+            raise SystemExit("blocks per layer must hold the saved blocks")
+        dev = rk.dev
+        g = torch.Generator(device=dev).manual_seed(0)
+        h0 = rk.shard_index * self.heads
+        self.layers = []
+        for _ in range(self.n_layers):
+            full = torch.randn(2, self.n_blocks, BS, KV_HEADS, HEAD_DIM, generator=g, device=dev,
+                               dtype=torch.float32).to(torch.bfloat16)
+            self.layers.append(full[:, :, :, h0:h0 + self.heads].contiguous())
+            del full
+        torch.cuda.empty_cache()
+        self.layout, self.kp, self.vp = cc.layout_from_kv_tensors(self.layers)
+        perm = torch.randperm(self.n_blocks, generator=torch.Generator().manual_seed(2))
+        self.bt_save = perm[:self.nblk].numpy().astype(np.uint64)
+        self.disjoint = 2 * self.nblk <= self.n_blocks
+        spare = perm[self.nblk:]
+        free = spare if self.disjoint else perm
+        self.bt_load = free[torch.randperm(free.numel(), generator=torch.Generator().manual_seed(3))][
+            :self.nblk].numpy().astype(np.uint64)
+        # rotating reload table: the disjoint reload table, or -- when the
+        # cache cannot hold two tables -- request r reloads into the blocks
+        # request r - group was saved from (saved before, read by nobody
+        # after), the first group into spare blocks.  The duplex step and the
+        # batched device step (records reused across batches) need it.
+        d = self.group * self.prb
+        if self.disjoint:
+            self.bt_dup = self.bt_load
+        elif spare.numel() >= d:
+            self.bt_dup = np.concatenate([spare[:d].numpy().astype(np.uint64), self.bt_save[:self.nblk - d]])
+        else:
+            self.bt_dup = None
+        self.tokens = torch.randint(0, VOCAB, (self.n_req, self.n_tok), generator=torch.Generator().manual_seed(1),
+                                    dtype=torch.int64).to(torch.int32).numpy()
+
+    def free(self) -> None:
+        import torch
+        del self.layers
+        torch.cuda.empty_cache()
+
+    def config(self) -> dict:
+        if self.full_size:
+            return workload_config(self.rk.shards, self.preset)
+        c = workload_config(self.rk.shards, self.preset, layers=self.n_layers, requests=self.n_req,
+                            blocks=self.n_blocks, tokens=self.n_tok)
+        c["workload"] = (f"reduced case for profiling: {self.n_layers} layers, {self.n_req} requests x "
+                         f"{self.n_tok} tokens, {self.n_blocks} blocks/layer")
+        return c
+
+    # -- kernels only: records in HBM ---------------------------------------
+    def device_step(self, steps: int, warmup: int) -> dict:
+        """One gather launch (paged -> records) and one scatter launch (records
+        -> the reload table) per step, records in HBM (all of them when they
+        fit beside the paged cache, else batches reusing one buffer), CUDA
+        events on the launch stream."""
+        import torch
+
+        from demo_b200._lib import KVCOPY_FLAG_BULK, KvCopyDesc, lib
+        rk, dev = self.rk, self.rk.dev
+        kp_d = torch.tensor(self.kp, dtype=torch.int64, device=dev)
+        vp_d = torch.tensor(self.vp, dtype=torch.int64, device=dev)
+        free_b, _ = torch.cuda.mem_get_info(dev)
+        batch = int(max(1, min(self.nrec, (free_b - (12 << 30)) // self.rec_bytes)))
+        nbatch = (self.nrec + batch - 1) // batch
+        records = torch.empty(batch * self.rec_bytes, dtype=torch.uint8, device=dev)
+        rec_ptrs = torch.arange(batch, dtype=torch.int64, device=dev) * self.rec_bytes + records.data_ptr()
+        b_save = torch.from_numpy(self.bt_save.astype(np.int64)).to(dev)
+        # record batches are gathered and scattered in turn, so a scatter must
+        # not land on blocks a later batch still gathers: the rotating table
+        table = self.bt_dup if self.bt_dup is not None else self.bt_load
+        b_load = torch.from_numpy(table.astype(np.int64)).to(dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        def desc(bids, first, n, direction):
+            return KvCopyDesc(layer_k=kp_d.data_ptr(), layer_v=vp_d.data_ptr(), records=rec_ptrs.data_ptr(),
+                              slots=None, block_ids=bids.data_ptr() + first * self.bpc * 8, error=err.data_ptr(),
+                              page_buffer_size=self.n_blocks * BS, unit_bytes=self.unit, num_tokens=CHUNK,
+                              block_size=BS, num_layers=self.n_layers, num_records=n, direction=direction,
+                              flags=KVCOPY_FLAG_BULK)
+
+        batches = [(i * batch, min(batch, self.nrec - i * batch)) for i in range(nbatch)]
+        pairs = [(desc(b_save, f, n, 1), desc(b_load, f, n, 0)) for f, n in batches]
+        assert sum(lib.kv_copy_payload_bytes(C.byref(g)) for g, _ in pairs) == self.payload
+        path = lib.kv_copy_path(C.byref(pairs[0][0]))
+        stream = torch.cuda.Stream(dev)
+        sptr = C.c_void_p(stream.cuda_stream)
+
+        def step(ev=None):
+            for bi, (dg, ds) in enumerate(pairs):
+                if ev:
+                    ev[bi][0].record(stream)
+                assert lib.kv_copy_launch(C.byref(dg), sptr) == 0
+                if ev:
+                    ev[bi][1].record(stream)
+                assert lib.kv_copy_launch(C.byref(ds), sptr) == 0
+                if ev:
+                    ev[bi][2].record(stream)
+
+        sums0 = _block_sums(self.layers, b_save, dev)
+        step()                                # the first step, from the pristine cache: checked
+        torch.cuda.synchronize()
+        ok = _sums_equal(_block_sums(self.layers, b_load, dev), sums0)
+        del sums0
+        for _ in range(warmup - 1):
+            step()
+        torch.cuda.synchronize()
+        evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(nbatch)]
+               for _ in range(steps)]
+        l0 = lib.crosscache_kernel_launches()
+        rk.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            step(evs[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+        rk.barrier()
+        launches = lib.crosscache_kernel_launches() - l0
+        dt = rk.max(t0.elapsed_time(t1) / 1e3)
+        gather_ms = statistics.mean(sum(b[0].elapsed_time(b[1]) for b in e) for e in evs)
+        scatter_ms = statistics.mean(sum(b[1].elapsed_time(b[2]) for b in e) for e in evs)
+        assert int(err.item()) == 0, "kv copy reported an error"
+        if self.disjoint:
+            ok = ok and all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16))
+                            for t in self.layers)
+        ok = bool(rk.min(1.0 if ok else 0.0))
+        hbm_peak, peak_kind = peaks()
+        alg = 2 * min(batch, self.nrec) * self.rec_bytes        # read + write bytes of one launch
+        achieved = 2 * self.payload / (gather_ms / 1e3) / GB
+        traffic, traffic_src = ncu_traffic(path, self.unit, alg)
+        del records, rec_ptrs
+        torch.cuda.empty_cache()
+        return {"value": round(rk.sum(2 * self.payload) * steps / dt / GB, 3), "unit": "GB/s",
+                "ms_per_step": round(dt / steps * 1e3, 3), "steps": steps, "warmup": warmup,
+                "record_batches_per_step": nbatch, "launches": int(launches), "verified_bytes": ok,
+                "roofline": {"bound": "hbm", "kernel": PATH_NAMES.get(path, str(path)) + " gather",
+                             "path": path, "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                             "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+                             "traffic": traffic, "traffic_source": traffic_src, "algorithmic_bytes_per_launch": alg,
+                             "gather_ms": round(gather_ms, 4), "scatter_ms": round(scatter_ms, 4),
+                             "scatter_frac": round(2 * self.payload / (scatter_ms / 1e3) / GB / hbm_peak, 4),
+                             "unit_bytes": self.unit},
+                "note": "records in HBM; one gather + one scatter per record batch per step; CUDA events on "
+                        "the launch stream; frac of the measured HBM copy peak"}
+
+    def hash_kernel(self, steps: int, warmup: int) -> dict:
+        """the chained block-hash kernel over every request, tokens in HBM"""
+        import torch
+
+        from demo_b200.hashing import block_hashes_device
+        dev = self.rk.dev
+        nh = _sha_none()
+        tok_d = torch.from_numpy(self.tokens.reshape(-1).copy()).to(dev)
+        toff_d = torch.arange(self.n_req, dtype=torch.int64, device=dev) * self.n_tok
+        ooff_d = torch.arange(self.n_req, dtype=torch.int64, device=dev) * self.prb
+        nb_d = torch.full((self.n_req,), self.prb, dtype=torch.int32, device=dev)
+        hout = torch.empty(self.nblk, 32, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.Stream(dev)
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                block_hashes_device(tok_d, toff_d, nb_d, ooff_d, BS, nh, hout, stream=stream)
+            h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            h0.record(stream)
+            for _ in range(steps):
+                block_hashes_device(tok_d, toff_d, nb_d, ooff_d, BS, nh, hout, stream=stream)
+            h1.record(stream)
+        torch.cuda.synchronize()
+        ms = h0.elapsed_time(h1) / steps
+        return {"kernel_ms": round(ms, 4), "blocks": self.nblk, "chains": self.n_req,
+                "blocks_per_s": round(self.nblk / (ms / 1e3), 1),
+                "sha256_compressions_per_s": round(3 * self.nblk / (ms / 1e3), 1),
+                "us_per_block_along_a_chain": round(ms * 1e3 / self.prb, 3),
+                "bound": "integer latency along each chain (3 SHA-256 compressions per 16-token block)"}
+
+    # -- end to end: the public C API, pinned host record pool ----------------
+    def e2e(self, steps: int, warmup: int, pool_budget: float) -> dict:
+        """Both e2e steps through cache_store / cache_lookup_batch / cache_load
+        (host clock, every H2D / D2H inside), the pool sized to hold the step's
+        records (fewer requests per step if this rank's share of free host
+        memory cannot hold them all, said in `requests_per_step`)."""
+        import torch
+
+        from demo_b200 import cache as cc
+        from demo_b200._lib import lib
+        from demo_b200.tp import agree_min_hits
+
+        rk, dev = self.rk, self.rk.dev
+        G, kpr, prb, bpc = self.group, self.kpr, self.prb, self.bpc
+        fit = int(pool_budget // self.rec_bytes) - 1
+        R = int(rk.min(min(self.n_req, (max(0, fit) // kpr) // G * G)))
+        if R < G:
+            return {"skipped": f"pinned pool of {(G * kpr + 1) * self.rec_bytes / 2**30:.1f} GiB per rank does "
+                               f"not fit in {pool_budget / 2**30:.1f} GiB of this rank's share of free host memory"}
+        nblk, nrec = R * prb, R * kpr
+        payload = nrec * self.rec_bytes
+        cc.init(CHUNK, (nrec + 1) * self.rec_bytes, None)
+        w = cc.Worker(self.model, self.layout, self.kp, self.vp, node_id=rk.local, world_size=rk.world,
+                      rank=rk.rank)
+        w.register()
+        flat_tok = np.ascontiguousarray(self.tokens[:R].reshape(-1))
+        tok_lens = np.full(R, self.n_tok, dtype=np.int64)
+        hashes = np.zeros((nblk, 32), dtype=np.uint8)
+        key_nums = np.full(R, kpr, dtype=np.uint32)
+        hits = np.zeros(R, dtype=np.uint32)
+        none_hash = _sha_none()
+        save_all = np.ascontiguousarray(self.bt_save[:nblk])
+        saves = [np.ascontiguousarray(self.bt_save[r * prb:(r + 1) * prb]) for r in range(R)]
+        loads = [np.ascontiguousarray(self.bt_load[r * prb:(r + 1) * prb]) for r in range(R)]
+        b_save = torch.from_numpy(save_all.astype(np.int64)).to(dev)
+        b_load = torch.from_numpy(self.bt_load[:nblk].astype(np.int64)).to(dev)
+
+        def keys() -> bytes:
+            n = lib.kv_block_hash_host(rk.local, flat_tok.ctypes.data, tok_lens.ctypes.data, R, BS, none_hash,
+                                       hashes.ctypes.data)
+            assert n == nblk, n
+            return np.ascontiguousarray(hashes[bpc - 1::bpc]).tobytes()
+
+        def seq_step(lat):
+            t0 = time.perf_counter()
+            w.clear()
+            kb = keys()
+            th = time.perf_counter()
+            rk.barrier()                         # every rank starts its stores together
+            t1 = time.perf_counter()
+            ret = lib.cache_store(C.byref(w.ctx), kb, 32, save_all.ctypes.data, nblk)
+            assert ret == 0, ret
+            t2 = time.perf_counter()
+            rk.barrier()                         # the ranks' save skew, kept out of the agreement
+            t3 = time.perf_counter()
+            assert lib.cache_lookup_batch(C.byref(w.ctx), kb, key_nums.ctypes.data, R, 32, hits.ctypes.data) == 0
+            hit = agree_min_hits(hits, device=dev)       # NCCL all-reduce(min) under TP
+            t4 = time.perf_counter()
+            for r in range(R):
+                h = int(hit[r])
+                ts = time.perf_counter()
+                ret = lib.cache_load(C.byref(w.ctx), kb[r * kpr * 32:(r * kpr + h) * 32], 32, loads[r].ctypes.data,
+                                     h * bpc)
+                assert ret == 0, ret
+                if lat is not None:
+                    lat.append(time.perf_counter() - ts)
+            t5 = time.perf_counter()
+            return dict(hash=th - t0, store=t2 - t1, skew=t3 - t2, agree=t4 - t3, load=t5 - t4, total=t5 - t0,
+                        hits=int(hit.sum()))
+
+        dloads = ([np.ascontiguousarray(self.bt_dup[r * prb:(r + 1) * prb]) for r in range(R)]
+                  if self.bt_dup is not None else None)
+
+        def duplex_step(lat):
+            t0 = time.perf_counter()
+            w.clear()
+            kb = keys()
+            rk.barrier()
+            t1 = time.perf_counter()
+            done = [threading.Event() for _ in range(R)]
+            errs: list = []
+
+            def saver():
+                for r in range(R):
+                    try:
+                        ret = lib.cache_store(C.byref(w.ctx), kb[r * kpr * 32:(r + 1) * kpr * 32], 32,
+                                              saves[r].ctypes.data, prb)
+                        if ret:
+                            errs.append(("store", r, ret))
+                    finally:
+                        done[r].set()
+
+            th = threading.Thread(target=saver, daemon=True)
+            th.start()
+            agree_s, hit_tot = 0.0, 0
+            try:
+                for g0 in range(0, R, G):
+                    if not done[g0 + G - 1].wait(600):
+                        raise RuntimeError("stores did not finish")
+                    ta = time.perf_counter()
+                    kg = kb[g0 * kpr * 32:(g0 + G) * kpr * 32]
+                    assert lib.cache_lookup_batch(C.byref(w.ctx), kg, key_nums.ctypes.data, G, 32,
+                                                  hits.ctypes.data) == 0
+                    hit = agree_min_hits(hits[:G], device=dev)
+                    agree_s += time.perf_counter() - ta
+                    for j in range(G):
+                        r = g0 + j
+                        h = int(hit[j])
+                        hit_tot += h
+                        ts = time.perf_counter()
+                        ret = lib.cache_load(C.byref(w.ctx), kb[r * kpr * 32:(r * kpr + h) * 32], 32,
+                                             dloads[r].ctypes.data, h * bpc)
+                        if ret:
+                            errs.append(("load", r, ret))
+                        if lat is not None:
+                            lat.append(time.perf_counter() - ts)
+            finally:
+                th.join()
+            t2 = time.perf_counter()
+            assert not errs, errs
+            return dict(hash=0.0, io=t2 - t1, agree=agree_s, total=t2 - t0, hits=hit_tot)
+
+        def timed(fn):
+            lat: list[float] = []
+            parts = []
+            l0 = lib.crosscache_kernel_launches()
+            rk.barrier()
+            torch.cuda.synchronize()
+            ts0 = time.perf_counter()
+            for _ in range(steps):
+                parts.append(fn(lat))
+            torch.cuda.synchronize()
+            te = rk.max(time.perf_counter() - ts0)
+            rk.barrier()
+            return parts, lat, te, lib.crosscache_kernel_launches() - l0
+
+        def med(parts, key):
+            return rk.max(statistics.median(p[key] for p in parts))
+
+        try:
+            # sequential: store every request, look up, agree, load every request
+            if self.disjoint:
+                for t in self.layers:        # the exact final check needs the destination blocks empty
+                    t[:, b_load] = 0
+            sums = _block_sums(self.layers, b_save, dev)
+            seq_step(None)                   # checked first step
+            torch.cuda.synchronize()
+            ok_seq = _sums_equal(_block_sums(self.layers, b_load, dev), sums)
+            del sums
+            for _ in range(warmup - 1):
+                seq_step(None)
+            parts, lat, te, launches = timed(seq_step)
+            if self.disjoint:
+                ok_seq = ok_seq and all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16))
+                                        for t in self.layers)
+            ok_seq = bool(rk.min(1.0 if ok_seq else 0.0))
+            tot = rk.sum(2 * payload)
+            seq = {"value": round(tot * steps / te / GB, 3), "unit": "GB/s", "ms_per_step": round(te / steps * 1e3, 3),
+                   "save_gbs_aggregate": round(rk.sum(payload) / med(parts, "store") / GB, 3),
+                   "load_gbs_aggregate": round(rk.sum(payload) / med(parts, "load") / GB, 3),
+                   "save_gbs_per_gpu_slowest": round(payload / med(parts, "store") / GB, 3),
+                   "load_gbs_per_gpu_slowest": round(payload / med(parts, "load") / GB, 3),
+                   "hash_ms": round(med(parts, "hash") * 1e3, 3),
+                   "save_skew_ms": round(med(parts, "skew") * 1e3, 3),
+                   "lookup_agree_ms": round(med(parts, "agree") * 1e3, 3),
+                   "p50_load_latency_ms": round(rk.max(statistics.median(lat)) * 1e3, 3),
+                   "p90_load_latency_ms": round(rk.max(float(np.percentile(lat, 90))) * 1e3, 3),
+                   "hit_blocks_per_request": parts[-1]["hits"] * bpc // R, "gpu_launches": int(launches),
+                   "verified_bytes": ok_seq,
+                   "note": "hash; barrier; cache_store of every request; barrier (save skew); "
+                           "cache_lookup_batch + all-reduce(min); one cache_load per request"}
+            dup = None
+            if dloads is not None:
+                b_dup = torch.from_numpy(self.bt_dup[:nblk].astype(np.int64)).to(dev)
+                if self.disjoint:
+                    for t in self.layers:
+                        t[:, b_dup] = 0
+                sums = _block_sums(self.layers, b_save, dev)
+                duplex_step(None)            # checked first step
+                torch.cuda.synchronize()
+                ok_dup = _sums_equal(_block_sums(self.layers, b_dup, dev), sums)
+                del sums
+                for _ in range(warmup - 1):
+                    duplex_step(None)
+                parts, lat, te, launches = timed(duplex_step)
+                if self.disjoint:
+                    ok_dup = ok_dup and all(torch.equal(t[:, b_save].view(torch.int16),
+                                                        t[:, b_dup].view(torch.int16)) for t in self.layers)
+                ok_dup = bool(rk.min(1.0 if ok_dup else 0.0))
+                dup = {"value": round(tot * steps / te / GB, 3), "unit": "GB/s",
+                       "ms_per_step": round(te / steps * 1e3, 3),
+                       "lookup_agree_ms": round(med(parts, "agree") * 1e3, 3),
+                       "p50_load_latency_ms": round(rk.max(statistics.median(lat)) * 1e3, 3),
+                       "p90_load_latency_ms": round(rk.max(float(np.percentile(lat, 90))) * 1e3, 3),
+                       "hit_blocks_per_request": parts[-1]["hits"] * bpc // R, "gpu_launches": int(launches),
+                       "verified_bytes": ok_dup,
+                       "note": (f"hash; a store thread saves request after request while this thread, per "
+                                f"{'request' if G == 1 else f'group of {G} requests'}, waits for its stores, runs "
+                                f"cache_lookup_batch + all-reduce(min) and cache_load: request r's load (H2D) "
+                                f"overlaps the next requests' saves (D2H)")}
+            st = w.stats()
+        finally:
+            w.unregister()
+            cc.exit()
+        h2d = payload + flat_tok.nbytes + tok_lens.nbytes + 2 * nblk * 8
+        d2h = payload + hashes.nbytes
+        return {"requests_per_step": R, "requests": self.n_req, "payload_bytes_per_rank": payload,
+                "pool_bytes_per_rank": (nrec + 1) * self.rec_bytes, "steps": steps, "warmup": warmup,
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                "sequential": seq, "duplex": dup, "evictions": st["evictions"]}
+
+    # -- the no-allocation entry point on the same shapes ---------------------
+    def noalloc_step(self, steps: int, warmup: int) -> dict:
+        """kv_copy_noalloc (host arrays, static scratch) with KVCOPY_FLAG_BULK:
+        one gather + one scatter of every record per step, records in HBM,
+        CUDA events around each call on the stream it is given; the records
+        must equal kv_copy_launch's and the scatter must reproduce the saved
+        blocks"""
+        import torch
+
+        from demo_b200._lib import KVCOPY_FLAG_BULK, lib
+        dev = self.rk.dev
+        records = torch.empty(self.nrec * self.rec_bytes, dtype=torch.uint8, device=dev)
+        rp = (np.arange(self.nrec, dtype=np.uint64) * np.uint64(self.rec_bytes)) + np.uint64(records.data_ptr())
+        kp, vp = np.asarray(self.kp, np.uint64), np.asarray(self.vp, np.uint64)
+        bs_, bl_ = np.ascontiguousarray(self.bt_save), np.ascontiguousarray(self.bt_load)
+        stream = torch.cuda.Stream(dev)
+
+        def call(bids, direction):
+            return lib.kv_copy_noalloc(self.rk.local, kp.ctypes.data, vp.ctypes.data, rp.ctypes.data,
+                                       bids.ctypes.data, self.nrec, self.n_blocks * BS, self.unit, CHUNK, BS,
+                                       self.n_layers, direction, KVCOPY_FLAG_BULK, C.c_void_p(stream.cuda_stream))
+
+        assert call(bs_, 1) == 0 and call(bl_, 0) == 0
+        ok = all(torch.equal(t[:, torch.from_numpy(bs_.astype(np.int64)).to(dev)].view(torch.int16),
+                             t[:, torch.from_numpy(bl_.astype(np.int64)).to(dev)].view(torch.int16))
+                 for t in self.layers) if self.disjoint else None
+        g_ms, s_ms = [], []
+        for it in range(warmup + steps):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record(stream)
+            assert call(bs_, 1) == 0
+            ev[1].record(stream)
+            assert call(bl_, 0) == 0
+            ev[2].record(stream)
+            torch.cuda.synchronize()
+            if it >= warmup:
+                g_ms.append(ev[0].elapsed_time(ev[1]))
+                s_ms.append(ev[1].elapsed_time(ev[2]))
+        hbm_peak, _ = peaks()
+        moved = 2 * self.payload
+        gms, sms = statistics.median(g_ms), statistics.median(s_ms)
+        del records
+        torch.cuda.empty_cache()
+        return {"gather_gbs": round(moved / (gms / 1e3) / GB, 1), "scatter_gbs": round(moved / (sms / 1e3) / GB, 1),
+                "gather_frac": round(moved / (gms / 1e3) / GB / hbm_peak, 4),
+                "scatter_frac": round(moved / (sms / 1e3) / GB / hbm_peak, 4),
+                "gather_ms": round(gms, 4), "scatter_ms": round(sms, 4), "records": self.nrec,
+                "block_ids": self.nblk, "flags": "KVCOPY_FLAG_BULK", "steps": steps, "warmup": warmup,
+                "verified_bytes": ok,
+                "note": "each call uploads its host arrays into the static scratch, launches, and waits on the "
+                        "host; the time includes the uploads and the wait"}
+
+
+def _sub_line(res: dict, keep: tuple) -> dict:
+    return {k: res[k] for k in keep if k in res}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -897,7 +1562,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--link-seconds", type=float, default=2.0, help="seconds per host-link probe")
+    ap.add_argument("--skip-e2e", action="store_true", help="kernels only (for ncu captures)")
+    ap.add_argument("--no-subs", action="store_true", help="skip the tp70b / prefix-reuse / mla-evict objects")
+    ap.add_argument("--sub-steps", type=int, default=3, help="timed steps of each sub-workload")
+    ap.add_argument("--sub-warmup", type=int, default=2, help="warm-up steps of each sub-workload (the first checked)")
     ap.add_argument("--disk-dir", default=None,
                     help="also time the disk tier in a fresh directory under this path (off by default)")
     ap.add_argument("--disk-requests", type=int, default=8, help="requests of the disk-tier sample")
@@ -905,20 +1574,18 @@ def main() -> None:
                     help="also time a layer-pipelined load against a per-layer compute proxy")
     ap.add_argument("--via-server", action="store_true",
                     help="also time save/load through a CrossCache server process (ZeroMQ + CUDA IPC)")
-    ap.add_argument("--layers", type=int, default=L, help="smaller cases for ncu captures only")
-    ap.add_argument("--requests", type=int, default=REQS)
-    ap.add_argument("--blocks-per-layer", type=int, default=NUM_BLOCKS)
-    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--layers", type=int, default=None, help="smaller cases for ncu captures only")
+    ap.add_argument("--requests", type=int, default=None)
+    ap.add_argument("--blocks-per-layer", type=int, default=None)
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--emulate-tp", type=int, default=1,
+                    help="1 process: rank 0's head shard of a TP split (ncu captures of shard kernels only)")
     ap.add_argument("--workload", default="llama3-8b",
                     choices=["llama3-8b", "tp70b", "prefix-reuse", "mla-evict"],
                     help="llama3-8b: the headline save/load config; tp70b: the Llama-3-70B TP "
                          "config; prefix-reuse and mla-evict: the prefix-reuse and MLA-eviction "
                          "configs (1 GPU)")
     args = ap.parse_args()
-    if args.workload == "tp70b":
-        pr = PRESETS["tp70b"]
-        args.layers, args.requests, args.tokens, args.blocks_per_layer = (
-            pr["layers"], pr["requests"], pr["tokens"], pr["blocks"])
     if args.impl == "reference":
         run_reference_arm(args)
         return
@@ -930,398 +1597,89 @@ def main() -> None:
     import torch.distributed as dist
 
     from demo_b200 import cache as cc
-    from demo_b200._lib import KVCOPY_FLAG_BULK, KvCopyDesc, lib
+    from demo_b200._lib import lib
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
-    if KV_HEADS % world:
-        raise SystemExit("world size must divide 8 KV heads")
+    if world > 1 and args.emulate_tp != 1:
+        raise SystemExit("--emulate-tp is for one process")
+    shards = world if world > 1 else args.emulate_tp
+    if KV_HEADS % shards:
+        raise SystemExit("the TP size must divide 8 KV heads")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def sum_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
-
-    n_layers, n_req, n_blocks, n_tok = args.layers, args.requests, args.blocks_per_layer, args.tokens
-    preset = "tp70b" if args.workload == "tp70b" else "llama3-8b"
-    heads = KV_HEADS // world
-    hidden = heads * HEAD_DIM
-    unit = hidden * ELT
-    bpc = CHUNK // BS
-    nblk = n_req * n_tok // BS                 # 8192 blocks
-    nrec = nblk // bpc                         # 512 records
-    rec_bytes = 2 * n_layers * CHUNK * unit
-    payload = nrec * rec_bytes                 # one direction, this rank
-
-    # paged cache: this rank's head shard of N(0,1) bf16 values (seed 0)
-    g = torch.Generator(device=dev).manual_seed(0)
-    layers = []
-    for _ in range(n_layers):
-        full = torch.randn(2, n_blocks, BS, KV_HEADS, HEAD_DIM, generator=g, device=dev,
-                           dtype=torch.float32).to(torch.bfloat16)
-        layers.append(full[:, :, :, rank * heads:(rank + 1) * heads].contiguous())
-        del full
-    torch.cuda.empty_cache()
-    layout, kp, vp = cc.layout_from_kv_tensors(layers)
-    # block tables: a seeded permutation of free block ids for the save (seed 2).
-    # The reload goes to a fresh seeded permutation (seed 3): of the blocks the
-    # save did not use when the cache holds both tables (then repeated steps
-    # never overwrite a block a later gather reads and the final bytes are
-    # compared exactly), else of all blocks ("the cache was cleared").  Either
-    # way the first step is checked against per-block checksums taken before it.
-    if nblk > n_blocks:
-        raise SystemExit("blocks per layer must hold the saved blocks")
-    perm = torch.randperm(n_blocks, generator=torch.Generator().manual_seed(2))
-    bt_save = perm[:nblk].numpy().astype(np.uint64)
-    disjoint = 2 * nblk <= n_blocks
-    free = perm[nblk:] if disjoint else perm
-    bt_load = free[torch.randperm(free.numel(), generator=torch.Generator().manual_seed(3))][:nblk].numpy().astype(np.uint64)
-    tokens = torch.randint(0, VOCAB, (n_req, n_tok), generator=torch.Generator().manual_seed(1),
-                           dtype=torch.int64).to(torch.int32).numpy()
-
-    def block_sums(idx: "torch.Tensor") -> list:
-        """per (layer, K/V, block) position-weighted int64 checksums of the given blocks"""
-        out = []
-        for t in layers:
-            per = []
-            for kv in range(2):
-                x = t[kv, idx].view(torch.int16).reshape(idx.numel(), -1).to(torch.int64)
-                wgt = (torch.arange(x.shape[1], device=dev, dtype=torch.int64) % 251) + 1
-                per.append(torch.stack([x.sum(1), (x * wgt).sum(1)]))
-                del x
-            out.append(torch.stack(per))
-        return out
-
-    def sums_equal(a: list, b: list) -> bool:
-        return all(torch.equal(x, y) for x, y in zip(a, b))
-
-    # ---------------- value: device-resident records, kernel path ----------
-    kp_d = torch.tensor(kp, dtype=torch.int64, device=dev)
-    vp_d = torch.tensor(vp, dtype=torch.int64, device=dev)
-    # records in HBM: all of them when they fit next to the paged cache, else
-    # in batches that reuse one buffer (each batch = one gather + one scatter)
-    free_b, _ = torch.cuda.mem_get_info(dev)
-    batch = int(max(1, min(nrec, (free_b - (12 << 30)) // rec_bytes)))
-    nbatch = (nrec + batch - 1) // batch
-    records = torch.empty(batch * rec_bytes, dtype=torch.uint8, device=dev)
-    rec_ptrs = torch.arange(batch, dtype=torch.int64, device=dev) * rec_bytes + records.data_ptr()
-    b_save = torch.from_numpy(bt_save.astype(np.int64)).to(dev)
-    b_load = torch.from_numpy(bt_load.astype(np.int64)).to(dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-
-    def desc(bids, first, n, direction):
-        return KvCopyDesc(layer_k=kp_d.data_ptr(), layer_v=vp_d.data_ptr(), records=rec_ptrs.data_ptr(),
-                          slots=None, block_ids=bids.data_ptr() + first * bpc * 8, error=err.data_ptr(),
-                          page_buffer_size=n_blocks * BS, unit_bytes=unit, num_tokens=CHUNK,
-                          block_size=BS, num_layers=n_layers, num_records=n, direction=direction,
-                          flags=KVCOPY_FLAG_BULK)
-
-    batches = [(i * batch, min(batch, nrec - i * batch)) for i in range(nbatch)]
-    d_pairs = [(desc(b_save, f, n, 1), desc(b_load, f, n, 0)) for f, n in batches]
-    assert sum(lib.kv_copy_payload_bytes(C.byref(g)) for g, _ in d_pairs) == payload
-    stream = torch.cuda.Stream(dev)
-    sptr = C.c_void_p(stream.cuda_stream)
-
-    def kernel_step(ev=None):
-        for bi, (dg, ds) in enumerate(d_pairs):
-            if ev:
-                ev[bi][0].record(stream)
-            assert lib.kv_copy_launch(C.byref(dg), sptr) == 0
-            if ev:
-                ev[bi][1].record(stream)
-            assert lib.kv_copy_launch(C.byref(ds), sptr) == 0
-            if ev:
-                ev[bi][2].record(stream)
-
-    sums0 = block_sums(b_save)
-    kernel_step()                      # first step from the pristine cache: checked
-    torch.cuda.synchronize()
-    ok_first = sums_equal(block_sums(b_load), sums0)
-    for _ in range(args.warmup - 1):
-        kernel_step()
-    torch.cuda.synchronize()
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(nbatch)]
-           for _ in range(args.steps)]
-    l0 = lib.crosscache_kernel_launches()
-    barrier()
-    torch.cuda.synchronize()
+    rk = Ranks(world, rank, local, dev, shards, rank if world > 1 else 0)
+    # this rank's share of the host memory free at start (ranks share the host)
+    budget = rk.min(0.6 * _mem_available() / world)
+    hinfo = host_info() if rank == 0 else None
+    over = {k: v for k, v in (("layers", args.layers), ("requests", args.requests),
+                               ("blocks", args.blocks_per_layer), ("tokens", args.tokens)) if v is not None}
+    sub_ok = not args.no_subs and not args.skip_e2e and not over and args.emulate_tp == 1
     clocks = ClockSampler(local).__enter__()
-    if True:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for i in range(args.steps):
-            kernel_step(evs[i])
-        t1.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    launches = lib.crosscache_kernel_launches() - l0
-    dt = max_over_ranks(t0.elapsed_time(t1) / 1e3)
-    # per-step sums over the record batches (one launch each when all records fit)
-    gather_ms = statistics.mean(sum(b[0].elapsed_time(b[1]) for b in e) for e in evs)
-    scatter_ms = statistics.mean(sum(b[1].elapsed_time(b[2]) for b in e) for e in evs)
-    assert int(err.item()) == 0, "kv copy reported an error"
-    # verify: the first step against the pre-step checksums; with disjoint
-    # tables also every byte after the timed steps
-    ok_value = ok_first and (not disjoint or all(
-        torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers))
-    total_payload = sum_over_ranks(2 * payload)
-    value = total_payload * args.steps / dt / GB
-    hbm_peak, peak_kind = peaks()
-    achieved = 2 * payload / (gather_ms / 1e3) / GB       # read + write bytes of the gathers of a step
-    del records
-    torch.cuda.empty_cache()
 
-    # ---------------- block-hash kernel, tokens resident in HBM --------------
-    from demo_b200.hashing import block_hashes_device
-    none_hash_h = __import__("hashlib").sha256(__import__("pickle").dumps("0", protocol=5)).digest()
-    tok_d = torch.from_numpy(tokens.reshape(-1).copy()).to(dev)
-    toff_d = torch.arange(n_req, dtype=torch.int64, device=dev) * n_tok
-    ooff_d = torch.arange(n_req, dtype=torch.int64, device=dev) * (n_tok // BS)
-    nb_d = torch.full((n_req,), n_tok // BS, dtype=torch.int32, device=dev)
-    hout = torch.empty(nblk, 32, dtype=torch.uint8, device=dev)
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            block_hashes_device(tok_d, toff_d, nb_d, ooff_d, BS, none_hash_h, hout, stream=stream)
-        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        h0.record(stream)
-        for _ in range(args.steps):
-            block_hashes_device(tok_d, toff_d, nb_d, ooff_d, BS, none_hash_h, hout, stream=stream)
-        h1.record(stream)
-    torch.cuda.synchronize()
-    hash_ms = h0.elapsed_time(h1) / args.steps
-    hash_info = {"kernel_ms": round(hash_ms, 4), "blocks": nblk, "chains": n_req,
-                 "blocks_per_s": round(nblk / (hash_ms / 1e3), 1),
-                 "sha256_compressions_per_s": round(3 * nblk / (hash_ms / 1e3), 1),
-                 "us_per_block_along_a_chain": round(hash_ms * 1e3 / (n_tok // BS), 3),
-                 "bound": "integer latency along each chain (3 SHA-256 compressions per 16-token block)"}
-
-    # ---------------- e2e: public C API, pinned host pool -------------------
-    e2e = None
-    link = None
-    p50 = None
-    disk = None
-    server = None
-    layerwise = None
-    paged_layouts = None
+    head = Offload(rk, args.workload, over)
+    config = head.config()
+    device = head.device_step(args.steps, args.warmup)
+    block_hash = head.hash_kernel(args.steps, args.warmup)
+    link = e2e = None
+    disk = server = layerwise = paged_layouts = noalloc = prefix = mla = tp70 = None
     if not args.skip_e2e:
-        # host-link peaks measured in this run: pinned 256 MiB cudaMemcpyAsync,
-        # 16 per direction (4 GiB), every rank at once after a barrier -- the
-        # per-GPU link as the e2e steps see it when all ranks copy together
-        hbuf = torch.empty(256 << 20, dtype=torch.uint8, pin_memory=True)
-        dbuf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-        link_peak = {}
-        for name, fn in (("h2d", lambda: dbuf.copy_(hbuf, non_blocking=True)),
-                         ("d2h", lambda: hbuf.copy_(dbuf, non_blocking=True))):
-            for _ in range(2):
-                fn()
-            torch.cuda.synchronize()
-            barrier()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            for _ in range(16):
-                fn()
-            b.record()
-            torch.cuda.synchronize()
-            link_peak[name] = 16 * (256 << 20) / (a.elapsed_time(b) / 1e3) / GB
-        del hbuf, dbuf
-
-        cc.init(CHUNK, (nrec + 1) * rec_bytes, None)
-        w = cc.Worker("llama-3-8b", layout, kp, vp, node_id=local, world_size=world, rank=rank)
-        w.register()
-        from demo_b200._lib import lib as L_
-        from demo_b200.tp import agree_min_hits
-        flat_tok = np.ascontiguousarray(tokens.reshape(-1))
-        tok_lens = np.full(n_req, n_tok, dtype=np.int64)
-        none_hash = __import__("hashlib").sha256(__import__("pickle").dumps("0", protocol=5)).digest()
-        hashes = np.zeros((nblk, 32), dtype=np.uint8)
-        key_nums = np.full(n_req, n_tok // CHUNK, dtype=np.uint32)
-        hits = np.zeros(n_req, dtype=np.uint32)
-        bt_save_c = np.ascontiguousarray(bt_save)
-        per_req_blocks = n_tok // BS
-        load_bids = [np.ascontiguousarray(bt_load[r * per_req_blocks:(r + 1) * per_req_blocks]) for r in range(n_req)]
-
-        def e2e_step(lat: list | None):
-            t_a = time.perf_counter()
-            w.clear()
-            n = L_.kv_block_hash_host(local, flat_tok.ctypes.data, tok_lens.ctypes.data, n_req, BS, none_hash,
-                                      hashes.ctypes.data)
-            assert n == nblk
-            keys = np.ascontiguousarray(hashes[bpc - 1::bpc])              # 512 chunk keys
-            kb = keys.tobytes()
-            t_b = time.perf_counter()
-            ret = L_.cache_store(C.byref(w.ctx), kb, 32, bt_save_c.ctypes.data, nblk)
-            assert ret == 0, ret
-            t_c = time.perf_counter()
-            ret = L_.cache_lookup_batch(C.byref(w.ctx), kb, key_nums.ctypes.data, n_req, 32, hits.ctypes.data)
-            assert ret == 0
-            hit = agree_min_hits(hits, device=dev)       # NCCL all-reduce(min) under TP
-            t_d = time.perf_counter()
-            per_req_keys = n_tok // CHUNK
-            for r in range(n_req):
-                h = int(hit[r])
-                ts = time.perf_counter()
-                kr = kb[r * per_req_keys * 32:(r * per_req_keys + h) * 32]
-                ret = L_.cache_load(C.byref(w.ctx), kr, 32, load_bids[r].ctypes.data, h * bpc)
-                assert ret == 0, ret
-                if lat is not None:
-                    lat.append(time.perf_counter() - ts)
-            t_e = time.perf_counter()
-            return t_b - t_a, t_c - t_b, t_e - t_d, int(hit.sum()), t_d - t_c
-
-        if disjoint:
-            for t in layers:   # the exact final check needs the destination blocks empty
-                t[:, b_load] = 0
-        sums1 = block_sums(b_save)
-        e2e_step(None)         # checked first step
-        torch.cuda.synchronize()
-        ok_e2e_first = sums_equal(block_sums(b_load), sums1)
-        del sums1
-        for _ in range(args.warmup - 1):
-            e2e_step(None)
-        lat: list[float] = []
-        parts = []
-        l1 = lib.crosscache_kernel_launches()
-        barrier()
-        torch.cuda.synchronize()
-        ts0 = time.perf_counter()
-        for _ in range(args.steps):
-            parts.append(e2e_step(lat))
-        torch.cuda.synchronize()
-        te = max_over_ranks(time.perf_counter() - ts0)
-        barrier()
-        e2e_launches = lib.crosscache_kernel_launches() - l1
-        ok_e2e = ok_e2e_first and (not disjoint or all(
-            torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16)) for t in layers))
-
-        # duplex: request r's load (H2D) overlaps request r+1's save (D2H), the
-        # two running on separate adaptor lanes from two host threads -- the
-        # cache serving stores and loads at once, as the reference's separate
-        # store and load thread pools do.  Needs disjoint block tables.
-        duplex = None
-        if world == 1 and disjoint:
-            import threading
-            per_req_keys = n_tok // CHUNK
-            save_bids = [np.ascontiguousarray(bt_save[r * per_req_blocks:(r + 1) * per_req_blocks])
-                         for r in range(n_req)]
-
-            def duplex_step(dlat):
-                w.clear()
-                n = L_.kv_block_hash_host(local, flat_tok.ctypes.data, tok_lens.ctypes.data, n_req, BS,
-                                          none_hash, hashes.ctypes.data)
-                assert n == nblk
-                kb = np.ascontiguousarray(hashes[bpc - 1::bpc]).tobytes()
-                ready = [threading.Event() for _ in range(n_req)]
-                errs = []
-
-                def saver():
-                    for r in range(n_req):
-                        kr = kb[r * per_req_keys * 32:(r + 1) * per_req_keys * 32]
-                        ret = L_.cache_store(C.byref(w.ctx), kr, 32, save_bids[r].ctypes.data, per_req_blocks)
-                        if ret:
-                            errs.append(ret)
-                        ready[r].set()
-                th = threading.Thread(target=saver)
-                th.start()
-                for r in range(n_req):
-                    ready[r].wait()
-                    kr = kb[r * per_req_keys * 32:(r + 1) * per_req_keys * 32]
-                    h = L_.cache_lookup(C.byref(w.ctx), kr, per_req_keys, 32) // 32
-                    ts = time.perf_counter()
-                    ret = L_.cache_load(C.byref(w.ctx), kr[: h * 32], 32, load_bids[r].ctypes.data, h * bpc)
-                    if ret:
-                        errs.append(ret)
-                    if dlat is not None:
-                        dlat.append(time.perf_counter() - ts)
-                th.join()
-                assert not errs, errs
-
-            for t in layers:
-                t[:, b_load] = 0
-            duplex_step(None)
-            torch.cuda.synchronize()
-            ok_dup = all(torch.equal(t[:, b_save].view(torch.int16), t[:, b_load].view(torch.int16))
-                         for t in layers)
-            for _ in range(args.warmup - 1):
-                duplex_step(None)
-            dlat: list[float] = []
-            td0 = time.perf_counter()
-            for _ in range(args.steps):
-                duplex_step(dlat)
-            td = time.perf_counter() - td0
-            duplex = {"value": round(2 * payload * args.steps / td / GB, 3), "unit": "GB/s",
-                      "ms_per_step": round(td / args.steps * 1e3, 3),
-                      "p50_load_latency_ms": round(statistics.median(dlat) * 1e3, 3),
-                      "verified_bytes": bool(ok_dup),
-                      "note": "same steps as e2e (hash, store every request, look up and load every "
-                              "request) with the load of request r overlapping the save of request r+1"}
-        st = w.stats()
-        w.unregister()
-        cc.exit()
+        link = link_probe(rk, args.link_seconds)
+        e2e = head.e2e(args.steps, args.warmup, budget)
+    s = dict(dev=dev, nrec=head.nrec, rec_bytes=head.rec_bytes, bpc=head.bpc, n_blocks=head.n_blocks,
+             unit=head.unit, disjoint=head.disjoint, local=local, world=world, rank=rank, n_req=head.n_req,
+             n_tok=head.n_tok, per_req_blocks=head.prb, payload=head.payload)
+    if world == 1 and args.emulate_tp == 1:
+        b_save = torch.from_numpy(head.bt_save.astype(np.int64)).to(dev)
+        b_load = torch.from_numpy(head.bt_load.astype(np.int64)).to(dev)
+        paged_layouts = _paged_layout_probe(args, head.layers, b_save, b_load, s)
+        del b_save, b_load
+        if not over:
+            noalloc = head.noalloc_step(args.steps, args.warmup)
+    if not args.skip_e2e and (args.disk_dir or args.layerwise or args.via_server):
+        hashes = np.zeros((head.nblk, 32), dtype=np.uint8)
+        n = lib.kv_block_hash_host(local, np.ascontiguousarray(head.tokens.reshape(-1)).ctypes.data,
+                                   np.full(head.n_req, head.n_tok, dtype=np.int64).ctypes.data, head.n_req, BS,
+                                   _sha_none(), hashes.ctypes.data)
+        assert n == head.nblk
         if args.disk_dir:
-            disk = _disk_tier_probe(args, cc, L_, layers, layout, kp, vp, hashes, bt_save, bt_load, disjoint,
-                                    dict(local=local, world=world, rank=rank, n_req=n_req, n_tok=n_tok,
-                                         bpc=bpc, per_req_blocks=per_req_blocks, nrec=nrec,
-                                         rec_bytes=rec_bytes, dev=dev))
+            disk = _disk_tier_probe(args, cc, lib, head.layers, head.layout, head.kp, head.vp, hashes, head.bt_save,
+                                    head.bt_load, head.disjoint, s)
         if args.layerwise and world == 1:
-            layerwise = _layerwise_probe(args, cc, layers, layout, kp, vp, hashes, bt_save, bt_load,
-                                         dict(n_tok=n_tok, bpc=bpc, per_req_blocks=per_req_blocks,
-                                              rec_bytes=rec_bytes, dev=dev, local=local))
+            layerwise = _layerwise_probe(args, cc, head.layers, head.layout, head.kp, head.vp, hashes,
+                                         head.bt_save, head.bt_load, s)
         if args.via_server and world == 1:
-            server = _server_probe(args, layers, hashes, bt_save, bt_load, disjoint,
-                                   dict(n_req=n_req, n_tok=n_tok, bpc=bpc, per_req_blocks=per_req_blocks,
-                                        nrec=nrec, rec_bytes=rec_bytes, payload=payload, dev=dev))
-        hit_blocks = parts[-1][3] * bpc
-        save_s = max_over_ranks(statistics.median(p[1] for p in parts))
-        load_s = max_over_ranks(statistics.median(p[2] for p in parts))
-        hash_s = max_over_ranks(statistics.median(p[0] for p in parts))
-        agree_s = max_over_ranks(statistics.median(p[4] for p in parts))
-        p50 = max_over_ranks(statistics.median(lat)) * 1e3
-        e2e_value = total_payload * args.steps / te / GB
-        h2d = payload + flat_tok.nbytes + tok_lens.nbytes + nblk * 8
-        d2h = payload + hashes.nbytes
-        e2e = {"value": round(e2e_value, 3), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h), "ms_per_step": round(te / args.steps * 1e3, 3),
-               "save_gbs_per_gpu": round(payload / save_s / GB, 3),
-               "load_gbs_per_gpu": round(payload / load_s / GB, 3),
-               "hash_ms": round(hash_s * 1e3, 3), "lookup_agree_ms": round(agree_s * 1e3, 3),
-               "p50_load_latency_ms": round(p50, 3),
-               "p90_load_latency_ms": round(float(np.percentile(lat, 90)) * 1e3, 3),
-               "hit_blocks_per_request": hit_blocks // n_req, "gpu_launches": int(e2e_launches),
-               "verified_bytes": bool(ok_e2e), "evictions": st["evictions"], "duplex": duplex}
-        link = {"d2h_peak_gbs": round(link_peak["d2h"], 2), "h2d_peak_gbs": round(link_peak["h2d"], 2),
-                "save_frac": round(payload / save_s / GB / link_peak["d2h"], 4),
-                "load_frac": round(payload / load_s / GB / link_peak["h2d"], 4),
-                "note": "per GPU; pinned cudaMemcpyAsync, 4 GiB per direction, all ranks at once, this run"}
-
-    if world == 1:
-        paged_layouts = _paged_layout_probe(args, layers, b_save, b_load,
-                                            dict(dev=dev, nrec=nrec, rec_bytes=rec_bytes, bpc=bpc,
-                                                 n_blocks=n_blocks, unit=unit, disjoint=disjoint))
+            server = _server_probe(args, head.layers, hashes, head.bt_save, head.bt_load, head.disjoint, s)
+    if sub_ok and world == 1 and args.workload == "llama3-8b":
+        prefix = _sub_line(_prefix_reuse(dev, cc, lib, args.sub_steps, args.sub_warmup, layers=head.layers),
+                           ("value", "unit", "workload", "steps", "warmup", "ms_per_step", "hit_blocks_per_request",
+                            "hit_rate_chunks", "records_stored_per_step", "store_keys_deduplicated_per_step",
+                            "save_gbs", "load_gbs", "p50_load_latency_ms", "verified_bytes"))
+    head.free()
+    del head
+    if sub_ok and world == 1:
+        from oracle.cache_model import LRUPool     # host-side LRU model: the checker only
+        mla = _sub_line(_mla_evict(dev, cc, lib, LRUPool, args.sub_steps, args.sub_warmup),
+                        ("value", "unit", "workload", "steps", "warmup", "ms_per_step", "pool_records",
+                         "working_set_records", "hit_rate_chunks", "evictions_per_pass", "hits_per_pass",
+                         "lru_model_hits", "lru_model_evictions", "hits_match_model", "evictions_match_model",
+                         "save_gbs", "load_gbs", "p50_load_latency_ms", "loaded_block_mismatches",
+                         "verified_bytes"))
+    if sub_ok and args.workload == "llama3-8b":
+        big = Offload(rk, "tp70b")
+        tp70 = {"config": big.config(), "device": big.device_step(args.sub_steps, args.sub_warmup),
+                "e2e": big.e2e(args.sub_steps, args.sub_warmup, budget)}
+        big.free()
+        del big
     clocks.__exit__(None, None, None)
     cpu = None
-    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+    if rank == 0 and world == 1 and args.cpu_seconds > 0 and args.emulate_tp == 1:
         cpu = cpu_sample_run("port", args.cpu_seconds, None, os.cpu_count() or 1)
         cpu.pop("times_s", None)
         # the reference's own concurrency: 4 CaCopy threads (src/cache/cache.c:777)
@@ -1329,34 +1687,58 @@ def main() -> None:
         cpu["value_4_threads"] = round(four["value"], 3)
         cpu["cpu_model"] = _cpu_model()
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
-            "data": "synthetic (seeded N(0,1) bf16 KV, uniform token ids, random block tables)",
-            "config": workload_config(world, preset) if (n_layers, n_req, n_blocks, n_tok) == tuple(
-                PRESETS[preset][k] for k in ("layers", "requests", "blocks", "tokens")) else
-            {**workload_config(world, preset, layers=n_layers, requests=n_req, blocks=n_blocks, tokens=n_tok),
-             "workload": f"reduced case for profiling: {n_layers} layers, {n_req} requests x {n_tok} tokens, "
-                         f"{n_blocks} blocks/layer"},
-            "record_batches_per_step": nbatch,
-            "roofline": {"bound": "hbm",
-                         "kernel": ("kv_copy_kernel gather (16-byte register copies)" if kvcopy_path() == "lsu"
-                                    else "kv_copy_bulk_kernel gather (TMA cp.async.bulk via shared memory)"),
-                         "achieved": round(achieved, 1),
-                         "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                         "peak_kind": peak_kind, "traffic": ncu_traffic(2 * min(batch, nrec) * rec_bytes),
-                         "algorithmic_bytes_per_launch": 2 * min(batch, nrec) * rec_bytes,
-                         "gather_ms": round(gather_ms, 4), "scatter_ms": round(scatter_ms, 4),
-                         "scatter_frac": round(2 * payload / (scatter_ms / 1e3) / GB / hbm_peak, 4)},
-            "e2e": e2e, "link": link, "p50_load_latency_ms": round(p50, 3) if p50 is not None else None,
-            "block_hash": hash_info, "disk_tier": disk, "via_server": server, "layerwise": layerwise,
-            "paged_layouts": paged_layouts,
-            "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": clocks.summary(),
-            "verified_bytes": bool(ok_value),
-        }
-        print(json.dumps(line), flush=True)
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    dup = e2e.get("duplex") if e2e and "skipped" not in e2e else None
+    seq = e2e.get("sequential") if e2e and "skipped" not in e2e else None
+    head_e2e = dup or seq
+    if link and head_e2e:
+        if seq:
+            seq["save_frac_of_link"] = round(seq["save_gbs_aggregate"] / link["d2h"]["aggregate"], 4)
+            seq["load_frac_of_link"] = round(seq["load_gbs_aggregate"] / link["h2d"]["aggregate"], 4)
+        if dup:
+            dup["frac_of_link_both_directions"] = round(dup["value"] / link["both"]["aggregate"], 4)
+    if tp70 and link and "skipped" not in tp70["e2e"]:
+        t_seq, t_dup = tp70["e2e"]["sequential"], tp70["e2e"]["duplex"]
+        t_seq["save_frac_of_link"] = round(t_seq["save_gbs_aggregate"] / link["d2h"]["aggregate"], 4)
+        t_seq["load_frac_of_link"] = round(t_seq["load_gbs_aggregate"] / link["h2d"]["aggregate"], 4)
+        if t_dup:
+            t_dup["frac_of_link_both_directions"] = round(t_dup["value"] / link["both"]["aggregate"], 4)
+    if head_e2e:
+        value, ms = head_e2e["value"], head_e2e["ms_per_step"]
+        launches, p50 = head_e2e["gpu_launches"], head_e2e["p50_load_latency_ms"]
+        e2e_line = {"value": value, "unit": "GB/s", "mode": "duplex" if dup else "sequential",
+                    "h2d_bytes_per_step": e2e["h2d_bytes_per_step"], "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
+                    "bytes_note": "per rank per step: KV payload + token ids + block tables up, payload + block "
+                                  "hashes down",
+                    "ms_per_step": ms, "p50_load_latency_ms": p50,
+                    "requests_per_step": e2e["requests_per_step"], "verified_bytes": head_e2e["verified_bytes"]}
+    else:
+        value, ms, launches, p50 = device["value"], device["ms_per_step"], device["launches"], None
+        e2e_line = e2e
+    verified = [device["verified_bytes"]] + [x["verified_bytes"] for x in (seq, dup) if x]
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (seeded N(0,1) bf16 KV, uniform token ids, random block tables)",
+        "config": config,
+        "value_kind": ("save+load payload through cache_store / cache_load, KV in HBM <-> pinned host pool, "
+                       f"{'duplex' if dup else 'sequential'} step" if head_e2e else "device kernels only"),
+        "e2e": e2e_line, "sequential": seq, "duplex": dup, "link": link,
+        "p50_load_latency_ms": p50, "device": device, "roofline": device["roofline"],
+        "block_hash": block_hash, "tp70b": tp70, "prefix_reuse": prefix, "mla_evict": mla,
+        "noalloc": noalloc, "paged_layouts": paged_layouts,
+        "disk_tier": disk, "via_server": server, "layerwise": layerwise,
+        "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": clocks.summary(), "host": hinfo,
+        "pool_budget_gib_per_rank": round(budget / 2**30, 1),
+        "verified_bytes": all(verified),
+    }
+    if args.emulate_tp != 1:
+        config["workload"] += f" (1 process emulating rank 0 of TP={args.emulate_tp})"
+    print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 

@@ -19,6 +19,8 @@ KVCOPY_ERR_NULL_LAYER = 0x2
 KVCOPY_ERR_TIMEOUT = 0x4
 KVCOPY_ERR_ALIGN = 0x8
 KVCOPY_FLAG_BULK = 0x1
+KVCOPY_FLAG_TEST_STALL = 0x100
+KVCOPY_PATH_REGISTER, KVCOPY_PATH_BULK, KVCOPY_PATH_BULK_HND = 1, 2, 3
 KVHASH_MAX_BLOCK_SIZE = 8192
 KVHASH_ALGOS = {"sha256": 0, "sha256_cbor": 1}
 
@@ -186,9 +188,10 @@ SIGNATURES: dict[str, tuple] = {
     # include/kvcopy.h
     "kv_copy_launch": (C.c_int, [C.POINTER(KvCopyDesc), C.c_void_p]),
     "kv_copy_payload_bytes": (C.c_uint64, [C.POINTER(KvCopyDesc)]),
+    "kv_copy_path": (C.c_int, [C.POINTER(KvCopyDesc)]),
     "kv_copy_noalloc": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32,
                                   C.c_uint64, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int32,
-                                  C.c_void_p]),
+                                  C.c_uint32, C.c_void_p]),
     # include/kvhash.h
     "kv_block_hash_launch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                        C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p]),

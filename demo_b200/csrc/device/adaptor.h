@@ -38,4 +38,9 @@ public:
 /* launches of this library's kernels (all devices) */
 extern std::atomic<uint64_t> g_cc_kernel_launches;
 
+/* Load the code of every kv_copy kernel onto the current device (modules load
+ * lazily by default, so a kernel's first launch would otherwise be the moment
+ * the driver places it in device memory); 0 or -EIO.  kv_copy.cu. */
+int kv_copy_preload(void);
+
 #endif

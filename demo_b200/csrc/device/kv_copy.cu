@@ -327,6 +327,7 @@ static_assert(kBulkStages >= 2 && (uint64_t)kBulkStages * kBulkTileBytes <= 227u
               "bulk ring must fit the 227 KiB of shared memory a CTA can have");
 static_assert(kBulkTileBytes % 16 == 0, "bulk copies move multiples of 16 bytes");
 constexpr uint32_t kBulkSpinLimit = 1u << 24;   /* polls of ~128 ns back-off: ~2 s */
+constexpr uint32_t kStallSpinLimit = 1u << 14;  /* fault-detection test: a few ms */
 
 struct BulkParams {
     const uint64_t *layer_k;
@@ -346,6 +347,8 @@ struct BulkParams {
     uint32_t layer0;            /* first record layer this launch copies */
     uint32_t rec_layers;        /* layers a record holds */
     uint32_t max_grid;          /* CTA cap, 0 = none */
+    uint32_t spin_limit;        /* polls of one bounded mbarrier wait */
+    uint32_t stall;             /* KVCOPY_FLAG_TEST_STALL: CTA 0's first tile never completes */
     FastDiv div_tpl, div_layers, div_kv;
     /* head-major blocks, in 16-byte vectors: hv per head piece of a token,
      * tv = block_size * hv per head, vpb = heads * tv per block */
@@ -384,15 +387,40 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
-__device__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity)
+/* poll until the phase of `parity` completes, at most `budget` polls; the
+ * polls used are taken off `budget`, so a caller can spread one budget over
+ * several waits */
+__device__ bool mbar_wait_budget(uint64_t *bar, uint32_t parity, uint32_t &budget)
 {
-    for (uint32_t i = 0; i < kBulkSpinLimit; i++) {
+    for (uint32_t i = 0;; i++) {
         if (mbar_try_wait(bar, parity))
             return true;
+        if (budget == 0)
+            return false;
+        budget--;
         if (i > 32)
             __nanosleep(128);
     }
-    return false;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t limit)
+{
+    uint32_t budget = limit;
+    return mbar_wait_budget(bar, parity, budget);
+}
+
+/* After a wait on tile k ran out: wait, with one shared budget, for every
+ * load still in flight -- tiles k+1 .. issued-1 first, then tile k itself --
+ * so the CTA does not leave while a bulk copy may still write its shared
+ * memory.  A load that has not landed within the budget is given up on
+ * (the kernel must return: a GPU that never answers is worse than a CTA
+ * that exits with a copy outstanding). */
+__device__ void drain_after_timeout(uint64_t *bars, int stages, uint32_t k, uint32_t issued, uint32_t limit)
+{
+    uint32_t budget = limit;
+    for (uint32_t j = k + 1; j < issued; j++)
+        mbar_wait_budget(&bars[j % stages], (j / stages) & 1, budget);
+    mbar_wait_budget(&bars[k % stages], (k / stages) & 1, budget);
 }
 
 __device__ __forceinline__ void bulk_g2s(void *sdst, const void *gsrc, uint32_t bytes, uint64_t *bar)
@@ -505,6 +533,12 @@ __global__ void __launch_bounds__(32, 1) kv_copy_bulk_kernel(const BulkParams p)
     const uint32_t n_my = p.num_tiles > blockIdx.x ? (p.num_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 
     auto issue_load = [&](uint32_t k, int s) {
+        if (p.stall && k == 0 && blockIdx.x == 0) {
+            /* fault-detection test: arm the stage for bytes that are never
+             * issued, so no copy is in flight on it and its wait runs out */
+            mbar_expect_tx(&bars[s], 16);
+            return;
+        }
         bulk_issue_load<TO_RECORD>(p, bulk_decode(p, blockIdx.x + k * gridDim.x),
                                    bulk_smem + (uint32_t)s * kBulkTileBytes, &bars[s]);
     };
@@ -518,11 +552,10 @@ __global__ void __launch_bounds__(32, 1) kv_copy_bulk_kernel(const BulkParams p)
         issue_load(issued, (int)issued);
     for (uint32_t k = 0; k < n_my; k++) {
         const int s = (int)(k % kBulkStages);
-        if (!mbar_wait_bounded(&bars[s], (k / kBulkStages) & 1)) {
+        if (!mbar_wait_bounded(&bars[s], (k / kBulkStages) & 1, p.spin_limit)) {
             if (p.error)
                 atomicOr(p.error, KVCOPY_ERR_TIMEOUT);
-            for (uint32_t j = k + 1; j < issued; j++)       /* loads still in flight */
-                mbar_wait_bounded(&bars[j % kBulkStages], (j / kBulkStages) & 1);
+            drain_after_timeout(bars, kBulkStages, k, issued, p.spin_limit);
             break;
         }
         issue_store(k, s);
@@ -628,21 +661,24 @@ __global__ void __launch_bounds__(kHndThreads, 1) kv_copy_bulk_hnd_kernel(const 
         for (int s = 0; s < kHndStages; s++)
             mbar_init(&bars[s], 1);
         mbar_fence_init();
-        for (; issued < n_my && issued < (uint32_t)kHndStages; issued++)
-            bulk_issue_load<TO_RECORD>(p, bulk_decode(p, blockIdx.x + issued * gridDim.x),
-                                       bulk_smem + issued * kBulkTileBytes, &bars[issued]);
+        for (; issued < n_my && issued < (uint32_t)kHndStages; issued++) {
+            if (p.stall && issued == 0 && blockIdx.x == 0)
+                mbar_expect_tx(&bars[0], 16);   /* fault-detection test: never completes */
+            else
+                bulk_issue_load<TO_RECORD>(p, bulk_decode(p, blockIdx.x + issued * gridDim.x),
+                                           bulk_smem + issued * kBulkTileBytes, &bars[issued]);
+        }
     }
     for (uint32_t k = 0; k < n_my; k++) {
         const uint32_t s = k % kHndStages;
         uint8_t *const stage = bulk_smem + s * kBulkTileBytes;
         uint8_t *const buf = tbuf + (k & 1) * kBulkTileBytes;
         if (leader) {
-            bool ok = mbar_wait_bounded(&bars[s], (k / kHndStages) & 1);
+            bool ok = mbar_wait_bounded(&bars[s], (k / kHndStages) & 1, p.spin_limit);
             if (!ok) {
                 if (p.error)
                     atomicOr(p.error, KVCOPY_ERR_TIMEOUT);
-                for (uint32_t j = k + 1; j < issued; j++)   /* loads still in flight */
-                    mbar_wait_bounded(&bars[j % kHndStages], (j / kHndStages) & 1);
+                drain_after_timeout(bars, kHndStages, k, issued, p.spin_limit);
             }
             if (k >= 2)
                 bulk_wait_read1();      /* tile k-2's store has read buf */
@@ -738,6 +774,53 @@ bool bulk_allowed_by_env()
     return v == 1;
 }
 
+/* cudaFuncGetAttributes of every instantiation of kernel K: with lazy module
+ * loading (the default since CUDA 12.2) this is what makes the driver load
+ * the kernel's code onto the current device */
+template <int VEC, bool TO_RECORD, bool HND>
+bool preload_register_kernels()
+{
+    cudaFuncAttributes a;
+    return cudaFuncGetAttributes(&a, kv_copy_kernel<VEC, TO_RECORD, HND, WideShape>) == cudaSuccess &&
+           cudaFuncGetAttributes(&a, kv_copy_kernel<VEC, TO_RECORD, HND, NarrowShape>) == cudaSuccess;
+}
+
+template <bool TO_RECORD, bool HND>
+bool preload_all_vecs()
+{
+    return preload_register_kernels<16, TO_RECORD, HND>() && preload_register_kernels<8, TO_RECORD, HND>() &&
+           preload_register_kernels<4, TO_RECORD, HND>() && preload_register_kernels<2, TO_RECORD, HND>() &&
+           preload_register_kernels<1, TO_RECORD, HND>();
+}
+
+/* which kernel a descriptor runs: KVCOPY_PATH_*, or -EINVAL for a
+ * malformed descriptor (the checks kv_copy_launch makes before launching) */
+int select_path(const struct kv_copy_desc *d)
+{
+    if (!d || !d->layer_k || !d->records || !d->unit_bytes || !d->num_tokens ||
+        !d->num_layers || !d->block_size)
+        return -EINVAL;
+    if (d->flags & ~(uint32_t)(KVCOPY_FLAG_BULK | KVCOPY_FLAG_TEST_STALL))
+        return -EINVAL;
+    if (!d->slots && (!d->block_ids || d->num_tokens % d->block_size))
+        return -EINVAL;
+    const uint32_t rec_layers = d->record_layers ? d->record_layers : d->num_layers;
+    if ((uint64_t)d->layer_begin + d->num_layers > rec_layers)
+        return -EINVAL;
+    const uint64_t run_bytes = (uint64_t)d->block_size * d->unit_bytes;
+    const uint64_t block_stride = d->block_stride ? d->block_stride : run_bytes;
+    const bool dense = block_stride == run_bytes && !d->head_bytes;
+    if (block_stride < run_bytes || (d->head_bytes && d->unit_bytes % d->head_bytes))
+        return -EINVAL;
+    if (!dense && d->slots && d->page_buffer_size >= (1ull << 32))
+        return -EINVAL;
+    if ((d->flags & KVCOPY_FLAG_BULK) && !d->slots && d->head_bytes % 16 == 0 && d->unit_bytes % 16 == 0 &&
+        block_stride % 16 == 0 && run_bytes >= kBulkMinRunBytes && run_bytes <= kBulkTileBytes &&
+        d->page_buffer_size % d->block_size == 0 && bulk_allowed_by_env())
+        return d->head_bytes ? KVCOPY_PATH_BULK_HND : KVCOPY_PATH_BULK;
+    return KVCOPY_PATH_REGISTER;
+}
+
 }  // namespace
 
 extern "C" uint64_t kv_copy_payload_bytes(const struct kv_copy_desc *d)
@@ -748,18 +831,41 @@ extern "C" uint64_t kv_copy_payload_bytes(const struct kv_copy_desc *d)
            (uint64_t)d->unit_bytes * d->num_records;
 }
 
+extern "C" int kv_copy_path(const struct kv_copy_desc *d)
+{
+    return select_path(d);
+}
+
+int kv_copy_preload(void)
+{
+    if (!preload_all_vecs<true, false>() || !preload_all_vecs<false, false>() ||
+        !preload_all_vecs<true, true>() || !preload_all_vecs<false, true>())
+        return -EIO;
+    cudaFuncAttributes a;
+    const int smem = kBulkStages * (int)kBulkTileBytes;
+    const int smem_hnd = (kHndStages + 2) * (int)kBulkTileBytes;
+    if (cudaFuncGetAttributes(&a, kv_copy_bulk_kernel<true>) != cudaSuccess ||
+        cudaFuncGetAttributes(&a, kv_copy_bulk_kernel<false>) != cudaSuccess ||
+        cudaFuncGetAttributes(&a, kv_copy_bulk_hnd_kernel<true>) != cudaSuccess ||
+        cudaFuncGetAttributes(&a, kv_copy_bulk_hnd_kernel<false>) != cudaSuccess ||
+        cudaFuncSetAttribute(kv_copy_bulk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ||
+        cudaFuncSetAttribute(kv_copy_bulk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ||
+        cudaFuncSetAttribute(kv_copy_bulk_hnd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_hnd) ||
+        cudaFuncSetAttribute(kv_copy_bulk_hnd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_hnd))
+        return -EIO;
+    return 0;
+}
+
 extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
 {
-    if (!d || !d->layer_k || !d->records || !d->unit_bytes || !d->num_tokens ||
-        !d->num_layers || !d->block_size)
-        return -EINVAL;
+    const int path = select_path(d);
+    if (path < 0)
+        return path;
     if (!d->num_records)
         return 0;
-    if (!d->slots && (!d->block_ids || d->num_tokens % d->block_size))
-        return -EINVAL;
     const uint32_t rec_layers = d->record_layers ? d->record_layers : d->num_layers;
-    if ((uint64_t)d->layer_begin + d->num_layers > rec_layers)
-        return -EINVAL;
     /* the layer pointer arrays are indexed from the first layer copied */
     const uint64_t *lk = d->layer_k + d->layer_begin;
     const uint64_t *lv = d->layer_v ? d->layer_v + d->layer_begin : nullptr;
@@ -767,14 +873,11 @@ extern "C" int kv_copy_launch(const struct kv_copy_desc *d, void *stream)
     const uint64_t run_bytes = (uint64_t)d->block_size * d->unit_bytes;
     const uint64_t block_stride = d->block_stride ? d->block_stride : run_bytes;
     const bool dense = block_stride == run_bytes && !d->head_bytes;
-    if (block_stride < run_bytes || (d->head_bytes && d->unit_bytes % d->head_bytes))
-        return -EINVAL;
-    if (!dense && d->slots && d->page_buffer_size >= (1ull << 32))
-        return -EINVAL;
-    if ((d->flags & KVCOPY_FLAG_BULK) && !d->slots && d->head_bytes % 16 == 0 && d->unit_bytes % 16 == 0 &&
-        block_stride % 16 == 0 && run_bytes >= kBulkMinRunBytes && run_bytes <= kBulkTileBytes &&
-        d->page_buffer_size % d->block_size == 0 && bulk_allowed_by_env()) {
+    if (path != KVCOPY_PATH_REGISTER) {
         BulkParams bp{};
+        const bool stall = (d->flags & KVCOPY_FLAG_TEST_STALL) != 0;
+        bp.spin_limit = stall ? kStallSpinLimit : kBulkSpinLimit;
+        bp.stall = stall ? 1 : 0;
         bp.layer_k = lk;
         bp.layer_v = lv;
         bp.layer0 = d->layer_begin;

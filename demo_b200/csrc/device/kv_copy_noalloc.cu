@@ -14,14 +14,22 @@
  * How: the per-call metadata the kernel reads (layer bases, record addresses,
  * block ids) and its error word live in one file-scope
  * `static __device__ __align__(256)` array of fixed size (about 548 KiB,
- * limits below), which every GPU that loads the library holds until the
- * process exits.  Host code cannot use the array's name as a device address
- * (it is a host-side stand-in: a kernel given it faults or, where the GPU can
- * reach host memory, silently uses the wrong memory), so the first call on a
- * device looks up the array's device address with cudaGetSymbolAddress, with
- * that device current, and caches it; that first call should therefore come
- * before any stream capture.  Records must already be device-accessible
- * (HBM, or the mapped alias of pinned host memory): no staging is used.
+ * limits below), which every GPU that sets the entry point up holds until
+ * the process exits.  Host code cannot use the array's name as a device
+ * address (it is a host-side stand-in: a kernel given it faults or, where the
+ * GPU can reach host memory, silently uses the wrong memory), so the set-up
+ * looks up the array's device address with cudaGetSymbolAddress, with that
+ * device current, and keeps it.  CUDA loads modules lazily by default: the
+ * driver places the array, and each kernel's code, in device memory when
+ * they are first used.  The set-up therefore also loads every kv_copy kernel
+ * (cudaFuncGetAttributes), so that after it no call of this entry point
+ * makes the driver allocate either.  The set-up runs on the first call on a
+ * device; a call with num_records == 0 does only the set-up.  Make that call
+ * at start-up -- before the engine hands its free HBM to the KV cache, and
+ * before any stream capture.  A set-up that failed (for instance for lack
+ * of device memory) is not remembered: the next call tries again.  Records
+ * must already be device-accessible (HBM, or the mapped alias of pinned host
+ * memory): no staging is used.
  *
  * Every call shares the array, which keeps the last call's contents; each
  * call clears the error word before its launch.  Calls that overlap on the
@@ -67,39 +75,48 @@ constexpr size_t kWords = kOffErr + 1;
 static __device__ __align__(256) uint64_t g_noalloc_scratch[kWords];
 
 struct DeviceScratch {
-    std::once_flag once;
-    std::mutex mu;
+    std::mutex mu;       /* serialises calls on the device (they share the array) */
     uint64_t *ptr = nullptr;
-    cudaError_t err = cudaSuccess;
+    bool ready = false;
 };
 
 DeviceScratch g_scratch[64];
 
-/* device address of the scratch array on `dev` (which must be current) */
-uint64_t *scratch_of(int dev)
+/* the set-up of `dev` (which must be current), under s.mu: the array's
+ * device address, and every kv_copy kernel loaded onto the device */
+uint64_t *setup_locked(int dev)
 {
     DeviceScratch &s = g_scratch[dev];
-    std::call_once(s.once, [&] {
-        void *p = nullptr;
-        s.err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        s.ptr = static_cast<uint64_t *>(p);
-        if (s.err != cudaSuccess)
-            log_error("kv_copy_noalloc: cudaGetSymbolAddress on device %d failed: %s", dev,
-                      cudaGetErrorString(s.err));
-    });
-    return s.err == cudaSuccess ? s.ptr : nullptr;
+    if (s.ready)
+        return s.ptr;
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+        log_error("kv_copy_noalloc: cudaGetSymbolAddress on device %d failed: %s", dev, cudaGetErrorString(e));
+        return nullptr;
+    }
+    if (kv_copy_preload() != 0) {
+        log_error("kv_copy_noalloc: loading the kv_copy kernels on device %d failed: %s", dev,
+                  cudaGetErrorString(cudaGetLastError()));
+        return nullptr;
+    }
+    s.ptr = static_cast<uint64_t *>(p);
+    s.ready = true;
+    return s.ptr;
 }
 
 int run(int device, const uint64_t *layer_k, const uint64_t *layer_v, const uint64_t *records,
         const uint64_t *block_ids, uint32_t num_records, uint64_t page_buffer_size,
         uint32_t unit_bytes, uint32_t num_tokens, uint32_t block_size, uint32_t num_layers,
-        int32_t direction, cudaStream_t stream)
+        int32_t direction, uint32_t flags, cudaStream_t stream)
 {
-    uint64_t *scr = scratch_of(device);
+    std::lock_guard<std::mutex> lk(g_scratch[device].mu);
+    uint64_t *scr = setup_locked(device);
     if (!scr)
         return -EIO;
+    if (!num_records)
+        return 0;                                   /* set-up only */
     const uint64_t nblk = (uint64_t)num_records * (num_tokens / block_size);
-    std::lock_guard<std::mutex> lk(g_scratch[device].mu);
     if (cudaMemcpyAsync(scr + kOffK, layer_k, num_layers * 8ull, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
         (layer_v && cudaMemcpyAsync(scr + kOffV, layer_v, num_layers * 8ull, cudaMemcpyHostToDevice, stream) != cudaSuccess) ||
         cudaMemcpyAsync(scr + kOffRec, records, num_records * 8ull, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
@@ -121,6 +138,7 @@ int run(int device, const uint64_t *layer_k, const uint64_t *layer_v, const uint
     d.num_layers = num_layers;
     d.num_records = num_records;
     d.direction = direction;
+    d.flags = flags;
     int ret = kv_copy_launch(&d, stream);
     if (ret)
         return ret;
@@ -148,7 +166,7 @@ int run(int device, const uint64_t *layer_k, const uint64_t *layer_v, const uint
         return -EIO;
     if (err) {
         log_error("kv_copy_noalloc: kernel reported error bits 0x%x", err);
-        return -EINVAL;
+        return (err & KVCOPY_ERR_TIMEOUT) ? -ETIMEDOUT : -EINVAL;
     }
     return 0;
 }
@@ -159,25 +177,27 @@ extern "C" int kv_copy_noalloc(int device, const uint64_t *layer_k, const uint64
                                const uint64_t *records, const uint64_t *block_ids,
                                uint32_t num_records, uint64_t page_buffer_size,
                                uint32_t unit_bytes, uint32_t num_tokens, uint32_t block_size,
-                               uint32_t num_layers, int32_t direction, void *stream)
+                               uint32_t num_layers, int32_t direction, uint32_t flags, void *stream)
 {
-    if (device < 0 || device >= 64 || !layer_k || !records || !block_ids || !unit_bytes ||
-        !num_tokens || !block_size || num_tokens % block_size || !num_layers)
+    if (device < 0 || device >= 64)
         return -EINVAL;
-    if (!num_records)
-        return 0;
-    const uint64_t nblk = (uint64_t)num_records * (num_tokens / block_size);
-    if (num_layers > kLayersMax || num_records > kRecordsMax || nblk > kBlocksMax) {
-        log_error("kv_copy_noalloc: request exceeds the static scratch (layers %u > %u, records %u > %u "
-                  "or blocks %lu > %u)", num_layers, kLayersMax, num_records, kRecordsMax,
-                  (unsigned long)nblk, kBlocksMax);
-        return -E2BIG;
+    if (num_records && (!layer_k || !records || !block_ids || !unit_bytes || !num_tokens || !block_size ||
+                        num_tokens % block_size || !num_layers || (flags & ~(uint32_t)KVCOPY_FLAG_BULK)))
+        return -EINVAL;
+    if (num_records) {
+        const uint64_t nblk = (uint64_t)num_records * (num_tokens / block_size);
+        if (num_layers > kLayersMax || num_records > kRecordsMax || nblk > kBlocksMax) {
+            log_error("kv_copy_noalloc: request exceeds the static scratch (layers %u > %u, records %u > %u "
+                      "or blocks %lu > %u)", num_layers, kLayersMax, num_records, kRecordsMax,
+                      (unsigned long)nblk, kBlocksMax);
+            return -E2BIG;
+        }
     }
     int prev = -1;
     if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(device) != cudaSuccess)
         return -EIO;
     int ret = run(device, layer_k, layer_v, records, block_ids, num_records, page_buffer_size,
-                  unit_bytes, num_tokens, block_size, num_layers, direction,
+                  unit_bytes, num_tokens, block_size, num_layers, direction, flags,
                   static_cast<cudaStream_t>(stream));
     cudaSetDevice(prev);
     return ret;

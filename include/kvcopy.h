@@ -46,6 +46,19 @@ extern "C" {
                                        * (cp.async.bulk) staged in shared memory
                                        * (head-major blocks with head_bytes a
                                        * multiple of 16: transposed there too) */
+#define KVCOPY_FLAG_TEST_STALL  0x100 /* fault-detection tests only, bulk path:
+                                       * CTA 0 arms its first stage's mbarrier
+                                       * for 16 bytes it never copies, so that
+                                       * wait runs out after a few ms (no copy
+                                       * is in flight on that stage); the
+                                       * kernel sets KVCOPY_ERR_TIMEOUT, drains
+                                       * its other loads and returns.  The
+                                       * other CTAs copy their tiles. */
+
+/* kv_copy_path() results: the kernel a descriptor selects */
+#define KVCOPY_PATH_REGISTER    1     /* kv_copy_kernel: 16-byte register copies */
+#define KVCOPY_PATH_BULK        2     /* kv_copy_bulk_kernel: cp.async.bulk via shared memory */
+#define KVCOPY_PATH_BULK_HND    3     /* kv_copy_bulk_hnd_kernel: bulk + head-major transpose */
 
 struct kv_copy_desc {
     const uint64_t *layer_k;     /* [num_layers] K layer base addresses      */
@@ -96,6 +109,13 @@ struct kv_copy_desc {
  * page_buffer_size >= 2^32 in slot mode), or -EIO when the launch failed. */
 int kv_copy_launch(const struct kv_copy_desc *desc, void *stream);
 
+/* The kernel kv_copy_launch would run for `desc` (KVCOPY_PATH_*), or -EINVAL
+ * for a descriptor it would reject (including unknown flag bits).  Launches
+ * nothing: lets a caller label its measurements with the path taken (the
+ * bulk path needs KVCOPY_FLAG_BULK, block ids, block runs of 8-32 KiB and
+ * 16-byte multiples; everything else takes the register path). */
+int kv_copy_path(const struct kv_copy_desc *desc);
+
 /* Algorithmic payload of one launch: kv * num_layers * num_tokens * unit_bytes
  * * num_records (each byte is read once and written once). */
 uint64_t kv_copy_payload_bytes(const struct kv_copy_desc *desc);
@@ -107,21 +127,33 @@ uint64_t kv_copy_payload_bytes(const struct kv_copy_desc *desc);
  * this entry point runs the same gather (direction 1) / scatter (0) without
  * calling cudaMalloc, cudaFree or any allocating library routine.  Its scratch
  * (layer bases, record addresses, block ids, error word) is one static device
- * array of about 548 KiB that every GPU loading the library holds until exit;
+ * array of about 548 KiB that every GPU it was set up on holds until exit;
  * requests beyond the limits below return -E2BIG.
  *   layer_k / layer_v  HOST arrays of num_layers layer base addresses
  *                      (layer_v NULL for a K-only cache)
  *   records            HOST array of num_records device-accessible record
  *                      addresses (HBM, or mapped pinned host memory)
  *   block_ids          HOST array, num_tokens / block_size ids per record
+ *   flags              0 or KVCOPY_FLAG_BULK (same meaning as in
+ *                      kv_copy_desc: records and layers in HBM, 16-byte
+ *                      aligned; the TMA bulk kernels then run where the
+ *                      block run allows); other bits are -EINVAL
  * Synchronous on `stream`: returns 0 once the kernel finished, -EINVAL for a
  * bad argument or a block id outside the paged cache, -E2BIG, -ETIMEDOUT
- * (deadline CROSSCACHE_TIMEOUT_MS) or -EIO.  The first call on a device looks
- * up the array's device address (cudaGetSymbolAddress) and must come before
- * any stream capture.  Every call shares the array, which keeps the last
- * call's contents (the error word is cleared per call); calls that overlap on
- * the GPU race -- calls through this entry point in one process are
- * serialised, but one that returned -ETIMEDOUT may still be running. */
+ * (deadline CROSSCACHE_TIMEOUT_MS, or a bulk copy that did not complete) or
+ * -EIO.
+ * Set-up: the first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and loads every kv_copy kernel onto the device.
+ * CUDA loads modules lazily by default, so that is the moment the driver
+ * places the array and the kernels' code in device memory; a call with
+ * num_records == 0 (the pointer arguments may then be NULL) does only this
+ * set-up.  Make it at start-up, before the engine hands its free HBM to the
+ * KV cache, and before any stream capture.  A failed set-up is retried by the
+ * next call.
+ * Every call shares the array, which keeps the last call's contents (the
+ * error word is cleared per call); calls that overlap on the GPU race --
+ * calls through this entry point in one process are serialised, but one that
+ * returned -ETIMEDOUT may still be running. */
 #define KVCOPY_NOALLOC_MAX_LAYERS  256
 #define KVCOPY_NOALLOC_MAX_RECORDS 4096
 #define KVCOPY_NOALLOC_MAX_BLOCKS  65536
@@ -130,7 +162,7 @@ int kv_copy_noalloc(int device, const uint64_t *layer_k, const uint64_t *layer_v
                     const uint64_t *records, const uint64_t *block_ids,
                     uint32_t num_records, uint64_t page_buffer_size, uint32_t unit_bytes,
                     uint32_t num_tokens, uint32_t block_size, uint32_t num_layers,
-                    int32_t direction, void *stream);
+                    int32_t direction, uint32_t flags, void *stream);
 
 #ifdef __cplusplus
 }

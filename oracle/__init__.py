@@ -13,3 +13,16 @@ Nothing in the demo_b200 product package imports this package.
   cache_model.py  prefix lookup (cache.c:712-745) and a deterministic LRU
                   record-pool model
 """
+
+import os as _os
+from pathlib import Path as _Path
+
+REFERENCE_ENV = "CROSSCACHE_REFERENCE"
+
+
+def reference_root() -> _Path:
+    """The CrossCache source tree the checker builds and reads (the reference
+    project's CrossCache/ directory): $CROSSCACHE_REFERENCE, else where this
+    build's container mounts it.  May not exist (it never does on a GPU
+    box): callers check .exists()."""
+    return _Path(_os.environ.get(REFERENCE_ENV, "/root/reference/CrossCache"))

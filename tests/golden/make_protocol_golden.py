@@ -11,12 +11,16 @@ from __future__ import annotations
 
 import importlib.util
 import json
+import sys
 from pathlib import Path
 
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path("/root/reference/CrossCache/python/utils/protocol.py")
+sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+from oracle import reference_root  # noqa: E402
+
+REF = reference_root() / "python" / "utils" / "protocol.py"
 
 
 def load_ref():

@@ -95,7 +95,8 @@ def test_struct_layout_matches_ctypes(tmp_path):
 def test_reference_struct_layout_unchanged(tmp_path):
     """worker_context / transfer_params are laid out exactly like the
     reference headers (compiled against CrossCache's own include/inner_h)."""
-    ref_inc = Path("/root/reference/CrossCache/include/inner_h")
+    from oracle import reference_root
+    ref_inc = reference_root() / "include" / "inner_h"
     if not ref_inc.exists():
         pytest.skip("reference tree not present")
     probe = r"""
