@@ -95,11 +95,13 @@ int wait_event(cudaEvent_t ev, std::chrono::steady_clock::time_point deadline)
 
 struct Lane {
     int dev = -1;
+    int dir = 0;                 /* 1: saves (D2H), 0: loads (H2D) -- a lane serves one direction */
     cudaStream_t ks = nullptr;   /* kernels */
     cudaStream_t cs = nullptr;   /* copy engine */
     cudaEvent_t kdone[kNumSub] = {};
     cudaEvent_t cdone[kNumSub] = {};
     cudaEvent_t fin = nullptr;
+    cudaEvent_t mready = nullptr;  /* metadata uploaded (on cs) before the first kernel */
     uint8_t *staging = nullptr;  /* kNumSub sub-slots of sub_bytes */
     uint64_t sub_bytes = 0;
     uint64_t *d_subrec = nullptr;  /* kNumSub x max_group record pointers */
@@ -123,6 +125,7 @@ struct Lane {
                 !CU_OK(cudaEventCreateWithFlags(&cdone[i], cudaEventDisableTiming)))
                 return false;
         if (!CU_OK(cudaEventCreateWithFlags(&fin, cudaEventDisableTiming)) ||
+            !CU_OK(cudaEventCreateWithFlags(&mready, cudaEventDisableTiming)) ||
             !CU_OK(cudaMalloc(&d_err, sizeof(int32_t))) ||
             !CU_OK(cudaHostAlloc(&h_err, sizeof(int32_t), cudaHostAllocDefault)))
             return false;
@@ -211,6 +214,8 @@ struct Lane {
         }
         if (fin)
             cudaEventDestroy(fin);
+        if (mready)
+            cudaEventDestroy(mready);
         if (staging)
             cudaFree(staging);
         if (d_subrec)
@@ -547,9 +552,10 @@ struct DeviceCtx {
     std::mutex mu;
     std::condition_variable cv;
     std::vector<Lane *> all;
-    std::vector<Lane *> idle;
+    std::vector<Lane *> idle[2];         /* per direction: [0] loads, [1] saves */
+    int nlanes[2] = {0, 0};
     std::vector<AsyncOp *> async_idle;   /* finished async ops, reusable */
-    int max_lanes;
+    int max_lanes;                       /* per direction */
     int host_ptr_ok = 0;   /* registered host memory usable at its host address */
 
     /* async worker: enqueues the jobs of every async op of this device in
@@ -641,7 +647,7 @@ public:
         }
         num_devices_ = n;
         timeout_ms_ = env_int("CROSSCACHE_TIMEOUT_MS", 120000);
-        lanes_per_dev_ = std::max(1, env_int("CROSSCACHE_LANES", 2));
+        lanes_per_dev_ = std::max(1, env_int("CROSSCACHE_LANES", 2));   /* per direction */
         const char *m = getenv("CROSSCACHE_XFER_MODE");
         direct_ = m && !strcmp(m, "direct");
         async_ctas_ = (uint32_t)std::max(1, env_int("CROSSCACHE_ASYNC_CTAS", 32));
@@ -822,12 +828,15 @@ public:
             ctx = it->second.get();
         }
         std::lock_guard<std::mutex> lk(ctx->mu);
-        for (Lane *l : ctx->idle) {
-            ctx->all.erase(std::remove(ctx->all.begin(), ctx->all.end(), l), ctx->all.end());
-            l->release();
-            delete l;
+        for (int d = 0; d < 2; d++) {
+            for (Lane *l : ctx->idle[d]) {
+                ctx->all.erase(std::remove(ctx->all.begin(), ctx->all.end(), l), ctx->all.end());
+                ctx->nlanes[d]--;
+                l->release();
+                delete l;
+            }
+            ctx->idle[d].clear();
         }
-        ctx->idle.clear();
         for (AsyncOp *op : ctx->async_idle) {
             op->release();
             delete op;
@@ -851,16 +860,22 @@ private:
         return slot.get();
     }
 
-    Lane *acquire(DeviceCtx *ctx)
+    /* A lane of direction `dir` (1: saves, 0: loads), created on first need
+     * up to max_lanes per direction.  Saves and loads never share a lane,
+     * like the reference's separate Store and Load thread pools
+     * (src/main.c:394-410): a burst of saves cannot hold every lane while a
+     * load waits for one, or the other way round. */
+    Lane *acquire(DeviceCtx *ctx, int dir)
     {
         std::unique_lock<std::mutex> lk(ctx->mu);
         for (;;) {
-            if (!ctx->idle.empty()) {
-                Lane *l = ctx->idle.back();
-                ctx->idle.pop_back();
+            std::vector<Lane *> &idle = ctx->idle[dir];
+            if (!idle.empty()) {
+                Lane *l = idle.back();
+                idle.pop_back();
                 return l;
             }
-            if ((int)ctx->all.size() < ctx->max_lanes) {
+            if (ctx->nlanes[dir] < ctx->max_lanes) {
                 Lane *l = new (std::nothrow) Lane();
                 if (!l || !l->init(ctx->dev)) {
                     if (l) {
@@ -869,11 +884,13 @@ private:
                     }
                     return nullptr;
                 }
+                l->dir = dir;
                 ctx->all.push_back(l);
+                ctx->nlanes[dir]++;
                 return l;
             }
             if (ctx->cv.wait_for(lk, std::chrono::milliseconds(timeout_ms_)) == std::cv_status::timeout &&
-                ctx->idle.empty())
+                ctx->idle[dir].empty())
                 return nullptr;
         }
     }
@@ -883,8 +900,8 @@ private:
         std::lock_guard<std::mutex> lk(ctx->mu);
         if (l->poisoned)
             return;   /* device work may still be in flight: never reuse */
-        ctx->idle.push_back(l);
-        ctx->cv.notify_one();
+        ctx->idle[l->dir].push_back(l);
+        ctx->cv.notify_all();
     }
 
     void drain(DeviceCtx *ctx)
@@ -899,7 +916,9 @@ private:
             }
         }
         ctx->all.clear();
-        ctx->idle.clear();
+        ctx->idle[0].clear();
+        ctx->idle[1].clear();
+        ctx->nlanes[0] = ctx->nlanes[1] = 0;
         /* async ops still held by callers stay theirs; the idle ones go */
         for (AsyncOp *op : ctx->async_idle) {
             op->release();
@@ -957,15 +976,21 @@ private:
     std::map<void *, PinnedRegion> pinned_;
 };
 
-/* read back the error word after everything queued on `last`, then wait */
+/* read back the error word after everything queued on `last`, then wait.
+ * The read-back goes through the lane's copy stream: every copy command a
+ * lane issues (metadata up, records, error word down) is on cs and the
+ * kernel stream carries only kernels.  A tiny copy on the kernel stream can
+ * be given a copy engine that the other lane is keeping busy with 32 MiB
+ * record copies, and then waits behind them -- measured on B200 with one
+ * lane saving while another loads: H2D fell to half the rate the link gives
+ * plain copies in both directions at once. */
 int CudaAdaptor::finish(Lane *l, cudaStream_t last, int ret)
 {
-    if (ret == 0) {
-        if (last != l->ks && !CU_OK(cudaStreamWaitEvent(l->ks, l->fin, 0)))
-            ret = -EIO;
-    }
-    if (ret == 0 && (!CU_OK(cudaMemcpyAsync(l->h_err, l->d_err, 4, cudaMemcpyDeviceToHost, l->ks)) ||
-                     !CU_OK(cudaEventRecord(l->fin, l->ks))))
+    if (ret == 0 && last != l->cs &&
+        (!CU_OK(cudaEventRecord(l->fin, last)) || !CU_OK(cudaStreamWaitEvent(l->cs, l->fin, 0))))
+        ret = -EIO;
+    if (ret == 0 && (!CU_OK(cudaMemcpyAsync(l->h_err, l->d_err, 4, cudaMemcpyDeviceToHost, l->cs)) ||
+                     !CU_OK(cudaEventRecord(l->fin, l->cs))))
         ret = -EIO;
     if (ret == 0 || ret == -EIO) {
         int w = wait_event(l->fin, deadline());
@@ -1011,8 +1036,10 @@ int CudaAdaptor::run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch 
             l->h_meta[(uint64_t)R * bpr + r] = (uint64_t)(uintptr_t)p;
         }
     }
-    if (!CU_OK(cudaMemsetAsync(l->d_err, 0, 4, l->ks)) ||
-        !CU_OK(cudaMemcpyAsync(l->d_meta, l->h_meta, words * 8, cudaMemcpyHostToDevice, l->ks)))
+    /* metadata up through the copy stream (see finish); kernels wait for it */
+    if (!CU_OK(cudaMemsetAsync(l->d_err, 0, 4, l->cs)) ||
+        !CU_OK(cudaMemcpyAsync(l->d_meta, l->h_meta, words * 8, cudaMemcpyHostToDevice, l->cs)) ||
+        !CU_OK(cudaEventRecord(l->mready, l->cs)) || !CU_OK(cudaStreamWaitEvent(l->ks, l->mready, 0)))
         return -EIO;
 
     kv_copy_desc d{};
@@ -1089,13 +1116,8 @@ int CudaAdaptor::run_batch(Lane *l, DeviceCtx *ctx, const struct transfer_batch 
                 return -EIO;
         }
     }
-    if (save) {
-        /* the last copies were queued on cs: make ks wait for them */
-        if (!CU_OK(cudaEventRecord(l->fin, l->cs)))
-            return -EIO;
-        return finish(l, l->cs, 0);
-    }
-    return finish(l, l->ks, 0);
+    /* save: the last copies are on cs; load: the last kernel is on ks */
+    return finish(l, save ? l->cs : l->ks, 0);
 }
 
 /* paged geometry a kernel can address: blocks that do not overlap, heads
@@ -1118,7 +1140,7 @@ int CudaAdaptor::TransferKVCacheBatch(struct transfer_batch *b)
     if (!CU_OK(cudaSetDevice(b->devid)))
         return -EIO;
     DeviceCtx *ctx = device(b->devid);
-    Lane *l = acquire(ctx);
+    Lane *l = acquire(ctx, b->direction ? 1 : 0);
     if (!l)
         return -EBUSY;
     int ret = run_batch(l, ctx, b);
@@ -1416,7 +1438,7 @@ int CudaAdaptor::TransferKVCache(struct transfer_params *p)
     void *host = p->caches_h ? p->caches_h : p->caches;
 
     DeviceCtx *ctx = device(p->devid);
-    Lane *l = acquire(ctx);
+    Lane *l = acquire(ctx, p->direction ? 1 : 0);
     if (!l)
         return -EBUSY;
     int ret = 0;
