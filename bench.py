@@ -56,6 +56,20 @@ REQS, TOKENS, CHUNK, VOCAB = 64, 2048, 256, 128256
 GB = 1e9
 
 
+def duplex_threads(request_bytes: int) -> tuple[int, int]:
+    """(save threads, load threads) of the duplex step, from a sweep on B200
+    (GB/s of the step, savers x loaders):
+                       1x1   1x2   2x2   2x3   4x4
+      256 MiB requests 73.8  94.2  82.1  82.1  81.8   (Llama-3-8B, 8 heads)
+      2.5 GiB requests 84.8  71.6  92.7  94.9  94.9   (Llama-3-70B, 8 heads)
+    With both directions busy, the side with more bytes queued takes the
+    link, and short load calls lose ground at every call boundary: one more
+    load thread than save threads keeps H2D fed; long requests need two save
+    threads to hold D2H's share."""
+    saves = 1 if request_bytes < (1 << 30) else 2
+    return saves, saves + 1
+
+
 PRESETS = {
     # the headline config: Llama-3-8B GQA, 64 requests x 2048 tokens
     "llama3-8b": dict(layers=32, requests=64, tokens=2048, blocks=16384, model="llama-3-8b",
@@ -1298,7 +1312,7 @@ class Offload:
         fit = int(pool_budget // self.rec_bytes) - 1
         return int(self.rk.min(min(limit, max(0, fit) // (batches * self.kpr))))
 
-    def e2e(self, steps: int, warmup: int, pool_budget: float) -> dict:
+    def e2e(self, steps: int, warmup: int, pool_budget: float, threads: tuple | None = None) -> dict:
         """Two end-to-end steps through cache_store / cache_lookup_batch /
         cache_load (host clock, every H2D / D2H inside).
 
@@ -1468,6 +1482,7 @@ class Offload:
         rest = self.reload_perm if self.disjoint else self.reload_perm[
             ~np.isin(self.reload_perm, self.bt_save[:nblk])]
         dl_table = np.ascontiguousarray(rest[:nblk])
+        n_save, n_load = threads or duplex_threads(kpr * self.rec_bytes)
         saves = [np.ascontiguousarray(self.bt_save[r * prb:(r + 1) * prb]) for r in range(R)]
         dloads = [np.ascontiguousarray(dl_table[r * prb:(r + 1) * prb]) for r in range(R)]
         b_save = torch.from_numpy(self.bt_save[:nblk].astype(np.int64)).to(dev)
@@ -1486,17 +1501,17 @@ class Offload:
             t2 = time.perf_counter()
             errs: list = []
 
-            def saver():
-                for r in range(R):
+            def saver(j):
+                for r in range(j, R, n_save):
                     ret = lib.cache_store(C.byref(w.ctx), kb[r * kpr * 32:(r + 1) * kpr * 32], 32,
                                           saves[r].ctypes.data, prb)
                     if ret:
                         errs.append(("store", r, ret))
 
-            th_s = threading.Thread(target=saver, daemon=True)
-            th_s.start()
-            try:
-                for r in range(R):
+            load_end = [0.0] * n_load
+
+            def loader(j):
+                for r in range(j, R, n_load):
                     h = int(hit[r])
                     ts = time.perf_counter()
                     ret = lib.cache_load(C.byref(w.ctx), kprev[r * kpr * 32:(r * kpr + h) * 32], 32,
@@ -1505,9 +1520,15 @@ class Offload:
                         errs.append(("load", r, ret))
                     if lat is not None:
                         lat.append(time.perf_counter() - ts)
-                t_l = time.perf_counter()
-            finally:
-                th_s.join()
+                load_end[j] = time.perf_counter()
+
+            ths = [threading.Thread(target=saver, args=(j,), daemon=True) for j in range(n_save)] + [
+                threading.Thread(target=loader, args=(j,), daemon=True) for j in range(n_load)]
+            for t in ths:
+                t.start()
+            for t in ths:
+                t.join()
+            t_l = max(load_end)
             t3 = time.perf_counter()
             assert not errs, errs
             state.update(k=k, prev=kb)
@@ -1552,11 +1573,13 @@ class Offload:
             "hit_blocks_per_request": parts[-1]["hits"] * bpc // R, "gpu_launches": int(launches),
             "h2d_bytes_per_step": int(payload + up_b + 2 * nblk * 8), "d2h_bytes_per_step": int(payload + down_b),
             "evictions": st["evictions"], "verified_bytes": ok,
+            "save_threads": n_save, "load_threads": n_load,
             "note": ("per step: hash batch k (fresh prompts: the NONE_HASH seed is the step number); barrier "
                      "(step skew); cache_lookup_batch + one all-reduce(min) over batch k-1's keys; then "
-                     "cache_store of batch k (one call per request, a second thread) while cache_load brings "
-                     "batch k-1 back (one call per request): D2H and H2D at once, no collective between them. "
-                     "Pool of three batches: LRU evicts the batch loaded two steps before.")}
+                     f"cache_store of batch k ({n_save} thread(s), one call per request) while cache_load "
+                     f"brings batch k-1 back ({n_load} threads, one call per request): D2H and H2D at once, "
+                     "no collective between them; the load latency is with the other loads and saves in "
+                     "flight. Pool of three batches: LRU evicts the batch loaded two steps before.")}
         return out
 
     # -- the no-allocation entry point on the same shapes ---------------------
@@ -1626,6 +1649,8 @@ def main() -> None:
     ap.add_argument("--link-seconds", type=float, default=2.0, help="seconds per host-link probe")
     ap.add_argument("--skip-e2e", action="store_true", help="kernels only (for ncu captures)")
     ap.add_argument("--no-subs", action="store_true", help="skip the tp70b / prefix-reuse / mla-evict objects")
+    ap.add_argument("--duplex-threads", default=None,
+                    help="SAVE,LOAD thread counts of the duplex step (default: duplex_threads())")
     ap.add_argument("--sub-steps", type=int, default=3, help="timed steps of each sub-workload")
     ap.add_argument("--sub-warmup", type=int, default=2, help="warm-up steps of each sub-workload (the first checked)")
     ap.add_argument("--disk-dir", default=None,
@@ -1692,7 +1717,8 @@ def main() -> None:
     disk = server = layerwise = paged_layouts = noalloc = prefix = mla = tp70 = None
     if not args.skip_e2e:
         link = link_probe(rk, args.link_seconds)
-        e2e = head.e2e(args.steps, args.warmup, budget)
+        threads = tuple(int(x) for x in args.duplex_threads.split(",")) if args.duplex_threads else None
+        e2e = head.e2e(args.steps, args.warmup, budget, threads)
     s = dict(dev=dev, nrec=head.nrec, rec_bytes=head.rec_bytes, bpc=head.bpc, n_blocks=head.n_blocks,
              unit=head.unit, disjoint=head.disjoint, local=local, world=world, rank=rank, n_req=head.n_req,
              n_tok=head.n_tok, per_req_blocks=head.prb, payload=head.payload)
@@ -1773,12 +1799,18 @@ def main() -> None:
     if head_e2e:
         value, ms = head_e2e["value"], head_e2e["ms_per_step"]
         launches, p50 = head_e2e["gpu_launches"], head_e2e["p50_load_latency_ms"]
+        if seq and dup:
+            head_e2e = dict(head_e2e, p50_isolated_ms=seq["p50_load_latency_ms"])
         e2e_line = {"value": value, "unit": "GB/s", "mode": "duplex" if dup else "sequential",
                     "h2d_bytes_per_step": head_e2e["h2d_bytes_per_step"],
                     "d2h_bytes_per_step": head_e2e["d2h_bytes_per_step"],
                     "bytes_note": "per rank per step: KV payload + token ids + block tables up, payload + block "
                                   "hashes down",
                     "ms_per_step": ms, "p50_load_latency_ms": p50,
+                    "p50_load_latency_isolated_ms": head_e2e.get("p50_isolated_ms"),
+                    "latency_note": "p50_load_latency_ms: the value step's loads (with other loads and a save "
+                                    "in flight); isolated: one request's load with the link to itself "
+                                    "(sequential step)",
                     "requests_per_step": head_e2e["requests_per_step"], "verified_bytes": head_e2e["verified_bytes"]}
     else:
         value, ms, launches, p50 = device["value"], device["ms_per_step"], device["launches"], None
