@@ -621,7 +621,14 @@ int launch_bulk(const BulkParams &bp, bool to_record, cudaStream_t stream)
  *     the refill of that stage.
  * ---------------------------------------------------------------------- */
 constexpr int kHndThreads = 512;
-constexpr int kHndStages = 4;
+/* 5 load stages + 2 transpose buffers = 224 KiB: the transpose between a
+ * tile's load and its store lengthens a tile's life, and one more stage in
+ * flight bought 0.5 % (gather) and 1.3 % (scatter) of the copy peak on B200
+ * (headline shapes, same box, two runs each) over 4 */
+#ifndef KVCOPY_HND_STAGES
+#define KVCOPY_HND_STAGES 5
+#endif
+constexpr int kHndStages = KVCOPY_HND_STAGES;
 static_assert((uint64_t)(kHndStages + 2) * kBulkTileBytes <= 227u * 1024u - 256u,
               "head-major bulk stages and transpose buffers must fit in shared memory");
 
