@@ -1798,19 +1798,21 @@ def main() -> None:
             t_dup["frac_of_link_both_directions"] = round(t_dup["value"] / link["both"]["aggregate"], 4)
     if head_e2e:
         value, ms = head_e2e["value"], head_e2e["ms_per_step"]
-        launches, p50 = head_e2e["gpu_launches"], head_e2e["p50_load_latency_ms"]
-        if seq and dup:
-            head_e2e = dict(head_e2e, p50_isolated_ms=seq["p50_load_latency_ms"])
+        launches = head_e2e["gpu_launches"]
+        # the metric's latency: one request's load with the link to itself
+        # (sequential step); the duplex step's, with other transfers in
+        # flight, is reported beside it
+        p50 = (seq or head_e2e)["p50_load_latency_ms"]
         e2e_line = {"value": value, "unit": "GB/s", "mode": "duplex" if dup else "sequential",
                     "h2d_bytes_per_step": head_e2e["h2d_bytes_per_step"],
                     "d2h_bytes_per_step": head_e2e["d2h_bytes_per_step"],
                     "bytes_note": "per rank per step: KV payload + token ids + block tables up, payload + block "
                                   "hashes down",
                     "ms_per_step": ms, "p50_load_latency_ms": p50,
-                    "p50_load_latency_isolated_ms": head_e2e.get("p50_isolated_ms"),
-                    "latency_note": "p50_load_latency_ms: the value step's loads (with other loads and a save "
-                                    "in flight); isolated: one request's load with the link to itself "
-                                    "(sequential step)",
+                    "p50_load_latency_under_duplex_ms": dup["p50_load_latency_ms"] if dup else None,
+                    "latency_note": "p50_load_latency_ms: one request's load (cache_load of its records) with "
+                                    "the host link to itself (sequential step); under_duplex: the value "
+                                    "step's loads, with another load and a save in flight",
                     "requests_per_step": head_e2e["requests_per_step"], "verified_bytes": head_e2e["verified_bytes"]}
     else:
         value, ms, launches, p50 = device["value"], device["ms_per_step"], device["launches"], None
