@@ -74,6 +74,39 @@ int env_int(const char *name, int dflt)
     return s ? atoi(s) : dflt;
 }
 
+/* Fault a fresh anonymous mapping in from several threads (one write per
+ * 4 KiB page; with transparent huge pages the first write of each 2 MiB
+ * faults the whole page) before cudaHostRegister pins it, which otherwise
+ * faults and zeroes every page on the calling thread.  The reference
+ * prefaults its pool too (npu.cpp:49-90), on one thread.  Threads:
+ * CROSSCACHE_PREFAULT_THREADS, default min(16, host threads). */
+void prefault(void *addr, uint64_t size)
+{
+    const uint64_t page = 4096, chunk = 2ull << 20;
+    unsigned n = std::thread::hardware_concurrency();
+    n = n ? std::min(16u, n) : 1u;
+    if (const char *e = getenv("CROSSCACHE_PREFAULT_THREADS"))
+        n = (unsigned)std::max(1, atoi(e));
+    const uint64_t chunks = (size + chunk - 1) / chunk;
+    if (chunks < 64 || n == 1)
+        n = 1;
+    auto touch = [addr, size, page](uint64_t b, uint64_t e) {
+        volatile uint8_t *p = static_cast<volatile uint8_t *>(addr);
+        for (uint64_t o = b; o < e && o < size; o += page)
+            p[o] = 0;
+    };
+    if (n == 1) {
+        touch(0, size);
+        return;
+    }
+    std::vector<std::thread> th;
+    const uint64_t per = (chunks + n - 1) / n * chunk;
+    for (unsigned i = 0; i < n; i++)
+        th.emplace_back(touch, (uint64_t)i * per, (uint64_t)(i + 1) * per);
+    for (auto &t : th)
+        t.join();
+}
+
 /* poll an event until it completes or the deadline passes */
 int wait_event(cudaEvent_t ev, std::chrono::steady_clock::time_point deadline)
 {
@@ -690,6 +723,7 @@ public:
             return nullptr;
         }
         madvise(addr, size, MADV_HUGEPAGE);
+        prefault(addr, size);
         if (!CU_OK(cudaHostRegister(addr, size, cudaHostRegisterMapped | cudaHostRegisterPortable))) {
             munmap(addr, size);
             return nullptr;
