@@ -1722,7 +1722,10 @@ def main() -> None:
     s = dict(dev=dev, nrec=head.nrec, rec_bytes=head.rec_bytes, bpc=head.bpc, n_blocks=head.n_blocks,
              unit=head.unit, disjoint=head.disjoint, local=local, world=world, rank=rank, n_req=head.n_req,
              n_tok=head.n_tok, per_req_blocks=head.prb, payload=head.payload)
-    if world == 1 and args.emulate_tp == 1:
+    # on the headline shapes only: both hold every record in HBM beside the
+    # paged cache (two copies for the paged-layout probe), which the 80-layer
+    # preset's records (80 GiB at N = 1) do not leave room for
+    if world == 1 and args.emulate_tp == 1 and args.workload == "llama3-8b":
         b_save = torch.from_numpy(head.bt_save.astype(np.int64)).to(dev)
         b_load = torch.from_numpy(head.bt_load.astype(np.int64)).to(dev)
         paged_layouts = _paged_layout_probe(args, head.layers, b_save, b_load, s)
