@@ -127,7 +127,8 @@ class SchedulerAdapter:
 
 class WorkerAdapter:
     """python/adaptor.py:117-291 with the same store/load/get_finished
-    bookkeeping; the transfers run in this process on a worker thread."""
+    bookkeeping; the transfers run in this process, stores and loads each on
+    a worker thread of their own."""
 
     def __init__(self, model_name: str, world_size: int, kv_rank: int, vllm_block_size: int,
                  pool_size: int = 4 << 30, device: int | None = None, tp_group=None):
@@ -140,7 +141,12 @@ class WorkerAdapter:
         self.device = torch.cuda.current_device() if device is None else device
         self.tp_group = tp_group
         self.worker: cc.Worker | None = None
-        self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="CrossCacheXfer")
+        # one thread per direction, like the reference server's separate Store
+        # and Load pools (src/main.c:394-410): a step's loads do not queue
+        # behind the previous step's stores, and the host link carries both
+        # directions at once; each direction keeps its submission order
+        self._store_pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="CrossCacheStore")
+        self._load_pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="CrossCacheLoad")
         self.store_futures: dict[str, tuple[Future, list[str]]] = {}
         self.load_futures: dict[str, tuple[Future, list[str]]] = {}
         self.finished_stores: set[str] = set()
@@ -170,13 +176,14 @@ class WorkerAdapter:
 
     def unregister(self) -> None:
         self.end_layerwise_step()
-        self._pool.shutdown(wait=True)
+        self._store_pool.shutdown(wait=True)
+        self._load_pool.shutdown(wait=True)
         if self.worker is not None:
             self.worker.unregister()
             self.worker = None
             release_cache()
 
-    def _submit(self, fn, *args) -> Future:
+    def _submit(self, pool: ThreadPoolExecutor, fn, *args) -> Future:
         # the transfer must see every KV write queued on the compute stream
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(self.device))
@@ -184,7 +191,7 @@ class WorkerAdapter:
         def run():
             ev.synchronize()
             return fn(*args)
-        return self._pool.submit(run)
+        return pool.submit(run)
 
     def _per_request(self, ops: list[LoadStoreOp]) -> tuple[list[list[bytes]], list[list[int]]]:
         kreq = [list(self._block_hashes_to_keys(op.block_hashes)) for op in ops]
@@ -198,7 +205,7 @@ class WorkerAdapter:
         def run():
             ret, st = self.worker.store_batch(kreq, breq)
             return ret, {rid: int(s) for rid, s in zip(request_ids, st)}
-        self.store_futures[request_ids[0]] = (self._submit(run), request_ids[1:])
+        self.store_futures[request_ids[0]] = (self._submit(self._store_pool, run), request_ids[1:])
 
     def load_requests(self, request_ids: list[str], ops: list[LoadStoreOp]) -> None:
         kreq, breq = self._per_request(ops)
@@ -211,7 +218,7 @@ class WorkerAdapter:
                     for b in failed:
                         self._failed_load_blocks.update(int(x) for x in b)
             return ret, {rid: int(s) for rid, s in zip(request_ids, st)}
-        self.load_futures[request_ids[0]] = (self._submit(run), request_ids[1:])
+        self.load_futures[request_ids[0]] = (self._submit(self._load_pool, run), request_ids[1:])
 
     def take_failed_load_blocks(self) -> set[int]:
         """block ids whose load failed since the last call (for vLLM's
@@ -277,12 +284,12 @@ class WorkerAdapter:
     def end_layerwise_step(self) -> None:
         if self._layer_store is not None:
             ids = self._layer_store_ids
-            self.store_futures[ids[0]] = (self._pool.submit(self._layer_store.finish), ids[1:])
+            self.store_futures[ids[0]] = (self._store_pool.submit(self._layer_store.finish), ids[1:])
             self._layer_store = None
         if self._layer_load is not None:
             # records stay pinned until the copies end; nothing to report
             self._layer_load_futures = [f for f in self._layer_load_futures if not f.done()]
-            self._layer_load_futures.append(self._pool.submit(self._layer_load.finish))
+            self._layer_load_futures.append(self._load_pool.submit(self._layer_load.finish))
             self._layer_load = None
 
     def lookup_agreed(self, keys_per_request: list[list[bytes]]) -> np.ndarray:
