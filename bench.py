@@ -284,6 +284,37 @@ def cpu_sample_run(impl: str, seconds: float | None, iters: int | None, threads:
             "times_s": [round(t, 4) for t in times], "shards": shards, "unit_bytes": unit}
 
 
+def cpu_geometry_sample(label: str, layers: int, unit: int, block_size: int, kv: int, records: int,
+                        threads: int, seconds: float) -> dict:
+    """One configuration's CPU baseline: save then load `records` records of
+    its geometry (layers, unit bytes, block size, K+V or K only) through the
+    oracle's restatement of CrossCache's CPU path (mem.cpp:114-173 under
+    cache.c:513-593's chunking), paged cache in host memory, passes repeated
+    for about `seconds`.  Returns GB/s of save+load payload (median pass)."""
+    from oracle import kvcopy as ok
+
+    nb = records * (CHUNK // block_size)
+    layer_bytes = nb * block_size * unit
+    k = [np.full(layer_bytes, l, np.uint8) for l in range(layers)]
+    v = [np.full(layer_bytes, 100 + l, np.uint8) for l in range(layers)] if kv == 2 else None
+    rec_bytes = kv * layers * CHUNK * unit
+    recs = [np.zeros(rec_bytes, np.uint8) for _ in range(records)]
+    rng = np.random.default_rng(2)
+    bids, bids2 = rng.permutation(nb).astype(np.uint64), rng.permutation(nb).astype(np.uint64)
+
+    def one_step():
+        ok.cache_op(recs, k, v, bids, CHUNK, block_size, unit, 1, True, threads)
+        ok.cache_op(recs, k, v, bids2, CHUNK, block_size, unit, 1, False, threads)
+    times = _time_steps(one_step, seconds, None)
+    payload = 2 * records * rec_bytes
+    return {"value": round(statistics.median(payload / t / GB for t in times), 3), "unit": "GB/s",
+            "cores": threads, "kind": "port",
+            "sample": f"{label}: {records} records of {rec_bytes / 2**20:.2f} MiB ({layers} layers, "
+                      f"{'K+V' if kv == 2 else 'K only'}, {unit}-byte units, block {block_size}), save then load "
+                      f"into a second block table, paged cache in host memory; oracle/kvcopy_oracle.c "
+                      f"restatement of mem.cpp:114-173 + cache.c:513-593; median of {len(times)} passes"}
+
+
 def _cpu_model() -> str:
     try:
         with open("/proc/cpuinfo") as f:
@@ -1776,6 +1807,17 @@ def main() -> None:
         four = cpu_sample_run("port", args.cpu_seconds / 2, None, 4)
         cpu["value_4_threads"] = round(four["value"], 3)
         cpu["cpu_model"] = _cpu_model()
+        # each other configuration's CPU path at its own geometry, ~2 GiB per direction
+        nth, sub_s = os.cpu_count() or 1, args.cpu_seconds / 4
+        if prefix:
+            prefix["cpu_baseline"] = cpu_geometry_sample("prefix reuse (Llama-3-8B geometry)", L,
+                                                         KV_HEADS * HEAD_DIM * ELT, BS, 2, 64, nth, sub_s)
+        if tp70:
+            tp70["cpu_baseline"] = cpu_geometry_sample("Llama-3-70B, TP = 1", PRESETS["tp70b"]["layers"],
+                                                       KV_HEADS * HEAD_DIM * ELT, BS, 2, 24, nth, sub_s)
+        if mla:
+            mla["cpu_baseline"] = cpu_geometry_sample("DeepSeek-V2-Lite MLA latent", 27, 576 * 2, 64, 1, 256,
+                                                      nth, sub_s)
 
     if rank != 0:
         if world > 1:

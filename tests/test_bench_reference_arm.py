@@ -46,3 +46,15 @@ def test_duplex_thread_rule():
     import bench
     assert bench.duplex_threads(256 << 20) == (1, 2)
     assert bench.duplex_threads(5 << 29) == (2, 3)
+
+
+@pytest.mark.parametrize("kv,bs,unit", [(2, 16, 2048), (1, 64, 1152)], ids=["kv", "k_only"])
+def test_cpu_geometry_sample_moves_the_configuration_payload(kv, bs, unit):
+    """the per-configuration CPU baseline: one pass over a small sample of the
+    geometry (K+V as the 70B config, K only as the MLA config)"""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    res = bench.cpu_geometry_sample("test", 3, unit, bs, kv, 2, 2, 0.0)
+    assert res["value"] > 0 and res["unit"] == "GB/s" and res["kind"] == "port" and res["cores"] == 2
+    rec_mib = kv * 3 * bench.CHUNK * unit / 2**20
+    assert f"2 records of {rec_mib:.2f} MiB (3 layers, {'K+V' if kv == 2 else 'K only'}" in res["sample"]
