@@ -58,3 +58,10 @@ def test_cpu_geometry_sample_moves_the_configuration_payload(kv, bs, unit):
     assert res["value"] > 0 and res["unit"] == "GB/s" and res["kind"] == "port" and res["cores"] == 2
     rec_mib = kv * 3 * bench.CHUNK * unit / 2**20
     assert f"2 records of {rec_mib:.2f} MiB (3 layers, {'K+V' if kv == 2 else 'K only'}" in res["sample"]
+
+
+def test_host_copy_probe_reports_a_rate():
+    """the host memory copy rate the bench takes around its e2e steps"""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert bench.host_copy_gbs(2, 0.05) > 0
